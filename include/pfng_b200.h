@@ -1,0 +1,145 @@
+/*
+ * pfng_b200.h -- C ABI of the B200 (sm_100a) block-quantized matmul library.
+ *
+ * The library computes perf-framework-ng's hot path on the GPU:
+ *     C[m][n] = A_act[m][k] . W[n][k]^T
+ * for the weight/activation pairs q4_0 x q8_0, q4_K x q8_K and
+ * iq2_xxs x q8_K, plus the fp32 -> q8_0 / q8_K activation quantizers that
+ * feed it and the fp32 -> q4_0 / q4_K weight quantizers that produce W.
+ *
+ * All buffers are DEVICE pointers in the unmodified ggml block layouts of the
+ * reference (include/ggml.h:125-159):
+ *     block_q4_0    18 B per 32 values    block_q8_0  34 B per 32 values
+ *     block_q4_K   144 B per 256 values   block_q8_K 292 B per 256 values
+ *     block_iq2_xxs 66 B per 256 values
+ * W is [n][k / block_k] blocks, A is [m][k / block_k] blocks, C is fp32
+ * row-major with row stride ldc (floats).  Every call is asynchronous on
+ * `stream` (a cudaStream_t, 0 for the legacy default stream).
+ *
+ * Results: quantizer bytes and integer per-block partial dot products are
+ * bit-identical to the reference's scalar path; fp32 outputs agree with it to
+ * |C - C_ref| <= 1e-5 * sum_k |w_k * a_k| per element (summation order
+ * differs).
+ *
+ * Return value: PFNG_B200_OK (0) or a negative status.  Argument checks run
+ * on the host before any CUDA call, so a rejected call touches no device
+ * state.  m == 0 or n == 0 is a valid no-op.
+ */
+#ifndef PFNG_B200_H
+#define PFNG_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define PFNG_B200_OK 0
+#define PFNG_B200_ERR_INVALID_ARGUMENT (-1) /* null pointer with non-zero size, negative size */
+#define PFNG_B200_ERR_SHAPE (-2)            /* k not a multiple of the block size, ldc < n / ldx < k */
+#define PFNG_B200_ERR_ALIGNMENT (-3)        /* pointer not aligned to its element or block type */
+#define PFNG_B200_ERR_WORKSPACE (-4)        /* workspace missing or smaller than *_workspace_size() */
+#define PFNG_B200_ERR_DEVICE (-5)           /* current device is not compute capability 10.0 */
+#define PFNG_B200_ERR_KERNEL_TIMEOUT (-6)   /* a bounded wait inside a kernel gave up */
+#define PFNG_B200_ERR_UNSUPPORTED (-7)      /* forced kernel path cannot run this shape */
+#define PFNG_B200_ERR_CUDA_BASE (-1000)     /* -1000 - cudaError_t of a failed CUDA call */
+
+/* ---- kernel path selection (the `path` argument) ------------------------ */
+#define PFNG_B200_PATH_AUTO 0 /* choose by shape: GEMV for small m, tensor-core GEMM otherwise */
+#define PFNG_B200_PATH_GEMV 1 /* small-m HBM-streaming kernel (dp4a); m <= 8 */
+#define PFNG_B200_PATH_MMA 2  /* int8 tensor-core GEMM */
+#define PFNG_B200_PATH_SIMPLE 3 /* one-thread-per-output kernel for any k; correctness fallback */
+
+/* Weight types, in the order of the reference's QuantizationType
+ * (bench/framework/kernel_registry.h:37-42). */
+#define PFNG_B200_Q4_0 0
+#define PFNG_B200_Q4_K 1
+#define PFNG_B200_IQ2_XXS 2
+
+/* Library version, and a readable name for a status code. */
+int pfng_b200_version(void);
+const char *pfng_b200_status_string(int status);
+
+/* Reads and clears the kernel error flag after synchronizing `stream`.
+ * Returns PFNG_B200_ERR_KERNEL_TIMEOUT if any kernel of this library gave up
+ * a bounded wait since the last call, else PFNG_B200_OK (or a CUDA error). */
+int pfng_b200_check_kernel_error(void *stream);
+
+/* ---- activation quantizers ---------------------------------------------
+ * x: fp32 [m][ldx] (ldx >= k); y: blocks [m][k / 32] or [m][k / 256].
+ * Replace llama_reference::quantize_row_q8_0 (llama_reference.cpp:38-52) and
+ * quantize_row_q8_K (llama_reference.cpp:54-70), applied row by row. */
+int pfng_b200_quantize_q8_0(const float *x, int64_t ldx, void *y, int64_t m, int64_t k, void *stream);
+int pfng_b200_quantize_q8_K(const float *x, int64_t ldx, void *y, int64_t m, int64_t k, void *stream);
+
+/* ---- weight quantizers (producers of W) ---------------------------------
+ * Replace llama_reference::quantize_row_q4_0 (llama_reference.cpp:13-36) and
+ * quantize_row_q4_K (llama_reference.cpp:72-111), which the reference runs on
+ * the host in create_q4_0_input / create_q4_K_input
+ * (bench/framework/benchmark.cpp:34-66). */
+int pfng_b200_quantize_q4_0(const float *x, int64_t ldx, void *y, int64_t n, int64_t k, void *stream);
+int pfng_b200_quantize_q4_K(const float *x, int64_t ldx, void *y, int64_t n, int64_t k, void *stream);
+
+/* ---- matmul on quantized activations ------------------------------------
+ * C = A . W^T with A already quantized (q8_0 for q4_0, q8_K otherwise).
+ * Replace the per-element dot loops of compute_q4_0 / compute_q4_K /
+ * compute_iq2_xxs (llama_reference.cpp:172-175, :186-189, :200-203) and the
+ * KernelCallbacks::run of a reference adapter
+ * (bench/framework/kernel_registry.h:97).
+ * workspace: device scratch of at least pfng_b200_mm_workspace_size() bytes,
+ * 256-byte aligned (may be NULL when that size is 0). */
+size_t pfng_b200_mm_workspace_size(int wtype, int64_t m, int64_t n, int64_t k, int path);
+int pfng_b200_mm_q4_0_q8_0(const void *w, const void *a, float *c, int64_t m, int64_t n, int64_t k, int64_t ldc,
+                           void *workspace, size_t workspace_bytes, int path, void *stream);
+int pfng_b200_mm_q4_K_q8_K(const void *w, const void *a, float *c, int64_t m, int64_t n, int64_t k, int64_t ldc,
+                           void *workspace, size_t workspace_bytes, int path, void *stream);
+int pfng_b200_mm_iq2_xxs_q8_K(const void *w, const void *a, float *c, int64_t m, int64_t n, int64_t k,
+                              int64_t ldc, void *workspace, size_t workspace_bytes, int path, void *stream);
+
+/* ---- matmul on fp32 activations (quantize + matmul) ----------------------
+ * The reference's full compute(type, input) (llama_reference.cpp:213): the
+ * activations x [m][ldx] are quantized exactly as the quantizers above do,
+ * then multiplied.  For small m the quantization is fused into the matmul
+ * kernel (one launch); otherwise it goes through the workspace. */
+size_t pfng_b200_compute_workspace_size(int wtype, int64_t m, int64_t n, int64_t k, int path);
+int pfng_b200_compute_q4_0(const void *w, const float *x, int64_t ldx, float *c, int64_t m, int64_t n, int64_t k,
+                           int64_t ldc, void *workspace, size_t workspace_bytes, int path, void *stream);
+int pfng_b200_compute_q4_K(const void *w, const float *x, int64_t ldx, float *c, int64_t m, int64_t n, int64_t k,
+                           int64_t ldc, void *workspace, size_t workspace_bytes, int path, void *stream);
+int pfng_b200_compute_iq2_xxs(const void *w, const float *x, int64_t ldx, float *c, int64_t m, int64_t n,
+                              int64_t k, int64_t ldc, void *workspace, size_t workspace_bytes, int path,
+                              void *stream);
+
+/* ---- integer partials (verification) ------------------------------------
+ * out: int32 [m][n][k / 32], the integer dot product of every 32-value
+ * sub-block, produced by the same kernel path as the matmul (`path`) before
+ * any scale is applied:
+ *   q4_0:    sum (nibble - 8) * a          (llama_reference.cpp:138-142)
+ *   q4_K:    sum nibble * a per sub-block  (the q term of :125-130)
+ *   iq2_xxs: sum grid_value * a, unscaled  (:155-157)
+ * Uses the same workspace size as the matmul. */
+int pfng_b200_partials_q4_0_q8_0(const void *w, const void *a, int32_t *out, int64_t m, int64_t n, int64_t k,
+                                 void *workspace, size_t workspace_bytes, int path, void *stream);
+int pfng_b200_partials_q4_K_q8_K(const void *w, const void *a, int32_t *out, int64_t m, int64_t n, int64_t k,
+                                 void *workspace, size_t workspace_bytes, int path, void *stream);
+int pfng_b200_partials_iq2_xxs_q8_K(const void *w, const void *a, int32_t *out, int64_t m, int64_t n, int64_t k,
+                                    void *workspace, size_t workspace_bytes, int path, void *stream);
+
+/* ---- multi-GPU helpers (N-sharded weights) -------------------------------
+ * Rank r of `world` owns weight rows [*begin, *end): the rows are split in
+ * multiples of `granule` (a kernel tile), the last rank taking the ragged
+ * remainder.  Pure host arithmetic. */
+int pfng_b200_shard_rows(int64_t n, int world, int rank, int64_t granule, int64_t *begin, int64_t *end);
+/* Reassemble C [m][ldc] from the all-gathered per-rank slices
+ * `slices` = [world][m][slice_width] (rank r's slice holds its rows'
+ * columns, width end_r - begin_r, zero-padded to slice_width). */
+int pfng_b200_unshard_columns(const float *slices, float *c, int64_t m, int64_t n, int64_t ldc, int world,
+                              int64_t granule, int64_t slice_width, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

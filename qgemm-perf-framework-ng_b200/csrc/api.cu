@@ -1,0 +1,398 @@
+// api.cu -- the extern "C" entry points of libpfng_b200 (include/pfng_b200.h):
+// host-side argument checks, kernel-path selection and workspace carving.
+//
+// Argument checks run before any CUDA call, so a rejected call has no device
+// side effects and can be exercised on a machine without a GPU.
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "pfng_b200.h"
+#include "pfng_common.cuh"
+#include "pfng_internal.h"
+
+namespace pfng {
+
+// Library error word for bounded waits (one per device, in the module).
+__device__ int g_kernel_error_word;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+struct DeviceInfo {
+    int sm_count = 0;
+    size_t smem_optin = 0;
+    int major = 0;
+    int *error_word = nullptr;
+    bool ready = false;
+};
+DeviceInfo g_devices[kMaxDevices];
+std::mutex g_devices_mutex;
+
+int status_of(cudaError_t e) { return e == cudaSuccess ? PFNG_B200_OK : PFNG_B200_ERR_CUDA_BASE - static_cast<int>(e); }
+
+// Queries (once per device) what the launchers need; returns a status.
+int device_info(DeviceInfo **out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return status_of(e);
+    if (dev < 0 || dev >= kMaxDevices) return PFNG_B200_ERR_DEVICE;
+    std::lock_guard<std::mutex> lock(g_devices_mutex);
+    DeviceInfo &info = g_devices[dev];
+    if (!info.ready) {
+        int sms = 0, optin = 0, major = 0;
+        if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return status_of(e);
+        if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess)
+            return status_of(e);
+        if ((e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess)
+            return status_of(e);
+        void *word = nullptr;
+        if ((e = cudaGetSymbolAddress(&word, g_kernel_error_word)) != cudaSuccess) return status_of(e);
+        info.sm_count = sms;
+        info.smem_optin = static_cast<size_t>(optin);
+        info.major = major;
+        info.error_word = static_cast<int *>(word);
+        info.ready = true;
+    }
+    if (info.major != 10) return PFNG_B200_ERR_DEVICE;
+    *out = &info;
+    return PFNG_B200_OK;
+}
+
+DeviceInfo *current_info() {
+    DeviceInfo *info = nullptr;
+    return device_info(&info) == PFNG_B200_OK ? info : nullptr;
+}
+
+bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+int block_k(int wtype) { return wtype == PFNG_B200_Q4_0 ? 32 : 256; }
+size_t a_block_bytes(int wtype) { return wtype == PFNG_B200_Q4_0 ? kQ8_0Bytes : kQ8_KBytes; }
+uintptr_t w_align(int wtype) { return wtype == PFNG_B200_Q4_K ? 4 : 2; }
+uintptr_t a_align(int wtype) { return wtype == PFNG_B200_Q4_0 ? 2 : 4; }
+
+// Common shape/pointer checks for the matmul-family entry points.
+int check_mm(int wtype, const void *w, const void *a_or_x, const void *out, int64_t m, int64_t n, int64_t k,
+             int64_t ldc, int64_t ldx, bool f32_input, bool partials, int path) {
+    if (wtype < 0 || wtype > 2) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    if (m < 0 || n < 0 || k < 0) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    if (path < PFNG_B200_PATH_AUTO || path > PFNG_B200_PATH_SIMPLE) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    if (k % block_k(wtype) != 0) return PFNG_B200_ERR_SHAPE;
+    if (!partials && m > 0 && ldc < n) return PFNG_B200_ERR_SHAPE;
+    if (f32_input && m > 0 && ldx < k) return PFNG_B200_ERR_SHAPE;
+    if (m == 0 || n == 0) return PFNG_B200_OK;
+    if (!out) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    if (!aligned(out, 4)) return PFNG_B200_ERR_ALIGNMENT;
+    if (k == 0) return PFNG_B200_OK;
+    if (!w || !a_or_x) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    if (!aligned(w, w_align(wtype))) return PFNG_B200_ERR_ALIGNMENT;
+    if (!aligned(a_or_x, f32_input ? 4 : a_align(wtype))) return PFNG_B200_ERR_ALIGNMENT;
+    return PFNG_B200_OK;
+}
+
+int check_quant(const float *x, int64_t ldx, const void *y, int64_t rows, int64_t k, int qk, uintptr_t yalign) {
+    if (rows < 0 || k < 0) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    if (k % qk != 0) return PFNG_B200_ERR_SHAPE;
+    if (rows > 0 && ldx < k) return PFNG_B200_ERR_SHAPE;
+    if (rows == 0 || k == 0) return PFNG_B200_OK;
+    if (!x || !y) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    if (!aligned(x, 4) || !aligned(y, yalign)) return PFNG_B200_ERR_ALIGNMENT;
+    return PFNG_B200_OK;
+}
+
+// Resolved kernel path for a matmul call.
+int resolve_path(int wtype, int64_t m, int64_t n, int64_t k, const void *w, int path) {
+    if (path == PFNG_B200_PATH_AUTO) {
+        if (m <= 8 && gemv_supported(wtype, m, n, k, w)) return PFNG_B200_PATH_GEMV;
+        if (m > 8 && gemm_supported(wtype, m, n, k, w)) return PFNG_B200_PATH_MMA;
+        return PFNG_B200_PATH_SIMPLE;
+    }
+    if (path == PFNG_B200_PATH_GEMV && !gemv_supported(wtype, m, n, k, w)) return -1;
+    if (path == PFNG_B200_PATH_MMA && !gemm_supported(wtype, m, n, k, w)) return -1;
+    return path;
+}
+
+size_t raw_a_bytes(int wtype, int64_t m, int64_t k) {
+    return static_cast<size_t>(m) * static_cast<size_t>(k / block_k(wtype)) * a_block_bytes(wtype);
+}
+
+// Workspace needed by a resolved path (f32: activations arrive as fp32).
+size_t workspace_for(int wtype, int64_t m, int64_t k, int resolved, bool f32) {
+    if (m == 0 || k == 0) return 0;
+    if (resolved == PFNG_B200_PATH_MMA) return split_a_bytes(m, k, block_k(wtype) == 32 ? 32 : 256);
+    if (resolved == PFNG_B200_PATH_SIMPLE && f32) return raw_a_bytes(wtype, m, k) + 256;
+    return 0;
+}
+
+cudaError_t zero_c(float *c, int64_t m, int64_t n, int64_t ldc, cudaStream_t s) {
+    return cudaMemset2DAsync(c, static_cast<size_t>(ldc) * sizeof(float), 0, static_cast<size_t>(n) * sizeof(float),
+                             static_cast<size_t>(m), s);
+}
+
+void *align_ptr(void *p, uintptr_t a) {
+    return reinterpret_cast<void *>((reinterpret_cast<uintptr_t>(p) + a - 1) & ~(a - 1));
+}
+
+// The shared body of mm / compute / partials.
+int run_matmul(int wtype, const void *w, const void *a, const float *x, int64_t ldx, float *c, int64_t ldc,
+               int32_t *partials, int64_t m, int64_t n, int64_t k, void *workspace, size_t workspace_bytes,
+               int path, cudaStream_t s) {
+    const bool f32 = x != nullptr;
+    int st = check_mm(wtype, w, f32 ? static_cast<const void *>(x) : a, partials ? static_cast<void *>(partials) : c,
+                      m, n, k, ldc, ldx, f32, partials != nullptr, path);
+    if (st != PFNG_B200_OK || m == 0 || n == 0) return st;
+    DeviceInfo *info = nullptr;
+    if ((st = device_info(&info)) != PFNG_B200_OK) return st;
+    if (k == 0) return partials ? PFNG_B200_OK : status_of(zero_c(c, m, n, ldc, s));
+    const int resolved = resolve_path(wtype, m, n, k, w, path);
+    if (resolved < 0) return PFNG_B200_ERR_UNSUPPORTED;
+    const size_t need = workspace_for(wtype, m, k, resolved, f32);
+    if (need > 0 && (!workspace || workspace_bytes < need)) return PFNG_B200_ERR_WORKSPACE;
+
+    cudaError_t e = cudaSuccess;
+    if (resolved == PFNG_B200_PATH_GEMV) {
+        GemvArgs g{wtype, w, f32 ? nullptr : a, x, ldx, c, ldc, partials, info->error_word, m, n, k};
+        e = launch_gemv(g, s);
+    } else if (resolved == PFNG_B200_PATH_MMA) {
+        const int qk = wtype == PFNG_B200_Q4_0 ? 32 : 256;
+        const SplitA sa = split_a_carve(workspace, m, k, qk);
+        if (wtype == PFNG_B200_Q4_0)
+            e = f32 ? launch_quantize_q8_0_split(x, ldx, sa, m, k, s) : launch_convert_q8_0_split(a, sa, m, k, s);
+        else
+            e = f32 ? launch_quantize_q8_K_split(x, ldx, sa, m, k, s) : launch_convert_q8_K_split(a, sa, m, k, s);
+        if (e == cudaSuccess) {
+            GemmArgs g{wtype, w, sa, c, ldc, partials, m, n, k};
+            e = launch_gemm(g, s);
+        }
+    } else {
+        const void *araw = a;
+        if (f32) {
+            void *buf = align_ptr(workspace, 256);
+            e = wtype == PFNG_B200_Q4_0 ? launch_quantize_q8_0(x, ldx, buf, m, k, s)
+                                        : launch_quantize_q8_K(x, ldx, buf, m, k, s);
+            araw = buf;
+        }
+        if (e == cudaSuccess) {
+            SimpleArgs g{wtype, w, araw, c, ldc, partials, m, n, k};
+            e = launch_simple(g, s);
+        }
+    }
+    return status_of(e);
+}
+
+size_t query_workspace(int wtype, int64_t m, int64_t n, int64_t k, int path, bool f32) {
+    if (wtype < 0 || wtype > 2 || m <= 0 || n <= 0 || k <= 0) return 0;
+    if (path == PFNG_B200_PATH_AUTO) {
+        // AUTO may take the tensor-core or the simple path depending on the
+        // pointers' alignment, so ask for what either needs.
+        const size_t mma = m > 8 ? workspace_for(wtype, m, k, PFNG_B200_PATH_MMA, f32) : 0;
+        const size_t simple = workspace_for(wtype, m, k, PFNG_B200_PATH_SIMPLE, f32);
+        return mma > simple ? mma : simple;
+    }
+    return workspace_for(wtype, m, k, path, f32);
+}
+
+}  // namespace
+
+int device_sm_count() {
+    DeviceInfo *info = current_info();
+    return info ? info->sm_count : 148;
+}
+
+size_t device_smem_optin() {
+    DeviceInfo *info = current_info();
+    return info ? info->smem_optin : 0;
+}
+
+size_t split_a_bytes(int64_t m, int64_t k, int block) {
+    const int64_t rows = round_up(m, kGemmTileM);
+    const size_t qs = static_cast<size_t>(rows * k);
+    const size_t d = static_cast<size_t>(rows * (k / block)) * sizeof(float);
+    const size_t aux = static_cast<size_t>(rows * (k / 32)) * sizeof(int32_t);
+    return 256 + round_up(static_cast<int64_t>(qs), 256) + round_up(static_cast<int64_t>(d), 256) +
+           round_up(static_cast<int64_t>(aux), 256);
+}
+
+SplitA split_a_carve(void *workspace, int64_t m, int64_t k, int block) {
+    SplitA s{};
+    s.rows_pad = round_up(m, kGemmTileM);
+    s.k = k;
+    uint8_t *p = static_cast<uint8_t *>(align_ptr(workspace, 256));
+    s.qs = reinterpret_cast<int8_t *>(p);
+    p += round_up(s.rows_pad * k, 256);
+    s.d = reinterpret_cast<float *>(p);
+    p += round_up(static_cast<int64_t>(s.rows_pad * (k / block) * sizeof(float)), 256);
+    s.aux = reinterpret_cast<int32_t *>(p);
+    return s;
+}
+
+}  // namespace pfng
+
+using namespace pfng;
+
+extern "C" {
+
+int pfng_b200_version(void) { return 1; }
+
+const char *pfng_b200_status_string(int status) {
+    switch (status) {
+    case PFNG_B200_OK: return "ok";
+    case PFNG_B200_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case PFNG_B200_ERR_SHAPE: return "unsupported shape";
+    case PFNG_B200_ERR_ALIGNMENT: return "misaligned pointer";
+    case PFNG_B200_ERR_WORKSPACE: return "workspace missing or too small";
+    case PFNG_B200_ERR_DEVICE: return "device is not compute capability 10.x";
+    case PFNG_B200_ERR_KERNEL_TIMEOUT: return "a bounded wait inside a kernel gave up";
+    case PFNG_B200_ERR_UNSUPPORTED: return "forced kernel path cannot run this shape";
+    default:
+        if (status <= PFNG_B200_ERR_CUDA_BASE)
+            return cudaGetErrorString(static_cast<cudaError_t>(PFNG_B200_ERR_CUDA_BASE - status));
+        return "unknown status";
+    }
+}
+
+int pfng_b200_check_kernel_error(void *stream) {
+    DeviceInfo *info = nullptr;
+    int st = device_info(&info);
+    if (st != PFNG_B200_OK) return st;
+    cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return status_of(e);
+    int value = 0;
+    if ((e = cudaMemcpy(&value, info->error_word, sizeof(int), cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return status_of(e);
+    if (value == 0) return PFNG_B200_OK;
+    const int zero = 0;
+    if ((e = cudaMemcpy(info->error_word, &zero, sizeof(int), cudaMemcpyHostToDevice)) != cudaSuccess)
+        return status_of(e);
+    return PFNG_B200_ERR_KERNEL_TIMEOUT;
+}
+
+int pfng_b200_quantize_q8_0(const float *x, int64_t ldx, void *y, int64_t m, int64_t k, void *stream) {
+    int st = check_quant(x, ldx, y, m, k, 32, 2);
+    if (st != PFNG_B200_OK || m == 0 || k == 0) return st;
+    DeviceInfo *info = nullptr;
+    if ((st = device_info(&info)) != PFNG_B200_OK) return st;
+    return status_of(launch_quantize_q8_0(x, ldx, y, m, k, static_cast<cudaStream_t>(stream)));
+}
+
+int pfng_b200_quantize_q8_K(const float *x, int64_t ldx, void *y, int64_t m, int64_t k, void *stream) {
+    int st = check_quant(x, ldx, y, m, k, 256, 4);
+    if (st != PFNG_B200_OK || m == 0 || k == 0) return st;
+    DeviceInfo *info = nullptr;
+    if ((st = device_info(&info)) != PFNG_B200_OK) return st;
+    return status_of(launch_quantize_q8_K(x, ldx, y, m, k, static_cast<cudaStream_t>(stream)));
+}
+
+int pfng_b200_quantize_q4_0(const float *x, int64_t ldx, void *y, int64_t n, int64_t k, void *stream) {
+    int st = check_quant(x, ldx, y, n, k, 32, 2);
+    if (st != PFNG_B200_OK || n == 0 || k == 0) return st;
+    DeviceInfo *info = nullptr;
+    if ((st = device_info(&info)) != PFNG_B200_OK) return st;
+    return status_of(launch_quantize_q4_0(x, ldx, y, n, k, static_cast<cudaStream_t>(stream)));
+}
+
+int pfng_b200_quantize_q4_K(const float *x, int64_t ldx, void *y, int64_t n, int64_t k, void *stream) {
+    int st = check_quant(x, ldx, y, n, k, 256, 4);
+    if (st != PFNG_B200_OK || n == 0 || k == 0) return st;
+    DeviceInfo *info = nullptr;
+    if ((st = device_info(&info)) != PFNG_B200_OK) return st;
+    return status_of(launch_quantize_q4_K(x, ldx, y, n, k, static_cast<cudaStream_t>(stream)));
+}
+
+size_t pfng_b200_mm_workspace_size(int wtype, int64_t m, int64_t n, int64_t k, int path) {
+    return query_workspace(wtype, m, n, k, path, false);
+}
+
+size_t pfng_b200_compute_workspace_size(int wtype, int64_t m, int64_t n, int64_t k, int path) {
+    return query_workspace(wtype, m, n, k, path, true);
+}
+
+int pfng_b200_mm_q4_0_q8_0(const void *w, const void *a, float *c, int64_t m, int64_t n, int64_t k, int64_t ldc,
+                           void *workspace, size_t workspace_bytes, int path, void *stream) {
+    return run_matmul(PFNG_B200_Q4_0, w, a, nullptr, 0, c, ldc, nullptr, m, n, k, workspace, workspace_bytes, path,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int pfng_b200_mm_q4_K_q8_K(const void *w, const void *a, float *c, int64_t m, int64_t n, int64_t k, int64_t ldc,
+                           void *workspace, size_t workspace_bytes, int path, void *stream) {
+    return run_matmul(PFNG_B200_Q4_K, w, a, nullptr, 0, c, ldc, nullptr, m, n, k, workspace, workspace_bytes, path,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int pfng_b200_mm_iq2_xxs_q8_K(const void *w, const void *a, float *c, int64_t m, int64_t n, int64_t k, int64_t ldc,
+                              void *workspace, size_t workspace_bytes, int path, void *stream) {
+    return run_matmul(PFNG_B200_IQ2_XXS, w, a, nullptr, 0, c, ldc, nullptr, m, n, k, workspace, workspace_bytes, path,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int pfng_b200_compute_q4_0(const void *w, const float *x, int64_t ldx, float *c, int64_t m, int64_t n, int64_t k,
+                           int64_t ldc, void *workspace, size_t workspace_bytes, int path, void *stream) {
+    return run_matmul(PFNG_B200_Q4_0, w, nullptr, x, ldx, c, ldc, nullptr, m, n, k, workspace, workspace_bytes, path,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int pfng_b200_compute_q4_K(const void *w, const float *x, int64_t ldx, float *c, int64_t m, int64_t n, int64_t k,
+                           int64_t ldc, void *workspace, size_t workspace_bytes, int path, void *stream) {
+    return run_matmul(PFNG_B200_Q4_K, w, nullptr, x, ldx, c, ldc, nullptr, m, n, k, workspace, workspace_bytes, path,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int pfng_b200_compute_iq2_xxs(const void *w, const float *x, int64_t ldx, float *c, int64_t m, int64_t n, int64_t k,
+                              int64_t ldc, void *workspace, size_t workspace_bytes, int path, void *stream) {
+    return run_matmul(PFNG_B200_IQ2_XXS, w, nullptr, x, ldx, c, ldc, nullptr, m, n, k, workspace, workspace_bytes,
+                      path, static_cast<cudaStream_t>(stream));
+}
+
+int pfng_b200_partials_q4_0_q8_0(const void *w, const void *a, int32_t *out, int64_t m, int64_t n, int64_t k,
+                                 void *workspace, size_t workspace_bytes, int path, void *stream) {
+    return run_matmul(PFNG_B200_Q4_0, w, a, nullptr, 0, nullptr, n, out, m, n, k, workspace, workspace_bytes, path,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int pfng_b200_partials_q4_K_q8_K(const void *w, const void *a, int32_t *out, int64_t m, int64_t n, int64_t k,
+                                 void *workspace, size_t workspace_bytes, int path, void *stream) {
+    return run_matmul(PFNG_B200_Q4_K, w, a, nullptr, 0, nullptr, n, out, m, n, k, workspace, workspace_bytes, path,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int pfng_b200_partials_iq2_xxs_q8_K(const void *w, const void *a, int32_t *out, int64_t m, int64_t n, int64_t k,
+                                    void *workspace, size_t workspace_bytes, int path, void *stream) {
+    return run_matmul(PFNG_B200_IQ2_XXS, w, a, nullptr, 0, nullptr, n, out, m, n, k, workspace, workspace_bytes,
+                      path, static_cast<cudaStream_t>(stream));
+}
+
+int pfng_b200_shard_rows(int64_t n, int world, int rank, int64_t granule, int64_t *begin, int64_t *end) {
+    if (n < 0 || world < 1 || rank < 0 || rank >= world || granule < 1 || !begin || !end)
+        return PFNG_B200_ERR_INVALID_ARGUMENT;
+    // Split ceil(n / granule) granules as evenly as possible; the first
+    // (granules % world) ranks take one extra; the last granule may be ragged.
+    const int64_t granules = (n + granule - 1) / granule;
+    const int64_t base = granules / world, extra = granules % world;
+    const int64_t g0 = rank * base + (rank < extra ? rank : extra);
+    const int64_t g1 = g0 + base + (rank < extra ? 1 : 0);
+    *begin = g0 * granule < n ? g0 * granule : n;
+    *end = g1 * granule < n ? g1 * granule : n;
+    return PFNG_B200_OK;
+}
+
+int pfng_b200_unshard_columns(const float *slices, float *c, int64_t m, int64_t n, int64_t ldc, int world,
+                              int64_t granule, int64_t slice_width, void *stream) {
+    if (m < 0 || n < 0 || world < 1 || granule < 1 || slice_width < 0) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    if (m > 0 && ldc < n) return PFNG_B200_ERR_SHAPE;
+    if (m == 0 || n == 0) return PFNG_B200_OK;
+    if (!slices || !c) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    if (!aligned(slices, 4) || !aligned(c, 4)) return PFNG_B200_ERR_ALIGNMENT;
+    for (int r = 0; r < world; ++r) {
+        int64_t b = 0, e = 0;
+        pfng_b200_shard_rows(n, world, r, granule, &b, &e);
+        if (e - b > slice_width) return PFNG_B200_ERR_SHAPE;
+    }
+    DeviceInfo *info = nullptr;
+    int st = device_info(&info);
+    if (st != PFNG_B200_OK) return st;
+    return status_of(launch_unshard_columns(slices, c, m, n, ldc, world, granule, slice_width,
+                                            static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

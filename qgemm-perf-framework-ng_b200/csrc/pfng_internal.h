@@ -1,0 +1,91 @@
+// pfng_internal.h -- host-side declarations shared by the .cu files of
+// libpfng_b200 (not part of the public C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace pfng {
+
+// "Split" activation operand used by the tensor-core GEMMs: int8 values
+// row-major [rows][k] (rows 16-byte aligned), one fp32 scale per block and an
+// int32 per 32-value sub-block (see each producer for its meaning).  The
+// layout lives in the caller's workspace and is rebuilt every call.
+struct SplitA {
+    int8_t *qs;      // [rows_pad][k]
+    float *d;        // [rows_pad][k / block]   block = 32 (q8_0) or 256 (q8_K)
+    int32_t *aux;    // [rows_pad][k / 32]
+    int64_t rows_pad;
+    int64_t k;
+};
+
+constexpr int64_t kGemmTileM = 128;
+inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+size_t split_a_bytes(int64_t m, int64_t k, int block);
+SplitA split_a_carve(void *workspace, int64_t m, int64_t k, int block);
+
+// quantize.cu
+cudaError_t launch_quantize_q8_0(const float *x, int64_t ldx, void *y, int64_t m, int64_t k, cudaStream_t s);
+cudaError_t launch_quantize_q8_K(const float *x, int64_t ldx, void *y, int64_t m, int64_t k, cudaStream_t s);
+cudaError_t launch_quantize_q4_0(const float *x, int64_t ldx, void *y, int64_t n, int64_t k, cudaStream_t s);
+cudaError_t launch_quantize_q4_K(const float *x, int64_t ldx, void *y, int64_t n, int64_t k, cudaStream_t s);
+// fp32 -> split operand (q8_0: aux = 0x4B400000 - 8 * sum(q) per 32; q8_K: aux = sum(q) per 32)
+cudaError_t launch_quantize_q8_0_split(const float *x, int64_t ldx, const SplitA &out, int64_t m, int64_t k,
+                                       cudaStream_t s);
+cudaError_t launch_quantize_q8_K_split(const float *x, int64_t ldx, const SplitA &out, int64_t m, int64_t k,
+                                       cudaStream_t s);
+// raw blocks -> split operand
+cudaError_t launch_convert_q8_0_split(const void *a, const SplitA &out, int64_t m, int64_t k, cudaStream_t s);
+cudaError_t launch_convert_q8_K_split(const void *a, const SplitA &out, int64_t m, int64_t k, cudaStream_t s);
+
+// gemv.cu -- small-m kernels.  `x` (fp32) or `a` (raw q8 blocks) is given.
+// partials != nullptr selects the integer-partials output instead of C.
+struct GemvArgs {
+    int wtype;
+    const void *w;
+    const void *a;      // raw q8_0 / q8_K blocks, or nullptr
+    const float *x;     // fp32 activations, or nullptr
+    int64_t ldx;
+    float *c;
+    int64_t ldc;
+    int32_t *partials;
+    int *err;
+    int64_t m, n, k;
+};
+bool gemv_supported(int wtype, int64_t m, int64_t n, int64_t k, const void *w);
+cudaError_t launch_gemv(const GemvArgs &args, cudaStream_t s);
+
+// gemm.cu -- tensor-core GEMM on a split activation operand.
+struct GemmArgs {
+    int wtype;
+    const void *w;
+    SplitA a;
+    float *c;
+    int64_t ldc;
+    int32_t *partials;
+    int64_t m, n, k;
+};
+bool gemm_supported(int wtype, int64_t m, int64_t n, int64_t k, const void *w);
+cudaError_t launch_gemm(const GemmArgs &args, cudaStream_t s);
+
+// simple.cu -- one thread per output element, any k multiple of the block.
+struct SimpleArgs {
+    int wtype;
+    const void *w;
+    const void *a;  // raw q8 blocks
+    float *c;
+    int64_t ldc;
+    int32_t *partials;
+    int64_t m, n, k;
+};
+cudaError_t launch_simple(const SimpleArgs &args, cudaStream_t s);
+
+// shard.cu
+cudaError_t launch_unshard_columns(const float *slices, float *c, int64_t m, int64_t n, int64_t ldc, int world,
+                                   int64_t granule, int64_t slice_width, cudaStream_t s);
+
+int device_sm_count();
+size_t device_smem_optin();
+
+}  // namespace pfng

@@ -1,0 +1,81 @@
+// pfng_quant.cuh -- the activation-quantizer cores shared by the standalone
+// quantizer kernels and the fused quantize+matmul kernels, so both produce
+// the same bytes.  Operation order follows the reference's
+// quantize_row_q8_0 / quantize_row_q8_K
+// (bench/llama_reference/llama_reference.cpp:38-70): IEEE divide for the
+// scale and its reciprocal, an IEEE multiply, then round half away from zero.
+#pragma once
+
+#include "pfng_common.cuh"
+
+namespace pfng {
+
+// ---------------------------------------------------------------------------
+// q8_0: 8 lanes per 32-value block, lane g of the group holds values 4g..4g+3.
+// llama_reference.cpp:38-52.
+// ---------------------------------------------------------------------------
+struct Q8_0Lane {
+    uint32_t q;      // 4 packed int8
+    uint16_t dbits;  // fp16 scale
+    int qsum;        // sum of the whole block's int8 values (all lanes)
+};
+
+PFNG_DEV Q8_0Lane q8_0_quantize_lane(const float v[4]) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float scale = __fdiv_rn(amax, 127.0f);
+    const float inv = scale != 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
+    Q8_0Lane r;
+    r.q = 0;
+    int s = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int qi = static_cast<int>(roundf(__fmul_rn(v[i], inv)));
+        s += qi;
+        r.q |= (static_cast<uint32_t>(qi) & 0xffu) << (8 * i);
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    r.qsum = s;
+    r.dbits = f32_to_f16_bits(scale);
+    return r;
+}
+
+// q8_K: one warp per 256-value block, lane l holds values 8l..8l+7.
+struct Q8_KLane {
+    uint32_t q0, q1;  // 8 packed int8 (values 8l..8l+3, 8l+4..8l+7)
+    int sum16;        // sum over the 16 values of lanes (l & ~1, l | 1): the bsums entry
+    int sum32;        // sum over the 32 values of lanes 4(l/4)..4(l/4)+3
+    float d;          // fp32 scale
+};
+
+PFNG_DEV Q8_KLane q8_K_quantize_lane(const float v[8]) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    Q8_KLane r;
+    r.d = __fdiv_rn(amax, 127.0f);
+    const float inv = r.d != 0.0f ? __fdiv_rn(1.0f, r.d) : 0.0f;
+    r.q0 = 0;
+    r.q1 = 0;
+    int s = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int qi = static_cast<int>(roundf(__fmul_rn(v[i], inv)));
+        s += qi;
+        if (i < 4)
+            r.q0 |= (static_cast<uint32_t>(qi) & 0xffu) << (8 * i);
+        else
+            r.q1 |= (static_cast<uint32_t>(qi) & 0xffu) << (8 * (i - 4));
+    }
+    r.sum16 = s + __shfl_xor_sync(0xffffffffu, s, 1);
+    r.sum32 = r.sum16 + __shfl_xor_sync(0xffffffffu, r.sum16, 2);
+    return r;
+}
+
+}  // namespace pfng

@@ -1,0 +1,255 @@
+"""Python binding of libpfng_b200 (the C ABI in include/pfng_b200.h).
+
+The library computes perf-framework-ng's hot path on a B200:
+``C[m][n] = A[m][k] . W[n][k]^T`` for q4_0 x q8_0, q4_K x q8_K and
+iq2_xxs x q8_K, plus the fp32 -> q8_0 / q8_K / q4_0 / q4_K quantizers.  This
+module is plumbing: torch tensors hold device memory and streams, every
+computation is a call into the shared library.  There is no CPU path; if the
+library is not built, importing the functions raises immediately.
+
+Block arrays are passed as flat ``torch.uint8`` tensors in the ggml wire
+layout (bench/llama_reference and include/ggml.h of the reference); the
+``*_BYTES`` constants give the size of one block.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import pathlib
+import re
+
+PACKAGE_DIR = pathlib.Path(__file__).resolve().parent.parent
+REPO_ROOT = PACKAGE_DIR.parent
+LIB_PATH = PACKAGE_DIR / "libpfng_b200.so"
+HEADER_PATH = REPO_ROOT / "include" / "pfng_b200.h"
+
+Q4_0, Q4_K, IQ2_XXS = 0, 1, 2
+WTYPES = {"q4_0": Q4_0, "q4_K": Q4_K, "iq2_xxs": IQ2_XXS}
+PATH_AUTO, PATH_GEMV, PATH_MMA, PATH_SIMPLE = 0, 1, 2, 3
+PATHS = {"auto": PATH_AUTO, "gemv": PATH_GEMV, "mma": PATH_MMA, "simple": PATH_SIMPLE}
+
+Q4_0_BYTES, Q8_0_BYTES, Q4_K_BYTES, Q8_K_BYTES, IQ2_XXS_BYTES = 18, 34, 144, 292, 66
+# weight type -> (weight block bytes, weight block k, activation block bytes, activation block k)
+LAYOUT = {
+    Q4_0: (Q4_0_BYTES, 32, Q8_0_BYTES, 32),
+    Q4_K: (Q4_K_BYTES, 256, Q8_K_BYTES, 256),
+    IQ2_XXS: (IQ2_XXS_BYTES, 256, Q8_K_BYTES, 256),
+}
+
+OK = 0
+ERR_KERNEL_TIMEOUT = -6
+
+
+class PfngError(RuntimeError):
+    def __init__(self, status: int, what: str):
+        self.status = status
+        super().__init__(f"{what}: {status_string(status)} (status {status})")
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded shared library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `make -C {PACKAGE_DIR}` "
+                "(or __graft_entry__.build()); there is no fallback implementation")
+        _lib = ctypes.CDLL(str(LIB_PATH))
+        _declare(_lib)
+    return _lib
+
+
+def _declare(L: ctypes.CDLL) -> None:
+    P, I64, I, S = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
+    L.pfng_b200_version.restype = I
+    L.pfng_b200_status_string.restype = ctypes.c_char_p
+    L.pfng_b200_status_string.argtypes = [I]
+    L.pfng_b200_check_kernel_error.restype = I
+    L.pfng_b200_check_kernel_error.argtypes = [P]
+    for q in ("q8_0", "q8_K", "q4_0", "q4_K"):
+        f = getattr(L, f"pfng_b200_quantize_{q}")
+        f.restype = I
+        f.argtypes = [P, I64, P, I64, I64, P]
+    for name in ("mm_workspace_size", "compute_workspace_size"):
+        f = getattr(L, f"pfng_b200_{name}")
+        f.restype = S
+        f.argtypes = [I, I64, I64, I64, I]
+    for t in ("q4_0_q8_0", "q4_K_q8_K", "iq2_xxs_q8_K"):
+        f = getattr(L, f"pfng_b200_mm_{t}")
+        f.restype = I
+        f.argtypes = [P, P, P, I64, I64, I64, I64, P, S, I, P]
+        f = getattr(L, f"pfng_b200_partials_{t}")
+        f.restype = I
+        f.argtypes = [P, P, P, I64, I64, I64, P, S, I, P]
+    for t in ("q4_0", "q4_K", "iq2_xxs"):
+        f = getattr(L, f"pfng_b200_compute_{t}")
+        f.restype = I
+        f.argtypes = [P, P, I64, P, I64, I64, I64, I64, P, S, I, P]
+    L.pfng_b200_shard_rows.restype = I
+    L.pfng_b200_shard_rows.argtypes = [I64, I, I, I64, ctypes.POINTER(I64), ctypes.POINTER(I64)]
+    L.pfng_b200_unshard_columns.restype = I
+    L.pfng_b200_unshard_columns.argtypes = [P, P, I64, I64, I64, I, I64, I64, P]
+
+
+def header_functions() -> list[str]:
+    """Names of every function include/pfng_b200.h declares."""
+    text = HEADER_PATH.read_text()
+    return sorted(set(re.findall(r"\b(pfng_b200_[a-zA-Z0-9_]+)\s*\(", text)))
+
+
+def status_string(status: int) -> str:
+    return lib().pfng_b200_status_string(status).decode()
+
+
+def _check(status: int, what: str) -> None:
+    if status != OK:
+        raise PfngError(status, what)
+
+
+def _ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream) -> int:
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def _suffix(wtype: int) -> str:
+    return {Q4_0: "q4_0_q8_0", Q4_K: "q4_K_q8_K", IQ2_XXS: "iq2_xxs_q8_K"}[wtype]
+
+
+def _wt(wtype) -> int:
+    return WTYPES[wtype] if isinstance(wtype, str) else int(wtype)
+
+
+def _path(path) -> int:
+    return PATHS[path] if isinstance(path, str) else int(path)
+
+
+# ---------------------------------------------------------------- quantizers
+def _quantize(kind: str, x, qk: int, block_bytes: int, out=None, stream=None):
+    import torch
+    rows, k = x.shape
+    if out is None:
+        out = torch.empty(rows * (k // qk) * block_bytes, dtype=torch.uint8, device=x.device)
+    _check(getattr(lib(), f"pfng_b200_quantize_{kind}")(
+        _ptr(x), x.stride(0), _ptr(out), rows, k, _stream(stream)), f"quantize_{kind}")
+    return out
+
+
+def quantize_q8_0(x, out=None, stream=None):
+    """fp32 [m][k] -> block_q8_0 bytes (reference llama_reference.cpp:38-52)."""
+    return _quantize("q8_0", x, 32, Q8_0_BYTES, out, stream)
+
+
+def quantize_q8_K(x, out=None, stream=None):
+    """fp32 [m][k] -> block_q8_K bytes (reference llama_reference.cpp:54-70)."""
+    return _quantize("q8_K", x, 256, Q8_K_BYTES, out, stream)
+
+
+def quantize_q4_0(x, out=None, stream=None):
+    """fp32 [n][k] weights -> block_q4_0 bytes (reference llama_reference.cpp:13-36)."""
+    return _quantize("q4_0", x, 32, Q4_0_BYTES, out, stream)
+
+
+def quantize_q4_K(x, out=None, stream=None):
+    """fp32 [n][k] weights -> block_q4_K bytes (reference llama_reference.cpp:72-111)."""
+    return _quantize("q4_K", x, 256, Q4_K_BYTES, out, stream)
+
+
+def quantize_activation(wtype, x, out=None, stream=None):
+    return quantize_q8_0(x, out, stream) if _wt(wtype) == Q4_0 else quantize_q8_K(x, out, stream)
+
+
+# ------------------------------------------------------------------- matmul
+def mm_workspace_size(wtype, m: int, n: int, k: int, path="auto") -> int:
+    return lib().pfng_b200_mm_workspace_size(_wt(wtype), m, n, k, _path(path))
+
+
+def compute_workspace_size(wtype, m: int, n: int, k: int, path="auto") -> int:
+    return lib().pfng_b200_compute_workspace_size(_wt(wtype), m, n, k, _path(path))
+
+
+def _workspace(nbytes: int, device, workspace):
+    import torch
+    if nbytes == 0:
+        return workspace
+    if workspace is not None and workspace.numel() >= nbytes:
+        return workspace
+    return torch.empty(nbytes, dtype=torch.uint8, device=device)
+
+
+def mm(wtype, w, a, m: int, n: int, k: int, out=None, path="auto", workspace=None, stream=None):
+    """C = A . W^T with pre-quantized activations `a` (q8_0 or q8_K bytes)."""
+    import torch
+    wt, p = _wt(wtype), _path(path)
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, device=w.device)
+    ws = _workspace(mm_workspace_size(wt, m, n, k, p), w.device, workspace)
+    nbytes = 0 if ws is None else ws.numel()
+    _check(getattr(lib(), f"pfng_b200_mm_{_suffix(wt)}")(
+        _ptr(w), _ptr(a), _ptr(out), m, n, k, out.stride(0), _ptr(ws), nbytes, p, _stream(stream)),
+        f"mm_{_suffix(wt)}")
+    return out
+
+
+def compute(wtype, w, x, n: int, out=None, path="auto", workspace=None, stream=None):
+    """The reference's compute(): quantize fp32 activations x [m][k], then C = A . W^T."""
+    import torch
+    wt, p = _wt(wtype), _path(path)
+    m, k = x.shape
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, device=w.device)
+    ws = _workspace(compute_workspace_size(wt, m, n, k, p), w.device, workspace)
+    nbytes = 0 if ws is None else ws.numel()
+    name = {Q4_0: "q4_0", Q4_K: "q4_K", IQ2_XXS: "iq2_xxs"}[wt]
+    _check(getattr(lib(), f"pfng_b200_compute_{name}")(
+        _ptr(w), _ptr(x), x.stride(0), _ptr(out), m, n, k, out.stride(0), _ptr(ws), nbytes, p,
+        _stream(stream)), f"compute_{name}")
+    return out
+
+
+def partials(wtype, w, a, m: int, n: int, k: int, path="auto", workspace=None, stream=None):
+    """int32 [m][n][k/32] integer sub-block dot products of the chosen kernel path."""
+    import torch
+    wt, p = _wt(wtype), _path(path)
+    out = torch.empty((m, n, k // 32), dtype=torch.int32, device=w.device)
+    ws = _workspace(mm_workspace_size(wt, m, n, k, p), w.device, workspace)
+    nbytes = 0 if ws is None else ws.numel()
+    _check(getattr(lib(), f"pfng_b200_partials_{_suffix(wt)}")(
+        _ptr(w), _ptr(a), _ptr(out), m, n, k, _ptr(ws), nbytes, p, _stream(stream)),
+        f"partials_{_suffix(wt)}")
+    return out
+
+
+def check_kernel_error(stream=None) -> None:
+    _check(lib().pfng_b200_check_kernel_error(_stream(stream)), "kernel error word")
+
+
+# ----------------------------------------------------------------- sharding
+def shard_rows(n: int, world: int, rank: int, granule: int) -> tuple[int, int]:
+    b, e = ctypes.c_int64(0), ctypes.c_int64(0)
+    _check(lib().pfng_b200_shard_rows(n, world, rank, granule, ctypes.byref(b), ctypes.byref(e)),
+           "shard_rows")
+    return b.value, e.value
+
+
+def unshard_columns(slices, m: int, n: int, world: int, granule: int, out=None, stream=None):
+    import torch
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, device=slices.device)
+    width = slices.shape[-1]
+    _check(lib().pfng_b200_unshard_columns(_ptr(slices), _ptr(out), m, n, out.stride(0), world, granule,
+                                           width, _stream(stream)), "unshard_columns")
+    return out
+
+
+def loaded_library_path() -> str:
+    """Path of the shared object this process loaded (for provenance checks)."""
+    lib()
+    return os.path.realpath(LIB_PATH)
