@@ -112,6 +112,28 @@ int pfng_b200_compute_iq2_xxs(const void *w, const float *x, int64_t ldx, float 
                               int64_t k, int64_t ldc, void *workspace, size_t workspace_bytes, int path,
                               void *stream);
 
+/* ---- decode: several weight matrices sharing one activation --------------
+ * The projections that read the same layer input (Q/K/V, or gate/up) in ONE
+ * launch: the fp32 activations x [m][ldx] are quantized once per CTA (q8_0
+ * for q4_0, q8_K otherwise) and the weight rows of all `count` matrices are
+ * streamed as one sequence, so the per-launch start-up is paid once.  Matrix
+ * g has n[g] rows (all share k) and writes C_g [m][ldc[g]].  w, n, c and ldc
+ * are HOST arrays of `count` entries holding device pointers / sizes.
+ * Needs m <= 8, count <= 8 and 16-byte aligned weights (the GEMV path),
+ * otherwise returns PFNG_B200_ERR_UNSUPPORTED.  Every C_g is bit-identical
+ * to pfng_b200_compute_*(w[g], ..., PFNG_B200_PATH_GEMV).
+ * flags: 0, or PFNG_B200_OVERLAP_WEIGHTS -- a promise that no kernel still
+ * running before this call on `stream` writes the weights.  The launch may
+ * then start (programmatic dependent launch) and stream the weights while
+ * the preceding kernel finishes; reading x and writing C stay ordered after
+ * it.  Back-to-back decode launches then form one continuous weight stream.
+ * The reference has no counterpart: it multiplies one matrix per call
+ * (llama_reference.cpp:213); this batches those calls. */
+#define PFNG_B200_OVERLAP_WEIGHTS 1u
+int pfng_b200_compute_grouped(int wtype, int count, const void *const *w, const int64_t *n, float *const *c,
+                              const int64_t *ldc, const float *x, int64_t ldx, int64_t m, int64_t k, unsigned flags,
+                              void *stream);
+
 /* ---- integer partials (verification) ------------------------------------
  * out: int32 [m][n][k / 32], the integer dot product of every 32-value
  * sub-block, produced by the same kernel path as the matmul (`path`) before

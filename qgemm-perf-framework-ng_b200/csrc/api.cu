@@ -104,11 +104,11 @@ int check_quant(const float *x, int64_t ldx, const void *y, int64_t rows, int64_
 // Resolved kernel path for a matmul call.
 int resolve_path(int wtype, int64_t m, int64_t n, int64_t k, const void *w, int path) {
     if (path == PFNG_B200_PATH_AUTO) {
-        if (m <= 8 && gemv_supported(wtype, m, n, k, w)) return PFNG_B200_PATH_GEMV;
+        if (m <= 8 && gemv_supported(wtype, m, 1, &n, k, &w)) return PFNG_B200_PATH_GEMV;
         if (m > 8 && gemm_supported(wtype, m, n, k, w)) return PFNG_B200_PATH_MMA;
         return PFNG_B200_PATH_SIMPLE;
     }
-    if (path == PFNG_B200_PATH_GEMV && !gemv_supported(wtype, m, n, k, w)) return -1;
+    if (path == PFNG_B200_PATH_GEMV && !gemv_supported(wtype, m, 1, &n, k, &w)) return -1;
     if (path == PFNG_B200_PATH_MMA && !gemm_supported(wtype, m, n, k, w)) return -1;
     return path;
 }
@@ -152,7 +152,20 @@ int run_matmul(int wtype, const void *w, const void *a, const float *x, int64_t 
 
     cudaError_t e = cudaSuccess;
     if (resolved == PFNG_B200_PATH_GEMV) {
-        GemvArgs g{wtype, w, f32 ? nullptr : a, x, ldx, c, ldc, partials, info->error_word, m, n, k};
+        GemvArgs g{};
+        g.wtype = wtype;
+        g.count = 1;
+        g.w[0] = w;
+        g.c[0] = c;
+        g.ldc[0] = ldc;
+        g.n[0] = n;
+        g.a = f32 ? nullptr : a;
+        g.x = x;
+        g.ldx = ldx;
+        g.partials = partials;
+        g.err = info->error_word;
+        g.m = m;
+        g.k = k;
         e = launch_gemv(g, s);
     } else if (resolved == PFNG_B200_PATH_MMA) {
         const int qk = wtype == PFNG_B200_Q4_0 ? 32 : 256;
@@ -342,6 +355,46 @@ int pfng_b200_compute_iq2_xxs(const void *w, const float *x, int64_t ldx, float 
                               int64_t ldc, void *workspace, size_t workspace_bytes, int path, void *stream) {
     return run_matmul(PFNG_B200_IQ2_XXS, w, nullptr, x, ldx, c, ldc, nullptr, m, n, k, workspace, workspace_bytes,
                       path, static_cast<cudaStream_t>(stream));
+}
+
+int pfng_b200_compute_grouped(int wtype, int count, const void *const *w, const int64_t *n, float *const *c,
+                              const int64_t *ldc, const float *x, int64_t ldx, int64_t m, int64_t k, unsigned flags,
+                              void *stream) {
+    if (wtype < 0 || wtype > 2 || count < 1 || !w || !n || !c || !ldc) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    if (flags & ~static_cast<unsigned>(PFNG_B200_OVERLAP_WEIGHTS)) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    if (count > kGemvMaxGroup) return PFNG_B200_ERR_UNSUPPORTED;
+    for (int g = 0; g < count; ++g) {
+        const int st = check_mm(wtype, w[g], x, c[g], m, n[g], k, ldc[g], ldx, true, false, PFNG_B200_PATH_GEMV);
+        if (st != PFNG_B200_OK) return st;
+    }
+    if (m == 0) return PFNG_B200_OK;
+    DeviceInfo *info = nullptr;
+    int st = device_info(&info);
+    if (st != PFNG_B200_OK) return st;
+    GemvArgs ga{};
+    ga.wtype = wtype;
+    for (int g = 0; g < count; ++g) {
+        if (n[g] == 0) continue;  // empty matrices take no part
+        if (k == 0) {
+            if ((st = status_of(zero_c(c[g], m, n[g], ldc[g], static_cast<cudaStream_t>(stream)))) != PFNG_B200_OK)
+                return st;
+            continue;
+        }
+        ga.w[ga.count] = w[g];
+        ga.c[ga.count] = c[g];
+        ga.ldc[ga.count] = ldc[g];
+        ga.n[ga.count] = n[g];
+        ++ga.count;
+    }
+    if (ga.count == 0) return PFNG_B200_OK;
+    if (!gemv_supported(wtype, m, ga.count, ga.n, k, ga.w)) return PFNG_B200_ERR_UNSUPPORTED;
+    ga.x = x;
+    ga.ldx = ldx;
+    ga.err = info->error_word;
+    ga.m = m;
+    ga.k = k;
+    ga.overlap = (flags & PFNG_B200_OVERLAP_WEIGHTS) != 0;
+    return status_of(launch_gemv(ga, static_cast<cudaStream_t>(stream)));
 }
 
 int pfng_b200_partials_q4_0_q8_0(const void *w, const void *a, int32_t *out, int64_t m, int64_t n, int64_t k,

@@ -5,18 +5,30 @@
 // bench/llama_reference/llama_reference.cpp:165-205 (dot products :113-161).
 //
 // Structure (one persistent CTA per SM, warp-specialised):
-//   * a producer warp streams tiles of R consecutive weight rows -- a
+//   * a producer warp streams tiles of R consecutive weight rows -- one
 //     contiguous byte range of W -- into a ring of S shared-memory stages with
 //     bulk TMA copies (cp.async.bulk, mbarrier transaction counts, L2
 //     evict-first since every weight byte is read once);
 //   * 8 consumer warps first stage the activation rows in shared memory
 //     (either the caller's q8 blocks, or fp32 rows quantized in place with
-//     the same code as the standalone quantizer), then each takes one row of
-//     a tile: lanes walk the row's blocks, unpack 4-bit / grid weights to
-//     int8, dot them against the activations with dp4a, fold the integer
-//     partials with the block scales in fp32 and reduce across the warp.
-// The kernel is bound by HBM bandwidth; per weight byte it issues a handful
-// of shared-memory reads and integer ops, well under what an SM sustains.
+//     the same code as the standalone quantizer), then each repeatedly claims
+//     the next PAIR of rows of the CTA's tile sequence (a shared counter, so
+//     warps that finish early take more work; a tile's stage is released
+//     once all its pairs are done) and processes it: lanes walk the rows'
+//     blocks, unpack 4-bit / grid weights to int8, dot them against the
+//     activations with dp4a, fold the integer partials with the block scales
+//     in fp32 and reduce across the warp.  The two q4_0 rows of a pair are
+//     interleaved, which doubles the independent work in flight per warp.
+//   Tiles stay >= ~9 KB: bulk copies much smaller than that do not reach
+//   full HBM bandwidth with one CTA per SM.
+//
+// q4_0 lane mapping: lane l of a warp takes the block PAIR (2l, 2l+1) of each
+// group of 64 blocks.  A pair is 36 contiguous bytes = 9 aligned words at word
+// offset 9l + i, so the 32 lanes hit 32 distinct banks (9 is odd): the reads
+// are conflict-free and need one funnel shift per word for the even block
+// only.  The activations use the same pairing, stored chunk-major so each
+// 16-byte read of a warp is one contiguous 512-byte line; for m = 1 they are
+// held in registers for the whole kernel.
 //
 // Every mbarrier wait is bounded (pfng_common.cuh): a wait that gives up
 // records an error code, stops the CTA's work and returns.
@@ -31,131 +43,224 @@ namespace {
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kGemvThreads = kConsumerThreads + 32;
-constexpr int kMaxStages = 16;
+constexpr int kMaxStages = 32;       // a power of two
+constexpr int kPairRows = 2;         // rows a warp claims at a time
+constexpr int kMaxGroup = kGemvMaxGroup;
 constexpr uint32_t kBarrierBytes = 2 * kMaxStages * 8;
 constexpr uint32_t kGridTableBytes = 256 * 8;
 constexpr uint32_t kStageSlack = 32;  // bytes read past a window by aligned loads; never used
+constexpr int kRegGroupsMax = 2;      // m = 1 keeps up to 2 x 64 blocks (k <= 4096) in registers
 
 struct GemvParams {
-    const uint8_t *w;
     const uint8_t *a;  // raw q8 blocks or nullptr
     const float *x;    // fp32 activations or nullptr
     int64_t ldx;
-    float *c;
-    int64_t ldc;
-    int32_t *partials;
+    int32_t *partials; // count == 1: [m][n][k / 32]
     int *err;  // library error word for bounded waits
-    int m;
-    int64_t n, k;
-    int64_t row_bytes;
-    int rows_per_tile;
-    int64_t num_tiles;
-    int stages;
+    int m, n, k;       // n: rows of matrix 0 (partials indexing)
+    int x_vec;         // fp32 rows are 16-byte aligned with ldx % 4 == 0
+    int row_bytes;
+    int rows_per_tile;  // 4 or 8 (a multiple of kPairRows)
+    int pair_shift;     // log2(rows_per_tile / kPairRows)
+    int num_tiles;
+    int stages;        // a power of two
+    int stage_shift;   // log2(stages)
     uint32_t stage_bytes;
     uint32_t grid_offset, act_offset, stage_offset;
+    int groups;        // q4_0: ceil(nb / 64)
+    int overlap;       // launched as a programmatic dependent (see kernel)
+    // weight matrices sharing the activations (count >= 1); tiles of matrix
+    // g are [tile_base[g], tile_base[g + 1]) of the launch's tile sequence
+    int count;
+    const uint8_t *wg[kMaxGroup];
+    float *cg[kMaxGroup];
+    int64_t ldcg[kMaxGroup];
+    int ng[kMaxGroup];
+    int tile_base[kMaxGroup + 1];
 };
 
-// Activation rows staged in shared memory.
-struct Act {
-    const int8_t *qs;     // [MT][k]
-    const float *d;       // [MT][k/32] (q8_0) or [MT][k/256] (q8_K)
-    const int32_t *s8;    // q8_0: 8 * sum of the block's values, [MT][k/32]
-    const int16_t *bs;    // q8_K: bsums [MT][k/16]
+// Output of one weight matrix.
+struct Out {
+    float *c;
+    int64_t ldc;
 };
 
 PFNG_DEV void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumerThreads) : "memory"); }
 
-// --------------------------------------------------------------------------
-// activation staging
-// --------------------------------------------------------------------------
+// dp4a with an unsigned first operand: sum of (u8 a_i) * (s8 b_i) + c.
+PFNG_DEV int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// sum over 16 weights (4 words of nibbles: low nibbles are k 0..15, high
+// nibbles k 16..31 of a q4_0 block) times the activations, without the -8.
+PFNG_DEV int nibble_dot(const uint32_t (&q)[4], const uint4 &alo, const uint4 &ahi) {
+    int lo = dp4a_us(q[0] & 0x0f0f0f0fu, static_cast<int>(alo.x), 0);
+    int hi = dp4a_us(q[0] & 0xf0f0f0f0u, static_cast<int>(ahi.x), 0);
+    lo = dp4a_us(q[1] & 0x0f0f0f0fu, static_cast<int>(alo.y), lo);
+    hi = dp4a_us(q[1] & 0xf0f0f0f0u, static_cast<int>(ahi.y), hi);
+    lo = dp4a_us(q[2] & 0x0f0f0f0fu, static_cast<int>(alo.z), lo);
+    hi = dp4a_us(q[2] & 0xf0f0f0f0u, static_cast<int>(ahi.z), hi);
+    lo = dp4a_us(q[3] & 0x0f0f0f0fu, static_cast<int>(alo.w), lo);
+    hi = dp4a_us(q[3] & 0xf0f0f0f0u, static_cast<int>(ahi.w), hi);
+    return lo + (hi >> 4);  // hi holds 16 x the high-nibble dot product exactly
+}
+
+// ---------------------------------------------------------------------------
+// q4_0 activation staging: "pair-chunk" layout.
+//   qs:  per row m, per group t of 64 blocks, 4 chunks x 32 lanes x 16 B;
+//        block j = 64 t + 2 l + h, bytes [16 c', 16 c' + 16) of the block
+//        live in chunk c = 2 h + c' at lane slot l.
+//   d:   float [m][64 * groups], s8: int [m][64 * groups] (8 * sum of q).
+// Blocks past nb are zero.
+// ---------------------------------------------------------------------------
+PFNG_DEV uint32_t q4_0_act_qs_offset(int m, int groups, int j, int byte_in_block) {
+    const int t = j >> 6, l = (j >> 1) & 31, h = j & 1;
+    const int c = 2 * h + (byte_in_block >> 4);
+    return static_cast<uint32_t>((((m * groups + t) * 4 + c) * 32 + l) * 16 + (byte_in_block & 15));
+}
+
 template <int MT, bool kF32>
 PFNG_DEV void stage_act_q8_0(const GemvParams &p, uint8_t *smem, int tid) {
-    const int64_t nb = p.k / 32;
-    int8_t *qs = reinterpret_cast<int8_t *>(smem + p.act_offset);
-    float *d = reinterpret_cast<float *>(qs + MT * p.k);
-    int32_t *s8 = reinterpret_cast<int32_t *>(d + MT * nb);
-    const int64_t total = MT * nb;
+    const int nb = p.k / 32;
+    const int nbp = p.groups * 64;
+    uint8_t *qs = smem + p.act_offset;
+    float *d = reinterpret_cast<float *>(qs + MT * p.groups * 2048);
+    int32_t *s8 = reinterpret_cast<int32_t *>(d + MT * nbp);
+    const int total = MT * nbp;  // a multiple of 64: every warp iteration covers 4 live blocks
     const int lane = tid & 31, warp = tid >> 5, g = lane & 7;
-    for (int64_t wb = warp * 4; wb < total; wb += kConsumerWarps * 4) {
-        const int64_t bi = wb + (lane >> 3);
-        const bool live = bi < total;
-        const int64_t row = live ? bi / nb : 0, col = live ? bi % nb : 0;
-        const bool valid = live && row < p.m;
-        uint32_t q = 0;
-        uint32_t dbits = 0;
-        int qsum = 0;
-        if constexpr (kF32) {
-            float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            if (valid) {
-                const float *src = p.x + row * p.ldx + col * 32 + 4 * g;
+    constexpr int kBatch = 4;    // iterations whose loads are issued together
+    for (int wb0 = warp * 4; wb0 < total; wb0 += kBatch * kConsumerWarps * 4) {
+        // 1) issue the loads of kBatch iterations (one memory round trip)
+        uint32_t raw_q[kBatch], raw_d[kBatch];
+        float v[kBatch][4];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) v[i] = __ldg(src + i);
-            }
-            const Q8_0Lane r = q8_0_quantize_lane(v);
-            q = r.q;
-            dbits = r.dbits;
-            qsum = r.qsum;
-        } else {
+        for (int it = 0; it < kBatch; ++it) {
+            const int wb = wb0 + it * kConsumerWarps * 4;
+            const int bi = wb + (lane >> 3);
+            const int row = bi / nbp, j = bi % nbp;
+            const bool valid = wb < total && row < p.m && j < nb;
+            v[it][0] = v[it][1] = v[it][2] = v[it][3] = 0.0f;
+            raw_q[it] = raw_d[it] = 0;
             if (valid) {
-                const uint8_t *blk = p.a + (row * nb + col) * kQ8_0Bytes;
-                const uint16_t *h = reinterpret_cast<const uint16_t *>(blk + 2 + 4 * g);
-                q = static_cast<uint32_t>(__ldg(h)) | (static_cast<uint32_t>(__ldg(h + 1)) << 16);
-                dbits = __ldg(reinterpret_cast<const uint16_t *>(blk));
-            }
-            int s = __dp4a(static_cast<int>(q), 0x01010101, 0);
+                if constexpr (kF32) {
+                    const float *src = p.x + row * p.ldx + j * 32 + 4 * g;
+                    if (p.x_vec) {
+                        const float4 t = __ldg(reinterpret_cast<const float4 *>(src));
+                        v[it][0] = t.x, v[it][1] = t.y, v[it][2] = t.z, v[it][3] = t.w;
+                    } else {
 #pragma unroll
-            for (int o = 1; o < 8; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-            qsum = s;
+                        for (int i = 0; i < 4; ++i) v[it][i] = __ldg(src + i);
+                    }
+                } else {
+                    const uint8_t *blk = p.a + (static_cast<int64_t>(row) * nb + j) * kQ8_0Bytes;
+                    const uint16_t *h = reinterpret_cast<const uint16_t *>(blk + 2 + 4 * g);
+                    raw_q[it] = static_cast<uint32_t>(__ldg(h)) | (static_cast<uint32_t>(__ldg(h + 1)) << 16);
+                    raw_d[it] = __ldg(reinterpret_cast<const uint16_t *>(blk));
+                }
+            }
         }
-        if (!live) continue;
-        *reinterpret_cast<uint32_t *>(qs + row * p.k + col * 32 + 4 * g) = valid ? q : 0u;
-        if (g == 0) {
-            d[row * nb + col] = valid ? f16_bits_to_f32(dbits) : 0.0f;
-            s8[row * nb + col] = valid ? 8 * qsum : 0;
+        // 2) quantize (the batch's chains interleaved) / reduce, and store
+        Q8_0Lane qr[kBatch];
+        if constexpr (kF32) q8_0_quantize_lanes<kBatch>(v, qr);
+#pragma unroll
+        for (int it = 0; it < kBatch; ++it) {
+            const int wb = wb0 + it * kConsumerWarps * 4;
+            if (wb >= total) break;
+            const int bi = wb + (lane >> 3);
+            const int row = bi / nbp, j = bi % nbp;
+            const bool valid = row < p.m && j < nb;
+            uint32_t q, dbits;
+            int qsum;
+            if constexpr (kF32) {
+                q = qr[it].q;
+                dbits = qr[it].dbits;
+                qsum = qr[it].qsum;
+            } else {
+                q = raw_q[it];
+                dbits = raw_d[it];
+                int sm = __dp4a(static_cast<int>(q), 0x01010101, 0);
+#pragma unroll
+                for (int o = 1; o < 8; o <<= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+                qsum = sm;
+            }
+            *reinterpret_cast<uint32_t *>(qs + q4_0_act_qs_offset(row, p.groups, j, 4 * g)) = valid ? q : 0u;
+            if (g == 0) {
+                d[row * nbp + j] = valid ? f16_bits_to_f32(dbits) : 0.0f;
+                s8[row * nbp + j] = valid ? 8 * qsum : 0;
+            }
         }
     }
 }
 
+// q8_K activations (q4_K, iq2_xxs): qs [MT][k], d [MT][k/256], bsums [MT][k/16].
 template <int MT, bool kF32>
 PFNG_DEV void stage_act_q8_K(const GemvParams &p, uint8_t *smem, int tid) {
-    const int64_t nb = p.k / 256;
+    const int nb = p.k / 256;
     int8_t *qs = reinterpret_cast<int8_t *>(smem + p.act_offset);
     float *d = reinterpret_cast<float *>(qs + MT * p.k);
     int16_t *bs = reinterpret_cast<int16_t *>(d + MT * nb);
-    const int64_t total = MT * nb;
+    const int total = MT * nb;
     const int lane = tid & 31, warp = tid >> 5;
-    for (int64_t bi = warp; bi < total; bi += kConsumerWarps) {
-        const int64_t row = bi / nb, col = bi % nb;
-        const bool valid = row < p.m;
-        uint32_t q0 = 0, q1 = 0;
-        float dv = 0.0f;
-        int bsum = 0;  // lanes < 16: bsums[lane]
-        if constexpr (kF32) {
-            float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            if (valid) {
-                const float *src = p.x + row * p.ldx + col * 256 + 8 * lane;
+    constexpr int kBatch = 2;  // blocks whose loads are issued together
+    for (int bi0 = warp; bi0 < total; bi0 += kBatch * kConsumerWarps) {
+        float v[kBatch][8];
+        uint32_t q0[kBatch], q1[kBatch];
+        float dv[kBatch];
+        int bsum[kBatch];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = __ldg(src + i);
+        for (int it = 0; it < kBatch; ++it) {
+            const int bi = bi0 + it * kConsumerWarps;
+            const int row = bi / nb, col = bi % nb;
+            const bool valid = bi < total && row < p.m;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[it][i] = 0.0f;
+            q0[it] = q1[it] = 0;
+            dv[it] = 0.0f;
+            bsum[it] = 0;
+            if (!valid) continue;
+            if constexpr (kF32) {
+                const float *src = p.x + row * p.ldx + col * 256 + 8 * lane;
+                if (p.x_vec) {
+                    const float4 t0 = __ldg(reinterpret_cast<const float4 *>(src));
+                    const float4 t1 = __ldg(reinterpret_cast<const float4 *>(src + 4));
+                    v[it][0] = t0.x, v[it][1] = t0.y, v[it][2] = t0.z, v[it][3] = t0.w;
+                    v[it][4] = t1.x, v[it][5] = t1.y, v[it][6] = t1.z, v[it][7] = t1.w;
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) v[it][i] = __ldg(src + i);
+                }
+            } else {
+                const uint8_t *blk = p.a + (static_cast<int64_t>(row) * nb + col) * kQ8_KBytes;
+                const uint32_t *q = reinterpret_cast<const uint32_t *>(blk + kQ8_KQsOffset + 8 * lane);
+                q0[it] = __ldg(q);
+                q1[it] = __ldg(q + 1);
+                dv[it] = __ldg(reinterpret_cast<const float *>(blk));
+                if (lane < 16) bsum[it] = __ldg(reinterpret_cast<const int16_t *>(blk + kQ8_KBsumsOffset) + lane);
             }
-            const Q8_KLane r = q8_K_quantize_lane(v);
-            q0 = r.q0;
-            q1 = r.q1;
-            dv = r.d;
-            // bsums entry j lives in lanes 2j and 2j+1
-            bsum = __shfl_sync(0xffffffffu, r.sum16, (2 * lane) & 31);
-        } else if (valid) {
-            const uint8_t *blk = p.a + (row * nb + col) * kQ8_KBytes;
-            const uint32_t *q = reinterpret_cast<const uint32_t *>(blk + kQ8_KQsOffset + 8 * lane);
-            q0 = __ldg(q);
-            q1 = __ldg(q + 1);
-            dv = __ldg(reinterpret_cast<const float *>(blk));
-            if (lane < 16) bsum = __ldg(reinterpret_cast<const int16_t *>(blk + kQ8_KBsumsOffset) + lane);
         }
-        uint32_t *dst = reinterpret_cast<uint32_t *>(qs + row * p.k + col * 256 + 8 * lane);
-        dst[0] = q0;
-        dst[1] = q1;
-        if (lane < 16) bs[row * (p.k / 16) + col * 16 + lane] = static_cast<int16_t>(valid ? bsum : 0);
-        if (lane == 0) d[row * nb + col] = dv;
+#pragma unroll
+        for (int it = 0; it < kBatch; ++it) {
+            const int bi = bi0 + it * kConsumerWarps;
+            if (bi >= total) break;
+            const int row = bi / nb, col = bi % nb;
+            const bool valid = row < p.m;
+            if constexpr (kF32) {
+                const Q8_KLane r = q8_K_quantize_lane(v[it]);
+                q0[it] = r.q0;
+                q1[it] = r.q1;
+                dv[it] = r.d;
+                // bsums entry j lives in lanes 2j and 2j+1
+                bsum[it] = __shfl_sync(0xffffffffu, r.sum16, (2 * lane) & 31);
+            }
+            uint32_t *dst = reinterpret_cast<uint32_t *>(qs + row * p.k + col * 256 + 8 * lane);
+            dst[0] = q0[it];
+            dst[1] = q1[it];
+            if (lane < 16) bs[row * (p.k / 16) + col * 16 + lane] = static_cast<int16_t>(valid ? bsum[it] : 0);
+            if (lane == 0) d[row * nb + col] = valid ? dv[it] : 0.0f;
+        }
     }
 }
 
@@ -164,54 +269,143 @@ PFNG_DEV void stage_act_q8_K(const GemvParams &p, uint8_t *smem, int tid) {
 // offset of the row inside it.  Loops are warp-uniform (shuffles inside).
 // --------------------------------------------------------------------------
 template <int MT>
-PFNG_DEV void warp_reduce_store(const GemvParams &p, float (&acc)[MT], int64_t row, int lane) {
+PFNG_DEV void warp_reduce_store(const GemvParams &p, const Out &o, float (&acc)[MT], int row, int lane) {
 #pragma unroll
     for (int mi = 0; mi < MT; ++mi) {
         float v = acc[mi];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (lane == 0 && mi < p.m) p.c[mi * p.ldc + row] = v;
+        for (int sh = 16; sh > 0; sh >>= 1) v += __shfl_xor_sync(0xffffffffu, v, sh);
+        if (lane == 0 && mi < p.m) o.c[mi * o.ldc + row] = v;
     }
 }
 
-template <int MT, bool kPartials>
-PFNG_DEV void row_q4_0(const GemvParams &p, const Act &act, const uint8_t *tile, uint32_t row_off, int64_t row,
-                       int lane) {
-    const int nb = static_cast<int>(p.k / 32);
-    float acc[MT];
+// Activations of one lane for the m = 1 register path.
+template <int GM>
+struct ActRegs {
+    uint4 q[GM][4];   // chunks 0..3 of the lane's block pair in each group
+    float2 d[GM];
+    int2 s8[GM];
+};
+
+// Weights of one lane's block pair: 36 bytes at a 4-aligned offset.
+struct PairW {
+    uint32_t qa[4], qb[4];
+    float da, db;
+};
+
+PFNG_DEV PairW load_pair(const uint8_t *tile, uint32_t off) {
+    const uint32_t *w = reinterpret_cast<const uint32_t *>(tile + off);
+    uint32_t v[9];
 #pragma unroll
-    for (int mi = 0; mi < MT; ++mi) acc[mi] = 0.0f;
-    for (int base = 0; base < nb; base += 32) {
-        const int j = base + lane;
-        if (j < nb) {
-            uint32_t q[4], dbits;
-            load_q4_0_block_smem(tile, row_off + 18u * j, q, dbits);
-            const float dw = f16_bits_to_f32(dbits);
-            uint32_t lo[4], hi[4];
+    for (int i = 0; i < 9; ++i) v[i] = w[i];
+    PairW r;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) lo[i] = q[i] & 0x0f0f0f0fu, hi[i] = (q[i] >> 4) & 0x0f0f0f0fu;
+    for (int i = 0; i < 4; ++i) r.qa[i] = __funnelshift_r(v[i], v[i + 1], 16);
 #pragma unroll
-            for (int mi = 0; mi < MT; ++mi) {
-                const int4 *a4 = reinterpret_cast<const int4 *>(act.qs + mi * p.k + 32 * j);
-                const int4 a0 = a4[0], a1 = a4[1];
-                int dot = dp4a(lo[0], a0.x, 0);
-                dot = dp4a(lo[1], a0.y, dot);
-                dot = dp4a(lo[2], a0.z, dot);
-                dot = dp4a(lo[3], a0.w, dot);
-                dot = dp4a(hi[0], a1.x, dot);
-                dot = dp4a(hi[1], a1.y, dot);
-                dot = dp4a(hi[2], a1.z, dot);
-                dot = dp4a(hi[3], a1.w, dot);
-                const int isum = dot - act.s8[mi * nb + j];
-                if constexpr (kPartials) {
-                    if (mi < p.m) p.partials[(mi * p.n + row) * nb + j] = isum;
-                } else {
-                    acc[mi] = __fmaf_rn(__fmul_rn(static_cast<float>(isum), dw), act.d[mi * nb + j], acc[mi]);
+    for (int i = 0; i < 4; ++i) r.qb[i] = v[5 + i];
+    r.da = f16_bits_to_f32(v[0] & 0xffffu);
+    r.db = f16_bits_to_f32(v[4] >> 16);
+    return r;
+}
+
+// m = 1, activations in registers (groups <= GM).  Rows row0 and row0 + 1
+// (the second only if nrows == 2) start at row_off and row_off + row_bytes.
+template <int GM, bool kPartials>
+PFNG_DEV void rows_q4_0_reg(const GemvParams &p, const Out &o, const ActRegs<GM> &ar, const uint8_t *tile,
+                            uint32_t row_off, int row0, int nrows, int lane) {
+    const int nb = p.k / 32;
+    const uint32_t off1 = row_off + static_cast<uint32_t>(nrows > 1 ? p.row_bytes : 0);
+    float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll
+    for (int t = 0; t < GM; ++t) {
+        if (t < p.groups && 64 * t + 2 * lane < nb) {
+            const uint32_t o = 1152u * t + 36u * lane;
+            const PairW w0 = load_pair(tile, row_off + o);
+            const PairW w1 = load_pair(tile, off1 + o);
+            const int ia0 = nibble_dot(w0.qa, ar.q[t][0], ar.q[t][1]) - ar.s8[t].x;
+            const int ia1 = nibble_dot(w1.qa, ar.q[t][0], ar.q[t][1]) - ar.s8[t].x;
+            const int ib0 = nibble_dot(w0.qb, ar.q[t][2], ar.q[t][3]) - ar.s8[t].y;
+            const int ib1 = nibble_dot(w1.qb, ar.q[t][2], ar.q[t][3]) - ar.s8[t].y;
+            if constexpr (kPartials) {
+                const int j = 64 * t + 2 * lane;
+                int32_t *out = p.partials + static_cast<int64_t>(row0) * nb + j;
+                out[0] = ia0;
+                out[1] = ib0;
+                if (nrows > 1) {
+                    out[nb] = ia1;
+                    out[nb + 1] = ib1;
                 }
+            } else {
+                acc0 = __fmaf_rn(__fmul_rn(static_cast<float>(ia0), w0.da), ar.d[t].x, acc0);
+                acc1 = __fmaf_rn(__fmul_rn(static_cast<float>(ia1), w1.da), ar.d[t].x, acc1);
+                acc0 = __fmaf_rn(__fmul_rn(static_cast<float>(ib0), w0.db), ar.d[t].y, acc0);
+                acc1 = __fmaf_rn(__fmul_rn(static_cast<float>(ib1), w1.db), ar.d[t].y, acc1);
             }
         }
     }
-    if constexpr (!kPartials) warp_reduce_store<MT>(p, acc, row, lane);
+    if constexpr (!kPartials) {
+#pragma unroll
+        for (int sh = 16; sh > 0; sh >>= 1) {
+            acc0 += __shfl_xor_sync(0xffffffffu, acc0, sh);
+            acc1 += __shfl_xor_sync(0xffffffffu, acc1, sh);
+        }
+        if (lane == 0) {
+            o.c[row0] = acc0;
+            if (nrows > 1) o.c[row0 + 1] = acc1;
+        }
+    }
+}
+
+// any m <= 8, activations in shared memory; two rows as above.
+template <int MT, bool kPartials>
+PFNG_DEV void rows_q4_0_smem(const GemvParams &p, const Out &o, const uint8_t *act, const uint8_t *tile,
+                             uint32_t row_off, int row0, int nrows, int lane) {
+    const int nb = p.k / 32;
+    const int nbp = p.groups * 64;
+    const float *ad = reinterpret_cast<const float *>(act + MT * p.groups * 2048);
+    const int32_t *as8 = reinterpret_cast<const int32_t *>(ad + MT * nbp);
+    const uint32_t off1 = row_off + static_cast<uint32_t>(nrows > 1 ? p.row_bytes : 0);
+    float acc0[MT], acc1[MT];
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi) acc0[mi] = 0.0f, acc1[mi] = 0.0f;
+    for (int t = 0; t < p.groups; ++t) {
+        if (64 * t + 2 * lane >= nb) continue;
+        const uint32_t o = 1152u * t + 36u * lane;
+        const PairW w0 = load_pair(tile, row_off + o);
+        const PairW w1 = load_pair(tile, off1 + o);
+        const int j = 64 * t + 2 * lane;
+#pragma unroll
+        for (int mi = 0; mi < MT; ++mi) {
+            const uint4 *aq = reinterpret_cast<const uint4 *>(act + ((mi * p.groups + t) * 4) * 512) + lane;
+            const uint4 c0 = aq[0], c1 = aq[32], c2 = aq[64], c3 = aq[96];
+            const float2 da = *reinterpret_cast<const float2 *>(ad + mi * nbp + j);
+            const int2 s8 = *reinterpret_cast<const int2 *>(as8 + mi * nbp + j);
+            const int ia0 = nibble_dot(w0.qa, c0, c1) - s8.x;
+            const int ia1 = nibble_dot(w1.qa, c0, c1) - s8.x;
+            const int ib0 = nibble_dot(w0.qb, c2, c3) - s8.y;
+            const int ib1 = nibble_dot(w1.qb, c2, c3) - s8.y;
+            if constexpr (kPartials) {
+                if (mi < p.m) {
+                    int32_t *out = p.partials + (static_cast<int64_t>(mi) * p.n + row0) * nb + j;
+                    out[0] = ia0;
+                    out[1] = ib0;
+                    if (nrows > 1) {
+                        out[nb] = ia1;
+                        out[nb + 1] = ib1;
+                    }
+                }
+            } else {
+                acc0[mi] = __fmaf_rn(__fmul_rn(static_cast<float>(ia0), w0.da), da.x, acc0[mi]);
+                acc1[mi] = __fmaf_rn(__fmul_rn(static_cast<float>(ia1), w1.da), da.x, acc1[mi]);
+                acc0[mi] = __fmaf_rn(__fmul_rn(static_cast<float>(ib0), w0.db), da.y, acc0[mi]);
+                acc1[mi] = __fmaf_rn(__fmul_rn(static_cast<float>(ib1), w1.db), da.y, acc1[mi]);
+            }
+        }
+    }
+    if constexpr (!kPartials) {
+        warp_reduce_store<MT>(p, o, acc0, row0, lane);
+        if (nrows > 1) warp_reduce_store<MT>(p, o, acc1, row0 + 1, lane);
+    }
 }
 
 PFNG_DEV uint32_t scale_byte(uint32_t s0, uint32_t s1, uint32_t s2, int i) {
@@ -231,9 +425,12 @@ PFNG_DEV void q4_K_scale_min(uint32_t s0, uint32_t s1, uint32_t s2, int j, int &
 }
 
 template <int MT, bool kPartials>
-PFNG_DEV void row_q4_K(const GemvParams &p, const Act &act, const uint8_t *tile, uint32_t row_off, int64_t row,
-                       int lane) {
-    const int nbk = static_cast<int>(p.k / 256);
+PFNG_DEV void row_q4_K(const GemvParams &p, const Out &o, const uint8_t *act, const uint8_t *tile, uint32_t row_off,
+                       int row, int lane) {
+    const int nbk = p.k / 256;
+    const int8_t *aqs = reinterpret_cast<const int8_t *>(act);
+    const float *ad = reinterpret_cast<const float *>(aqs + MT * p.k);
+    const int16_t *abs16 = reinterpret_cast<const int16_t *>(ad + MT * nbk);
     const int units = nbk * 8;  // (block, nibble pair, half of the 32 bytes)
     float acc[MT];
 #pragma unroll
@@ -253,47 +450,48 @@ PFNG_DEV void row_q4_K(const GemvParams &p, const Act &act, const uint8_t *tile,
         q4_K_scale_min(s0, s1, s2, sbl, scl, mnl);
         q4_K_scale_min(s0, s1, s2, sbh, sch, mnh);
         const float d = f16_bits_to_f32(dd & 0xffffu), dmin = f16_bits_to_f32(dd >> 16);
-        const uint32_t lo0 = qv.x & 0x0f0f0f0fu, lo1 = qv.y & 0x0f0f0f0fu, lo2 = qv.z & 0x0f0f0f0fu,
-                       lo3 = qv.w & 0x0f0f0f0fu;
-        const uint32_t hi0 = (qv.x >> 4) & 0x0f0f0f0fu, hi1 = (qv.y >> 4) & 0x0f0f0f0fu,
-                       hi2 = (qv.z >> 4) & 0x0f0f0f0fu, hi3 = (qv.w >> 4) & 0x0f0f0f0fu;
+        const uint32_t q[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
         for (int mi = 0; mi < MT; ++mi) {
-            const int8_t *aq = act.qs + mi * p.k + b * 256 + 16 * h;
+            const int8_t *aq = aqs + mi * p.k + b * 256 + 16 * h;
             const int4 al = *reinterpret_cast<const int4 *>(aq + sbl * 32);
             const int4 ah = *reinterpret_cast<const int4 *>(aq + sbh * 32);
-            int ql = dp4a(lo0, al.x, 0);
-            ql = dp4a(lo1, al.y, ql);
-            ql = dp4a(lo2, al.z, ql);
-            ql = dp4a(lo3, al.w, ql);
-            int qh = dp4a(hi0, ah.x, 0);
-            qh = dp4a(hi1, ah.y, qh);
-            qh = dp4a(hi2, ah.z, qh);
-            qh = dp4a(hi3, ah.w, qh);
+            int ql = dp4a_us(q[0] & 0x0f0f0f0fu, al.x, 0);
+            int qh = dp4a_us(q[0] & 0xf0f0f0f0u, ah.x, 0);
+            ql = dp4a_us(q[1] & 0x0f0f0f0fu, al.y, ql);
+            qh = dp4a_us(q[1] & 0xf0f0f0f0u, ah.y, qh);
+            ql = dp4a_us(q[2] & 0x0f0f0f0fu, al.z, ql);
+            qh = dp4a_us(q[2] & 0xf0f0f0f0u, ah.z, qh);
+            ql = dp4a_us(q[3] & 0x0f0f0f0fu, al.w, ql);
+            qh = dp4a_us(q[3] & 0xf0f0f0f0u, ah.w, qh);
+            qh >>= 4;
             if constexpr (kPartials) {
                 const int fl = ql + __shfl_xor_sync(0xffffffffu, ql, 1);
                 const int fh = qh + __shfl_xor_sync(0xffffffffu, qh, 1);
                 if (live && h == 0 && mi < p.m) {
-                    int32_t *out = p.partials + (mi * p.n + row) * (p.k / 32) + b * 8;
+                    int32_t *out = p.partials + (static_cast<int64_t>(mi) * p.n + row) * (p.k / 32) + b * 8;
                     out[sbl] = fl;
                     out[sbh] = fh;
                 }
             } else if (live) {
-                const int16_t *bs = act.bs + mi * (p.k / 16) + b * 16;
+                const int16_t *bs = abs16 + mi * (p.k / 16) + b * 16;
                 const int i1 = scl * ql + sch * qh;
                 const int i2 = mnl * bs[sbl * 2 + h] + mnh * bs[sbh * 2 + h];
-                const float part = __fsub_rn(__fmul_rn(d, static_cast<float>(i1)), __fmul_rn(dmin, static_cast<float>(i2)));
-                acc[mi] = __fmaf_rn(act.d[mi * nbk + b], part, acc[mi]);
+                const float part =
+                    __fsub_rn(__fmul_rn(d, static_cast<float>(i1)), __fmul_rn(dmin, static_cast<float>(i2)));
+                acc[mi] = __fmaf_rn(ad[mi * nbk + b], part, acc[mi]);
             }
         }
     }
-    if constexpr (!kPartials) warp_reduce_store<MT>(p, acc, row, lane);
+    if constexpr (!kPartials) warp_reduce_store<MT>(p, o, acc, row, lane);
 }
 
 template <int MT, bool kPartials>
-PFNG_DEV void row_iq2_xxs(const GemvParams &p, const Act &act, const uint8_t *tile, uint32_t row_off, int64_t row,
-                          int lane, const uint2 *grid) {
-    const int nbk = static_cast<int>(p.k / 256);
+PFNG_DEV void row_iq2_xxs(const GemvParams &p, const Out &o, const uint8_t *act, const uint8_t *tile,
+                          uint32_t row_off, int row, int lane, const uint2 *grid) {
+    const int nbk = p.k / 256;
+    const int8_t *aqs = reinterpret_cast<const int8_t *>(act);
+    const float *ad = reinterpret_cast<const float *>(aqs + MT * p.k);
     const int units = nbk * 8;  // (block, 32-value group)
     float acc[MT];
 #pragma unroll
@@ -321,80 +519,93 @@ PFNG_DEV void row_iq2_xxs(const GemvParams &p, const Act &act, const uint8_t *ti
             const int scale = 2 * static_cast<int>(ss >> 28) + 1;
 #pragma unroll
             for (int mi = 0; mi < MT; ++mi) {
-                const int4 *a4 = reinterpret_cast<const int4 *>(act.qs + mi * p.k + b * 256 + sb * 32);
+                const int4 *a4 = reinterpret_cast<const int4 *>(aqs + mi * p.k + b * 256 + sb * 32);
                 const int4 a0 = a4[0], a1 = a4[1];
-                int dot = dp4a(static_cast<int>(v[0]), a0.x, 0);
-                dot = dp4a(static_cast<int>(v[1]), a0.y, dot);
-                dot = dp4a(static_cast<int>(v[2]), a0.z, dot);
-                dot = dp4a(static_cast<int>(v[3]), a0.w, dot);
-                dot = dp4a(static_cast<int>(v[4]), a1.x, dot);
-                dot = dp4a(static_cast<int>(v[5]), a1.y, dot);
-                dot = dp4a(static_cast<int>(v[6]), a1.z, dot);
-                dot = dp4a(static_cast<int>(v[7]), a1.w, dot);
+                int dot0 = dp4a(static_cast<int>(v[0]), a0.x, 0);
+                int dot1 = dp4a(static_cast<int>(v[4]), a1.x, 0);
+                dot0 = dp4a(static_cast<int>(v[1]), a0.y, dot0);
+                dot1 = dp4a(static_cast<int>(v[5]), a1.y, dot1);
+                dot0 = dp4a(static_cast<int>(v[2]), a0.z, dot0);
+                dot1 = dp4a(static_cast<int>(v[6]), a1.z, dot1);
+                dot0 = dp4a(static_cast<int>(v[3]), a0.w, dot0);
+                dot1 = dp4a(static_cast<int>(v[7]), a1.w, dot1);
+                const int dot = dot0 + dot1;
                 if constexpr (kPartials) {
-                    if (mi < p.m) p.partials[(mi * p.n + row) * (p.k / 32) + b * 8 + sb] = dot;
+                    if (mi < p.m) p.partials[(static_cast<int64_t>(mi) * p.n + row) * (p.k / 32) + b * 8 + sb] = dot;
                 } else {
-                    const float s = __fmul_rn(__fmul_rn(0.125f, d), act.d[mi * nbk + b]);
+                    const float s = __fmul_rn(__fmul_rn(0.125f, d), ad[mi * nbk + b]);
                     acc[mi] = __fmaf_rn(s, static_cast<float>(scale * dot), acc[mi]);
                 }
             }
         }
     }
-    if constexpr (!kPartials) warp_reduce_store<MT>(p, acc, row, lane);
+    if constexpr (!kPartials) warp_reduce_store<MT>(p, o, acc, row, lane);
 }
 
 // --------------------------------------------------------------------------
 // the kernel
 // --------------------------------------------------------------------------
-template <int WT, int MT, bool kPartials, bool kF32>
+// RG > 0: q4_0 with m = 1 and the activations held in registers (RG groups).
+template <int WT, int MT, int RG, bool kPartials, bool kF32>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + kMaxStages;
     __shared__ int abort_flag;
+    __shared__ int next_tile;
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
-    const int R = p.rows_per_tile;
     const int S = p.stages;
 
-    if (tid == 0) {
-        for (int s = 0; s < S; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], R);
-        }
-        abort_flag = 0;
+    // Programmatic dependent launch: let the next launch on the stream start
+    // as soon as this grid's CTAs are resident (it needs the other half of
+    // the SM's shared memory).  Only the weight stream runs before
+    // griddepcontrol.wait below; activations and outputs are ordered after
+    // the preceding grid as usual.
+    if (p.overlap) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    if (tid < S) {
+        mbar_init(&full[tid], 1);
+        mbar_init(&empty[tid], p.rows_per_tile / kPairRows);  // one arrival per row pair
         fence_mbar_init();
+    }
+    if (tid == 0) {
+        abort_flag = 0;
+        next_tile = 0;
     }
     __syncthreads();
 
     if (warp == kConsumerWarps) {
-        // ---------------- producer ----------------
+        // ---------------- producer: tiles blockIdx.x + i * gridDim.x, in order ----------------
         if (lane == 0) {
             const uint64_t policy = l2_policy_evict_first();
-            int64_t issued = 0;
-            for (int64_t i = 0;; ++i) {
-                const int64_t tile = blockIdx.x + i * gridDim.x;
-                if (tile >= p.num_tiles) break;
-                const int stage = static_cast<int>(i % S);
-                if (i >= S && !mbar_wait(&empty[stage], static_cast<uint32_t>(((i / S) & 1) ^ 1), p.err, kErrWaitEmpty)) {
+            int issued = 0, stage = 0;
+            uint32_t phase = 0;
+            int g = 0;  // matrix of the current tile (tiles only increase)
+            for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+                if (issued >= S && !mbar_wait(&empty[stage], phase ^ 1u, p.err, kErrWaitEmpty)) {
                     abort_flag = 1;
                     break;
                 }
                 if (*reinterpret_cast<volatile int *>(&abort_flag)) break;
-                const int64_t start = tile * R * p.row_bytes;
-                const int64_t last = (tile + 1) * R < p.n ? (tile + 1) * R : p.n;
-                const int64_t end = last * p.row_bytes;
+                while (tile >= p.tile_base[g + 1]) ++g;
+                const int lt = tile - p.tile_base[g];
+                const int ng = p.ng[g];
+                const int64_t start = static_cast<int64_t>(lt) * p.rows_per_tile * p.row_bytes;
+                const int last = (lt + 1) * p.rows_per_tile < ng ? (lt + 1) * p.rows_per_tile : ng;
+                const int64_t end = static_cast<int64_t>(last) * p.row_bytes;
                 const int64_t ws = start & ~int64_t(15), we = (end + 15) & ~int64_t(15);
                 const uint32_t bytes = static_cast<uint32_t>(we - ws);
+                const uint8_t *src = p.wg[g] + ws;
                 uint8_t *dst = smem + p.stage_offset + static_cast<uint32_t>(stage) * p.stage_bytes;
                 mbar_arrive_expect_tx(&full[stage], bytes);
-                bulk_copy_g2s(dst, p.w + ws, bytes, &full[stage], policy);
-                issued = i + 1;
+                bulk_copy_g2s(dst, src, bytes, &full[stage], policy);
+                ++issued;
+                if (++stage == S) stage = 0, phase ^= 1u;
             }
             // Do not leave while copies into this CTA's shared memory are in
             // flight (matters only when a consumer gave up early).
-            for (int64_t i = issued - S > 0 ? issued - S : 0; i < issued; ++i)
-                mbar_wait(&full[i % S], static_cast<uint32_t>((i / S) & 1), p.err, kErrWaitFull);
+            for (int i = issued - S > 0 ? issued - S : 0; i < issued; ++i)
+                mbar_wait(&full[i & (S - 1)], static_cast<uint32_t>((i >> p.stage_shift) & 1), p.err, kErrWaitFull);
         }
         return;
     }
@@ -417,46 +628,78 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
             grid[i] = make_uint2(lo, hi);
         }
     }
-    Act act;
-    if constexpr (WT == 0) {
+    const uint8_t *act = smem + p.act_offset;
+    if (p.overlap) asm volatile("griddepcontrol.wait;" ::: "memory");
+    if constexpr (WT == 0)
         stage_act_q8_0<MT, kF32>(p, smem, tid);
-        const int64_t nb = p.k / 32;
-        act.qs = reinterpret_cast<const int8_t *>(smem + p.act_offset);
-        act.d = reinterpret_cast<const float *>(act.qs + MT * p.k);
-        act.s8 = reinterpret_cast<const int32_t *>(act.d + MT * nb);
-        act.bs = nullptr;
-    } else {
+    else
         stage_act_q8_K<MT, kF32>(p, smem, tid);
-        const int64_t nb = p.k / 256;
-        act.qs = reinterpret_cast<const int8_t *>(smem + p.act_offset);
-        act.d = reinterpret_cast<const float *>(act.qs + MT * p.k);
-        act.bs = reinterpret_cast<const int16_t *>(act.d + MT * nb);
-        act.s8 = nullptr;
-    }
     consumer_sync();
 
-    const int G = kConsumerWarps / R;
-    const int grp = warp / R, r = warp % R;
-    for (int64_t i = grp;; i += G) {
-        const int64_t tile = blockIdx.x + i * gridDim.x;
+    ActRegs<(RG > 0 ? RG : 1)> ar;
+    if constexpr (RG > 0) {
+        const int nbp = p.groups * 64;
+        const float *ad = reinterpret_cast<const float *>(act + p.groups * 2048);
+        const int32_t *as8 = reinterpret_cast<const int32_t *>(ad + nbp);
+#pragma unroll
+        for (int t = 0; t < RG; ++t) {
+            if (t < p.groups) {
+                const uint4 *aq = reinterpret_cast<const uint4 *>(act + t * 2048) + lane;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) ar.q[t][c] = aq[32 * c];
+                ar.d[t] = *reinterpret_cast<const float2 *>(ad + 64 * t + 2 * lane);
+                ar.s8[t] = *reinterpret_cast<const int2 *>(as8 + 64 * t + 2 * lane);
+            } else {
+#pragma unroll
+                for (int c = 0; c < 4; ++c) ar.q[t][c] = make_uint4(0, 0, 0, 0);
+                ar.d[t] = make_float2(0.0f, 0.0f);
+                ar.s8[t] = make_int2(0, 0);
+            }
+        }
+    }
+
+    int g = 0;  // matrix of the claimed tile (claims only increase)
+    for (;;) {
+        int q = 0;
+        if (lane == 0) q = atomicAdd(&next_tile, 1);
+        q = __shfl_sync(0xffffffffu, q, 0);
+        const int i = q >> p.pair_shift;                   // local tile index
+        const int pr = q & ((1 << p.pair_shift) - 1);      // pair within the tile
+        const int tile = blockIdx.x + i * gridDim.x;
         if (tile >= p.num_tiles) break;
         if (*reinterpret_cast<volatile int *>(&abort_flag)) break;
-        const int stage = static_cast<int>(i % S);
-        if (!mbar_wait(&full[stage], static_cast<uint32_t>((i / S) & 1), p.err, kErrWaitFull)) {
+        const int stage = i & (S - 1);
+        if (!mbar_wait(&full[stage], static_cast<uint32_t>((i >> p.stage_shift) & 1), p.err, kErrWaitFull)) {
             abort_flag = 1;
             break;
         }
-        const int64_t row = tile * R + r;
-        if (row < p.n) {
-            const int64_t ws = (tile * R * p.row_bytes) & ~int64_t(15);
-            const uint32_t row_off = static_cast<uint32_t>(row * p.row_bytes - ws);
+        while (tile >= p.tile_base[g + 1]) ++g;
+        const int lt = tile - p.tile_base[g];
+        const Out o{p.cg[g], p.ldcg[g]};
+        const int tile_row = lt * p.rows_per_tile;
+        const int row0 = tile_row + kPairRows * pr;
+        const int nrows = p.ng[g] - row0 < kPairRows ? p.ng[g] - row0 : kPairRows;
+        if (nrows > 0) {
+            // offset of row0 in the stage: the window starts at the tile's
+            // first byte rounded down to 16 (low bits from wrap-around math)
+            const uint32_t row_off =
+                static_cast<uint32_t>(kPairRows * pr) * static_cast<uint32_t>(p.row_bytes) +
+                ((static_cast<uint32_t>(tile_row) * static_cast<uint32_t>(p.row_bytes)) & 15u);
             const uint8_t *buf = smem + p.stage_offset + static_cast<uint32_t>(stage) * p.stage_bytes;
-            if constexpr (WT == 0)
-                row_q4_0<MT, kPartials>(p, act, buf, row_off, row, lane);
-            else if constexpr (WT == 1)
-                row_q4_K<MT, kPartials>(p, act, buf, row_off, row, lane);
-            else
-                row_iq2_xxs<MT, kPartials>(p, act, buf, row_off, row, lane, grid);
+            if constexpr (WT == 0) {
+                if constexpr (RG > 0)
+                    rows_q4_0_reg<RG, kPartials>(p, o, ar, buf, row_off, row0, nrows, lane);
+                else
+                    rows_q4_0_smem<MT, kPartials>(p, o, act, buf, row_off, row0, nrows, lane);
+            } else {
+                for (int r = 0; r < nrows; ++r) {
+                    const uint32_t off = row_off + static_cast<uint32_t>(r * p.row_bytes);
+                    if constexpr (WT == 1)
+                        row_q4_K<MT, kPartials>(p, o, act, buf, off, row0 + r, lane);
+                    else
+                        row_iq2_xxs<MT, kPartials>(p, o, act, buf, off, row0 + r, lane, grid);
+                }
+            }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[stage]);
@@ -474,83 +717,141 @@ int64_t row_bytes_of(int wtype, int64_t k) {
 int mt_of(int64_t m) { return m <= 1 ? 1 : m <= 2 ? 2 : m <= 4 ? 4 : 8; }
 
 uint32_t act_bytes_of(int wtype, int mt, int64_t k) {
-    if (wtype == 0) return static_cast<uint32_t>(mt * (k + (k / 32) * 8));
+    if (wtype == 0) {
+        const int64_t groups = (k / 32 + 63) / 64;
+        return static_cast<uint32_t>(mt * groups * (2048 + 64 * 8));
+    }
     return static_cast<uint32_t>(mt * (k + (k / 256) * 4 + (k / 16) * 2));
 }
 
 uint32_t align_up_u32(uint32_t v, uint32_t a) { return (v + a - 1) / a * a; }
 
 // Fills the tiling / shared-memory plan; false if the shape does not fit.
-bool plan(int wtype, int64_t m, int64_t n, int64_t k, GemvParams &p, uint32_t &smem_bytes) {
+bool plan(int wtype, int64_t m, int count, const int64_t *ns, int64_t k, GemvParams &p, uint32_t &smem_bytes) {
+    if (count < 1 || count > kMaxGroup || k > 0x7fffffff / 8) return false;
+    for (int g = 0; g < count; ++g)
+        if (ns[g] < 1 || ns[g] > 0x7fffffff / 8) return false;
     const int mt = mt_of(m);
-    p.row_bytes = row_bytes_of(wtype, k);
-    p.rows_per_tile = p.row_bytes >= 1024 ? 4 : 8;
-    p.num_tiles = (n + p.rows_per_tile - 1) / p.rows_per_tile;
-    p.stage_bytes = align_up_u32(static_cast<uint32_t>(p.rows_per_tile * p.row_bytes) + 16 + kStageSlack, 128);
+    const int64_t rb = row_bytes_of(wtype, k);
+    p.row_bytes = static_cast<int>(rb);
+    p.rows_per_tile = rb >= 2048 ? 4 : 8;
+    p.pair_shift = p.rows_per_tile == 4 ? 1 : 2;
+    p.count = count;
+    int64_t tiles = 0;
+    for (int g = 0; g < count; ++g) {
+        p.ng[g] = static_cast<int>(ns[g]);
+        p.tile_base[g] = static_cast<int>(tiles);
+        tiles += (ns[g] + p.rows_per_tile - 1) / p.rows_per_tile;
+    }
+    for (int g = count; g <= kMaxGroup; ++g) p.tile_base[g] = static_cast<int>(tiles);
+    if (tiles > 0x7fffffff) return false;
+    p.num_tiles = static_cast<int>(tiles);
+    p.groups = static_cast<int>((k / 32 + 63) / 64);
+    p.stage_bytes = align_up_u32(static_cast<uint32_t>(p.rows_per_tile * rb) + 16 + kStageSlack, 128);
     p.grid_offset = kBarrierBytes;
-    p.act_offset = p.grid_offset + (wtype == 2 ? kGridTableBytes : 0);
+    p.act_offset = align_up_u32(p.grid_offset + (wtype == 2 ? kGridTableBytes : 0), 128);
     p.stage_offset = align_up_u32(p.act_offset + act_bytes_of(wtype, mt, k), 128);
-    const size_t budget = device_smem_optin() - 1024;  // static shared + reserve
-    if (p.stage_offset + 2 * static_cast<size_t>(p.stage_bytes) > budget) return false;
+    // at most half the SM's shared memory, so that the next launch's CTA can
+    // be resident beside this one (overlapped decode launches)
+    const size_t optin = device_smem_optin();
+    const size_t budget = (optin + 1024) / 2 - 2048;
+    if (p.stage_offset + 4 * static_cast<size_t>(p.stage_bytes) > budget) return false;
     const size_t fit = (budget - p.stage_offset) / p.stage_bytes;
-    p.stages = static_cast<int>(fit < kMaxStages ? fit : kMaxStages);
+    int stages = 4, shift = 2;
+    while (stages * 2 <= kMaxStages && static_cast<size_t>(stages * 2) <= fit) stages *= 2, ++shift;
+    p.stages = stages;
+    p.stage_shift = shift;
     smem_bytes = p.stage_offset + static_cast<uint32_t>(p.stages) * p.stage_bytes;
     return true;
 }
 
-template <int WT, int MT, bool kPartials, bool kF32>
+template <int WT, int MT, int RG, bool kPartials, bool kF32>
 cudaError_t launch_one(const GemvParams &p, uint32_t smem, cudaStream_t s) {
-    auto kernel = gemv_kernel<WT, MT, kPartials, kF32>;
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    const int64_t sms = device_sm_count();
-    const int grid = static_cast<int>(p.num_tiles < sms ? p.num_tiles : sms);
-    kernel<<<grid, kGemvThreads, smem, s>>>(p);
-    return cudaGetLastError();
+    auto kernel = gemv_kernel<WT, MT, RG, kPartials, kF32>;
+    static thread_local int configured_smem[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || configured_smem[dev] < static_cast<int>(smem)) {
+        cudaError_t e =
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < 64) configured_smem[dev] = static_cast<int>(smem);
+    }
+    const int sms = device_sm_count();
+    const int grid = p.num_tiles < sms ? p.num_tiles : sms;
+    if (!p.overlap) {
+        kernel<<<grid, kGemvThreads, smem, s>>>(p);
+        return cudaGetLastError();
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(kGemvThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
-template <int WT, int MT>
+template <int WT, int MT, int RG>
 cudaError_t dispatch_flags(const GemvParams &p, uint32_t smem, bool partials, bool f32, cudaStream_t s) {
-    if (partials) return f32 ? launch_one<WT, MT, true, true>(p, smem, s) : launch_one<WT, MT, true, false>(p, smem, s);
-    return f32 ? launch_one<WT, MT, false, true>(p, smem, s) : launch_one<WT, MT, false, false>(p, smem, s);
+    if (partials)
+        return f32 ? launch_one<WT, MT, RG, true, true>(p, smem, s) : launch_one<WT, MT, RG, true, false>(p, smem, s);
+    return f32 ? launch_one<WT, MT, RG, false, true>(p, smem, s) : launch_one<WT, MT, RG, false, false>(p, smem, s);
 }
 
 template <int WT>
 cudaError_t dispatch_mt(const GemvParams &p, uint32_t smem, bool partials, bool f32, cudaStream_t s) {
+    if constexpr (WT == 0) {
+        if (p.m == 1) {
+            if (p.groups <= 1) return dispatch_flags<WT, 1, 1>(p, smem, partials, f32, s);
+            if (p.groups <= 2) return dispatch_flags<WT, 1, 2>(p, smem, partials, f32, s);
+            if (p.groups <= kRegGroupsMax) return dispatch_flags<WT, 1, kRegGroupsMax>(p, smem, partials, f32, s);
+        }
+    }
     switch (mt_of(p.m)) {
-    case 1: return dispatch_flags<WT, 1>(p, smem, partials, f32, s);
-    case 2: return dispatch_flags<WT, 2>(p, smem, partials, f32, s);
-    case 4: return dispatch_flags<WT, 4>(p, smem, partials, f32, s);
-    default: return dispatch_flags<WT, 8>(p, smem, partials, f32, s);
+    case 1: return dispatch_flags<WT, 1, 0>(p, smem, partials, f32, s);
+    case 2: return dispatch_flags<WT, 2, 0>(p, smem, partials, f32, s);
+    case 4: return dispatch_flags<WT, 4, 0>(p, smem, partials, f32, s);
+    default: return dispatch_flags<WT, 8, 0>(p, smem, partials, f32, s);
     }
 }
 
 }  // namespace
 
-bool gemv_supported(int wtype, int64_t m, int64_t n, int64_t k, const void *w) {
-    if (m < 1 || m > 8 || n < 1) return false;
+bool gemv_supported(int wtype, int64_t m, int count, const int64_t *n, int64_t k, const void *const *w) {
+    if (m < 1 || m > 8 || count < 1 || count > kMaxGroup) return false;
+    if (wtype == 0 && (k / 32) % 2 != 0) return false;  // block pairs
     const int64_t rb = row_bytes_of(wtype, k);
-    if ((reinterpret_cast<uintptr_t>(w) & 15u) != 0 || (n * rb) % 16 != 0) return false;
+    for (int g = 0; g < count; ++g)
+        if (n[g] < 1 || (reinterpret_cast<uintptr_t>(w[g]) & 15u) != 0 || (n[g] * rb) % 16 != 0) return false;
     GemvParams p{};
     uint32_t smem = 0;
-    return plan(wtype, m, n, k, p, smem);
+    return plan(wtype, m, count, n, k, p, smem);
 }
 
 cudaError_t launch_gemv(const GemvArgs &args, cudaStream_t s) {
     GemvParams p{};
     uint32_t smem = 0;
-    if (!plan(args.wtype, args.m, args.n, args.k, p, smem)) return cudaErrorInvalidValue;
-    p.w = static_cast<const uint8_t *>(args.w);
+    if (!plan(args.wtype, args.m, args.count, args.n, args.k, p, smem)) return cudaErrorInvalidValue;
+    for (int g = 0; g < args.count; ++g) {
+        p.wg[g] = static_cast<const uint8_t *>(args.w[g]);
+        p.cg[g] = args.c[g];
+        p.ldcg[g] = args.ldc[g];
+    }
     p.a = static_cast<const uint8_t *>(args.a);
     p.x = args.x;
     p.ldx = args.ldx;
-    p.c = args.c;
-    p.ldc = args.ldc;
+    p.x_vec = args.x && (reinterpret_cast<uintptr_t>(args.x) & 15u) == 0 && (args.ldx & 3) == 0;
     p.partials = args.partials;
     p.err = args.err;
+    p.overlap = args.overlap ? 1 : 0;
     p.m = static_cast<int>(args.m);
-    p.n = args.n;
-    p.k = args.k;
+    p.n = static_cast<int>(args.n[0]);
+    p.k = static_cast<int>(args.k);
     const bool partials = args.partials != nullptr;
     const bool f32 = args.x != nullptr;
     switch (args.wtype) {

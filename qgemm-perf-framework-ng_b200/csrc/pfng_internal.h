@@ -40,20 +40,26 @@ cudaError_t launch_convert_q8_0_split(const void *a, const SplitA &out, int64_t 
 cudaError_t launch_convert_q8_K_split(const void *a, const SplitA &out, int64_t m, int64_t k, cudaStream_t s);
 
 // gemv.cu -- small-m kernels.  `x` (fp32) or `a` (raw q8 blocks) is given.
-// partials != nullptr selects the integer-partials output instead of C.
+// Up to kGemvMaxGroup weight matrices (same k) share the activations and run
+// in one launch.  partials != nullptr (count == 1 only) selects the
+// integer-partials output instead of C.
+constexpr int kGemvMaxGroup = 8;
 struct GemvArgs {
     int wtype;
-    const void *w;
+    int count;
+    const void *w[kGemvMaxGroup];
+    float *c[kGemvMaxGroup];
+    int64_t ldc[kGemvMaxGroup];
+    int64_t n[kGemvMaxGroup];
     const void *a;      // raw q8_0 / q8_K blocks, or nullptr
     const float *x;     // fp32 activations, or nullptr
     int64_t ldx;
-    float *c;
-    int64_t ldc;
     int32_t *partials;
     int *err;
-    int64_t m, n, k;
+    int64_t m, k;
+    bool overlap;       // programmatic dependent launch (weights not written by the previous kernel)
 };
-bool gemv_supported(int wtype, int64_t m, int64_t n, int64_t k, const void *w);
+bool gemv_supported(int wtype, int64_t m, int count, const int64_t *n, int64_t k, const void *const *w);
 cudaError_t launch_gemv(const GemvArgs &args, cudaStream_t s);
 
 // gemm.cu -- tensor-core GEMM on a split activation operand.

@@ -20,28 +20,54 @@ struct Q8_0Lane {
     int qsum;        // sum of the whole block's int8 values (all lanes)
 };
 
-PFNG_DEV Q8_0Lane q8_0_quantize_lane(const float v[4]) {
-    float amax = 0.0f;
+// N independent blocks per lane group, each step applied to all N before the
+// next so their dependency chains (shuffles, divisions) overlap.  Every block
+// sees exactly the arithmetic of the single-block form.
+template <int N>
+PFNG_DEV void q8_0_quantize_lanes(const float (&v)[N][4], Q8_0Lane (&r)[N]) {
+    float amax[N], scale[N], inv[N];
+    int s[N];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    for (int b = 0; b < N; ++b) {
+        amax[b] = 0.0f;
 #pragma unroll
-    for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float scale = __fdiv_rn(amax, 127.0f);
-    const float inv = scale != 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
-    Q8_0Lane r;
-    r.q = 0;
-    int s = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int qi = static_cast<int>(roundf(__fmul_rn(v[i], inv)));
-        s += qi;
-        r.q |= (static_cast<uint32_t>(qi) & 0xffu) << (8 * i);
+        for (int i = 0; i < 4; ++i) amax[b] = fmaxf(amax[b], fabsf(v[b][i]));
     }
 #pragma unroll
-    for (int o = 1; o < 8; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    r.qsum = s;
-    r.dbits = f32_to_f16_bits(scale);
-    return r;
+    for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+        for (int b = 0; b < N; ++b) amax[b] = fmaxf(amax[b], __shfl_xor_sync(0xffffffffu, amax[b], o));
+#pragma unroll
+    for (int b = 0; b < N; ++b) scale[b] = __fdiv_rn(amax[b], 127.0f);
+#pragma unroll
+    for (int b = 0; b < N; ++b) inv[b] = scale[b] != 0.0f ? __fdiv_rn(1.0f, scale[b]) : 0.0f;
+#pragma unroll
+    for (int b = 0; b < N; ++b) {
+        r[b].q = 0;
+        s[b] = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int qi = static_cast<int>(roundf(__fmul_rn(v[b][i], inv[b])));
+            s[b] += qi;
+            r[b].q |= (static_cast<uint32_t>(qi) & 0xffu) << (8 * i);
+        }
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1)
+#pragma unroll
+        for (int b = 0; b < N; ++b) s[b] += __shfl_xor_sync(0xffffffffu, s[b], o);
+#pragma unroll
+    for (int b = 0; b < N; ++b) {
+        r[b].qsum = s[b];
+        r[b].dbits = f32_to_f16_bits(scale[b]);
+    }
+}
+
+PFNG_DEV Q8_0Lane q8_0_quantize_lane(const float v[4]) {
+    float vv[1][4] = {{v[0], v[1], v[2], v[3]}};
+    Q8_0Lane r[1];
+    q8_0_quantize_lanes<1>(vv, r);
+    return r[0];
 }
 
 // q8_K: one warp per 256-value block, lane l holds values 8l..8l+7.

@@ -38,6 +38,7 @@ LAYOUT = {
 
 OK = 0
 ERR_KERNEL_TIMEOUT = -6
+OVERLAP_WEIGHTS = 1
 
 
 class PfngError(RuntimeError):
@@ -88,6 +89,9 @@ def _declare(L: ctypes.CDLL) -> None:
         f = getattr(L, f"pfng_b200_compute_{t}")
         f.restype = I
         f.argtypes = [P, P, I64, P, I64, I64, I64, I64, P, S, I, P]
+    L.pfng_b200_compute_grouped.restype = I
+    L.pfng_b200_compute_grouped.argtypes = [I, I, ctypes.POINTER(P), ctypes.POINTER(I64), ctypes.POINTER(P),
+                                            ctypes.POINTER(I64), P, I64, I64, I64, ctypes.c_uint, P]
     L.pfng_b200_shard_rows.restype = I
     L.pfng_b200_shard_rows.argtypes = [I64, I, I, I64, ctypes.POINTER(I64), ctypes.POINTER(I64)]
     L.pfng_b200_unshard_columns.restype = I
@@ -212,6 +216,40 @@ def compute(wtype, w, x, n: int, out=None, path="auto", workspace=None, stream=N
         _ptr(w), _ptr(x), x.stride(0), _ptr(out), m, n, k, out.stride(0), _ptr(ws), nbytes, p,
         _stream(stream)), f"compute_{name}")
     return out
+
+
+class GroupedCall:
+    """Pre-marshalled arguments of pfng_b200_compute_grouped (several weight
+    matrices sharing one activation), reusable across calls and graph capture."""
+
+    def __init__(self, wtype, weights, ns, outs, x, overlap_weights=False):
+        count = len(weights)
+        self.flags = OVERLAP_WEIGHTS if overlap_weights else 0
+        self.wtype = _wt(wtype)
+        self.count = count
+        self.w = (ctypes.c_void_p * count)(*[t.data_ptr() for t in weights])
+        self.n = (ctypes.c_int64 * count)(*ns)
+        self.c = (ctypes.c_void_p * count)(*[o.data_ptr() for o in outs])
+        self.ldc = (ctypes.c_int64 * count)(*[o.stride(0) for o in outs])
+        self.x = x
+        self.keep = (weights, outs)
+
+    def __call__(self, x=None, stream=None):
+        x = self.x if x is None else x
+        m, k = x.shape
+        _check(lib().pfng_b200_compute_grouped(self.wtype, self.count, self.w, self.n, self.c, self.ldc,
+                                               _ptr(x), x.stride(0), m, k, self.flags, _stream(stream)),
+               "compute_grouped")
+
+
+def compute_grouped(wtype, weights, x, ns, outs=None, overlap_weights=False, stream=None):
+    """C_g = quantize(x) . W_g^T for several weight matrices in one launch."""
+    import torch
+    m = x.shape[0]
+    if outs is None:
+        outs = [torch.empty((m, n), dtype=torch.float32, device=x.device) for n in ns]
+    GroupedCall(wtype, weights, ns, outs, x, overlap_weights)(stream=stream)
+    return outs
 
 
 def partials(wtype, w, a, m: int, n: int, k: int, path="auto", workspace=None, stream=None):

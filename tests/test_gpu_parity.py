@@ -259,3 +259,56 @@ def test_unshard_columns():
         slices[r, :, : e - b] = full[:, b:e]
     out = pb.unshard_columns(slices, m, n, world, granule)
     assert torch.equal(out, full)
+
+
+@pytest.mark.parametrize("wtype", list(TYPES))
+@pytest.mark.parametrize("m", [1, 3])
+def test_grouped_matches_single(oracle, wtype, m):
+    # several weight matrices sharing one activation, one launch; each output
+    # equals the single-matrix GEMV bit for bit and the oracle within tolerance
+    rng = np.random.default_rng(31 + m)
+    k = 1536 if wtype != "q4_0" else 1024
+    ns = [300, 64, 1000] if wtype != "iq2_xxs" else [304, 64, 1000]
+    ws = [make_weights(oracle, wtype, n, k, rng) for n in ns]
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    wds = [dev_bytes(w) for w in ws]
+    xd = dev(x)
+    outs = pb.compute_grouped(wtype, wds, xd, ns)
+    a = oracle.quantize(act_kind(wtype), x)
+    for w, wd, n, o in zip(ws, wds, ns, outs):
+        single = host(pb.compute(wtype, wd, xd, n, path="gemv"))
+        got = host(o)
+        np.testing.assert_array_equal(got.view(np.uint32), single.view(np.uint32))
+        check_close(got, oracle.mm(wtype, w, a, m, n, k), oracle.bound(wtype, w, a, m, n, k), f"grouped {wtype}")
+
+
+def test_grouped_rejects_large_m():
+    w = torch.zeros(18 * 64 * 8, dtype=torch.uint8, device="cuda")
+    x = torch.zeros((9, 256), device="cuda")
+    with pytest.raises(pb.PfngError) as e:
+        pb.compute_grouped("q4_0", [w], x, [64])
+    assert e.value.status == -7
+
+
+def test_grouped_overlap_keeps_order(oracle):
+    # back-to-back launches with PFNG_B200_OVERLAP_WEIGHTS: each may start
+    # streaming its weights early, but reads its activations and writes its
+    # outputs after the preceding kernel -- here the activations of each call
+    # are produced by the kernel just before it.
+    rng = np.random.default_rng(44)
+    k, ns = 4096, [4096, 1000]
+    sets = [[make_weights(oracle, "q4_0", n, k, rng) for n in ns] for _ in range(3)]
+    dsets = [[dev_bytes(w) for w in s] for s in sets]
+    x0 = dev(rng.standard_normal((1, k)).astype(np.float32))
+    outs = [torch.empty((1, n), device="cuda") for n in ns]
+    expected = None
+    xs = []
+    x = x0
+    for r in range(3):
+        x = x * 1.5 + 0.25  # produced by a torch kernel right before the call
+        xs.append(x)
+        pb.compute_grouped("q4_0", dsets[r], x, ns, outs=outs, overlap_weights=True)
+    got = [host(o) for o in outs]
+    for g, n in enumerate(ns):
+        single = host(pb.compute("q4_0", dsets[2][g], xs[2], n, path="gemv"))
+        np.testing.assert_array_equal(got[g].view(np.uint32), single.view(np.uint32))
