@@ -160,6 +160,31 @@ int pfng_b200_shard_rows(int64_t n, int world, int rank, int64_t granule, int64_
 int pfng_b200_unshard_columns(const float *slices, float *c, int64_t m, int64_t n, int64_t ldc, int world,
                               int64_t granule, int64_t slice_width, void *stream);
 
+/* ---- matmul without any allocation ----------------------------------------
+ * pfng_b200_compute_q4_0 on the tensor-core path (fp32 activations x [m][ldx]
+ * quantized to q8_0, then C = A . W^T), for callers that must not allocate
+ * device memory on this call path -- e.g. a server whose memory pool owns the
+ * whole GPU from start-up, or a loop that cannot take the device-wide
+ * synchronisation of cudaMalloc / cudaFree.  It takes no workspace: its
+ * scratch (the quantized activations) is a fixed array of
+ * PFNG_B200_NOALLOC_SCRATCH_BYTES inside the library, held by every GPU that
+ * loads the library until the process exits.
+ *   - Problems whose scratch would exceed that size (about m * k * 1.25
+ *     bytes, m rounded up to 128; e.g. m <= 2048 at k = 4096) return
+ *     PFNG_B200_ERR_WORKSPACE; k must be a multiple of 256 and w 16-byte
+ *     aligned (else PFNG_B200_ERR_UNSUPPORTED).
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *   - All calls on a device share the array, which keeps the last call's
+ *     contents; each call rewrites everything it reads, but calls whose
+ *     kernels overlap on the GPU (other streams, other host threads) race on
+ *     it and must be ordered by the caller.
+ * No counterpart in the reference; results equal pfng_b200_compute_q4_0 with
+ * PFNG_B200_PATH_MMA. */
+#define PFNG_B200_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+int pfng_b200_compute_q4_0_noalloc(const void *w, const float *x, int64_t ldx, float *c, int64_t m, int64_t n,
+                                   int64_t k, int64_t ldc, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
