@@ -360,6 +360,179 @@ def ours(args) -> int:
     return 0
 
 
+
+# ------------------------------------------------------- other BASELINE configs
+def make_weights_device(pb, torch, wtype: str, n: int, k: int, gen, std: float = 1.0):
+    """Seeded synthetic weights on the device in the ggml layout of `wtype`."""
+    if wtype == "q4_0":
+        return pb.quantize_q4_0(torch.randn((n, k), generator=gen, device="cuda") * std)
+    if wtype == "q4_K":
+        return pb.quantize_q4_K(torch.randn((n, k), generator=gen, device="cuda") * std)
+    nb = n * (k // 256)  # iq2_xxs: random grid indices / signs / scales, d ~ U[1e-3, 1e-2]
+    blocks = torch.randint(0, 256, (nb, 66), generator=gen, device="cuda", dtype=torch.int32).to(torch.uint8)
+    d = torch.empty(nb, device="cuda").uniform_(1e-3, 1e-2, generator=gen).half()
+    blocks[:, :2] = d.view(torch.uint8).view(nb, 2)
+    return blocks.reshape(-1).contiguous()
+
+
+def weight_bytes(wtype: str, n: int, k: int) -> int:
+    return n * (k // 32 * 18 if wtype == "q4_0" else k // 256 * (144 if wtype == "q4_K" else 66))
+
+
+def int8_peak_tops():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return 2.0 * float(json.loads(path.read_text())["bf16_tflops"]), "2x measured bf16 GEMM (MEASURED_PEAKS.json)"
+    return 2.0 * 1590.0, "2x fallback bf16 1.59 PFLOP/s"
+
+
+def time_graph(torch, stream, fn, steps: int, warmup: int) -> float:
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(steps):
+            fn(i)
+    graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    graph.replay()
+    b.record(stream)
+    torch.cuda.synchronize()
+    del graph
+    return a.elapsed_time(b) / 1e3
+
+
+def prefill(args) -> int:
+    """configs[0] / [2] / [3]: one C = quantize(x) . W^T, M=480 N=1536 K=1536, on one GPU."""
+    import torch
+    import pfng_b200 as pb
+    torch.cuda.set_device(0)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    m, n, k = args.m, args.n, args.k
+    gen = torch.Generator(device="cuda").manual_seed(1)
+    per = weight_bytes(args.wtype, n, k) + m * k * 4
+    copies = max(2, -(-4 * L2_BYTES // per))
+    ws_ = [make_weights_device(pb, torch, args.wtype, n, k, gen) for _ in range(copies)]
+    xs = [torch.randn((m, k), generator=gen, device="cuda") for _ in range(copies)]
+    out = torch.empty((m, n), device="cuda")
+    wsp = torch.empty(max(1, pb.compute_workspace_size(args.wtype, m, n, k)), dtype=torch.uint8, device="cuda")
+    step = lambda i: pb.compute(args.wtype, ws_[i % copies], xs[i % copies], n, out=out, workspace=wsp,
+                                stream=stream)
+    with ClockSampler(torch.cuda.current_device()) as clocks:
+        elapsed = time_graph(torch, stream, step, args.steps, args.warmup)
+    pb.check_kernel_error()
+    ops = 2.0 * m * n * k
+    peak, peak_src = int8_peak_tops()
+    achieved = ops / (elapsed / args.steps) / 1e12
+    print(json.dumps({
+        "metric": METRIC, "workload": f"{args.wtype} GEMM M={m} N={n} K={k} (quantize x + matmul, one step)",
+        "value": args.steps * ops / elapsed / 1e9, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "us_per_step": elapsed / args.steps * 1e6,
+        "weight_GBps": args.steps * weight_bytes(args.wtype, n, k) / elapsed / 1e9,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s",
+                     "frac": achieved / peak, "peak_source": peak_src},
+        "clocks": clocks.summary(), "l2": f"{copies} rotating (W, x) copies > 4x L2",
+    }), flush=True)
+    return 0
+
+
+LLAMA_SHAPES = [(nn, kk) for nn, kk in ((4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096))]
+
+
+def llama(args) -> int:
+    """Llama-2-7B q4_0 prefill shapes, weight rows sharded over the ranks, x broadcast from
+    rank 0 and the output column slices all-gathered with NCCL.  One JSON line per shape."""
+    import torch
+    import pfng_b200 as pb
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    granule = 128
+    ms = [args.m] if args.m_given else [32, 512, 2048]
+    for m in ms:
+        for n, k in LLAMA_SHAPES:
+            b, e = pb.shard_rows(n, world, rank, granule)
+            width = max(pb.shard_rows(n, world, r, granule)[1] - pb.shard_rows(n, world, r, granule)[0]
+                        for r in range(world))
+            gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
+            per = weight_bytes("q4_0", max(e - b, 1), k) + m * k * 4
+            copies = max(2, -(-4 * L2_BYTES // per))
+            wsh = [make_weights_device(pb, torch, "q4_0", max(e - b, 1), k, gen, 0.02) for _ in range(copies)]
+            x = torch.randn((m, k), generator=torch.Generator(device="cuda").manual_seed(7), device="cuda")
+            slice_ = torch.zeros((m, width), device="cuda")
+            gathered = torch.empty((world, m, width), device="cuda")
+            full = torch.empty((m, n), device="cuda")
+            wsp = torch.empty(max(1, pb.compute_workspace_size("q4_0", m, width, k)), dtype=torch.uint8,
+                              device="cuda")
+
+            def local_gemm(i):
+                if e > b:
+                    pb.compute("q4_0", wsh[i % copies], x, e - b, out=slice_[:, : e - b], workspace=wsp,
+                               stream=stream)
+
+            def full_step(i):
+                if dist is not None:
+                    dist.broadcast(x, src=0)
+                local_gemm(i)
+                if dist is not None:
+                    dist.all_gather_into_tensor(gathered, slice_)
+                    pb.unshard_columns(gathered, m, n, world, granule, out=full, stream=stream)
+                else:
+                    full.copy_(slice_[:, :n])
+
+            def timed(fn):
+                for i in range(args.warmup):
+                    fn(i)
+                torch.cuda.synchronize()
+                if dist is not None:
+                    dist.barrier()
+                a, bb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                for i in range(args.steps):
+                    fn(i)
+                bb.record(stream)
+                torch.cuda.synchronize()
+                t = a.elapsed_time(bb) / 1e3
+                if dist is not None:
+                    tt = torch.tensor([t], device="cuda", dtype=torch.float64)
+                    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+                    t = float(tt.item())
+                return t
+
+            t_compute = timed(local_gemm)
+            t_e2e = timed(full_step)
+            pb.check_kernel_error()
+            if rank == 0:
+                ops = 2.0 * m * n * k
+                peak, peak_src = int8_peak_tops()
+                print(json.dumps({
+                    "metric": METRIC, "workload": f"configs[4] Llama-2-7B q4_0 M={m} N={n} K={k}",
+                    "n_gpus": world, "scaling": "strong", "value": args.steps * ops / t_e2e / 1e9, "unit": UNIT,
+                    "compute_only": args.steps * ops / t_compute / 1e9, "us_per_step_e2e": t_e2e / args.steps * 1e6,
+                    "us_per_step_compute": t_compute / args.steps * 1e6,
+                    "compute_frac_of_int8_peak": ops / (t_compute / args.steps) / 1e12 / peak,
+                    "peak_source": peak_src, "rows_per_rank": e - b,
+                    "exchange": "NCCL broadcast of x, all-gather of C column slices, device unshard"
+                    if world > 1 else "none",
+                }), flush=True)
+            del wsh, gathered, full, slice_
+            torch.cuda.empty_cache()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -367,11 +540,24 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the timed CPU baseline leg")
+    ap.add_argument("--workload", choices=["decode", "prefill", "llama"], default="decode",
+                    help="decode: configs[1] (the bench line); prefill: configs[0]/[2]/[3]; llama: configs[4]")
+    ap.add_argument("--wtype", choices=["q4_0", "q4_K", "iq2_xxs"], default="q4_0")
+    ap.add_argument("--m", type=int, default=None)
+    ap.add_argument("--n", type=int, default=1536)
+    ap.add_argument("--k", type=int, default=1536)
     args = ap.parse_args()
+    args.m_given = args.m is not None
+    if args.m is None:
+        args.m = 480
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     if args.impl == "reference":
         return reference_arm(args)
+    if args.workload == "prefill":
+        return prefill(args)
+    if args.workload == "llama":
+        return llama(args)
     return ours(args)
 
 

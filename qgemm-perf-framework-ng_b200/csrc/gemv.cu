@@ -5,22 +5,26 @@
 // bench/llama_reference/llama_reference.cpp:165-205 (dot products :113-161).
 //
 // Structure (one persistent CTA per SM, warp-specialised):
-//   * a producer warp streams tiles of R consecutive weight rows -- one
-//     contiguous byte range of W -- into a ring of S shared-memory stages with
-//     bulk TMA copies (cp.async.bulk, mbarrier transaction counts, L2
-//     evict-first since every weight byte is read once);
-//   * 8 consumer warps first stage the activation rows in shared memory
+//   * a producer warp streams the CTA's share of the weights -- one
+//     contiguous range of rows, the same number of rows for every CTA -- in
+//     tiles of up to R rows (one contiguous byte range of W each) into a ring
+//     of S shared-memory stages with bulk TMA copies (cp.async.bulk, mbarrier
+//     transaction counts, L2 evict-first since every weight byte is read
+//     once);
+//   * the consumer warps first stage the activation rows in shared memory
 //     (either the caller's q8 blocks, or fp32 rows quantized in place with
-//     the same code as the standalone quantizer), then each repeatedly claims
-//     the next PAIR of rows of the CTA's tile sequence (a shared counter, so
-//     warps that finish early take more work; a tile's stage is released
-//     once all its pairs are done) and processes it: lanes walk the rows'
-//     blocks, unpack 4-bit / grid weights to int8, dot them against the
-//     activations with dp4a, fold the integer partials with the block scales
-//     in fp32 and reduce across the warp.  The two q4_0 rows of a pair are
-//     interleaved, which doubles the independent work in flight per warp.
-//   Tiles stay >= ~9 KB: bulk copies much smaller than that do not reach
-//   full HBM bandwidth with one CTA per SM.
+//     the same rounding as the standalone quantizer), then each repeatedly
+//     claims the next PAIR of rows of the CTA's tile sequence (a shared
+//     counter, so warps that finish early take more work) and processes it:
+//     lanes walk the rows' blocks, unpack 4-bit / grid weights to int8, dot
+//     them against the activations with dp4a, fold the integer partials with
+//     the block scales in fp32 and reduce across the warp.  For q4_0 at
+//     m = 1 a warp copies its pair's weights to registers and releases the
+//     pair before computing, so stages return to the producer early.
+//   Measured on B200 (decode step of two matrices, 35 MB): 14 consumer warps
+//   with 8-row (18 KB) tiles and one CTA per SM stream fastest; fewer warps
+//   leave the consumers latency-bound, more add staging and scheduling cost,
+//   and 4-row tiles double the producer's per-tile work.
 //
 // q4_0 lane mapping: lane l of a warp takes the block PAIR (2l, 2l+1) of each
 // group of 64 blocks.  A pair is 36 contiguous bytes = 9 aligned words at word
@@ -40,11 +44,23 @@
 namespace pfng {
 namespace {
 
-constexpr int kConsumerWarps = 8;
+#ifndef PFNG_GEMV_CONSUMER_WARPS
+#define PFNG_GEMV_CONSUMER_WARPS 14
+#endif
+#ifndef PFNG_GEMV_CTAS_PER_SM
+#define PFNG_GEMV_CTAS_PER_SM 1
+#endif
+constexpr int kConsumerWarps = PFNG_GEMV_CONSUMER_WARPS;
+constexpr int kCtasPerSm = PFNG_GEMV_CTAS_PER_SM;  // 2: half the shared memory, so two launches can overlap
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kGemvThreads = kConsumerThreads + 32;
-constexpr int kMaxStages = 32;       // a power of two
+constexpr int kMaxStages = 32;
 constexpr int kPairRows = 2;         // rows a warp claims at a time
+#ifndef PFNG_GEMV_TILE_ROWS
+#define PFNG_GEMV_TILE_ROWS 8
+#endif
+constexpr int kTileRowsLong = PFNG_GEMV_TILE_ROWS;  // rows per tile when a row is >= 2 KB
+static_assert(kTileRowsLong >= kPairRows && (kTileRowsLong & (kTileRowsLong - 1)) == 0, "tile rows");
 constexpr int kMaxGroup = kGemvMaxGroup;
 constexpr uint32_t kBarrierBytes = 2 * kMaxStages * 8;
 constexpr uint32_t kGridTableBytes = 256 * 8;
@@ -60,23 +76,23 @@ struct GemvParams {
     int m, n, k;       // n: rows of matrix 0 (partials indexing)
     int x_vec;         // fp32 rows are 16-byte aligned with ldx % 4 == 0
     int row_bytes;
-    int rows_per_tile;  // 4 or 8 (a multiple of kPairRows)
+    int rows_per_tile;  // kPairRows times a power of two
     int pair_shift;     // log2(rows_per_tile / kPairRows)
-    int num_tiles;
-    int stages;        // a power of two
-    int stage_shift;   // log2(stages)
+    int num_tiles;      // ceil(total_rows / rows_per_tile): CTAs beyond it would be idle
+    int stages;        // ring depth (any count up to kMaxStages)
     uint32_t stage_bytes;
     uint32_t grid_offset, act_offset, stage_offset;
     int groups;        // q4_0: ceil(nb / 64)
     int overlap;       // launched as a programmatic dependent (see kernel)
     // weight matrices sharing the activations (count >= 1); tiles of matrix
-    // g are [tile_base[g], tile_base[g + 1]) of the launch's tile sequence
+    // g are rows [row_base[g], row_base[g + 1]) of the launch's row sequence
     int count;
     const uint8_t *wg[kMaxGroup];
     float *cg[kMaxGroup];
     int64_t ldcg[kMaxGroup];
     int ng[kMaxGroup];
-    int tile_base[kMaxGroup + 1];
+    int row_base[kMaxGroup + 1];
+    int total_rows;
 };
 
 // Output of one weight matrix.
@@ -129,67 +145,85 @@ PFNG_DEV void stage_act_q8_0(const GemvParams &p, uint8_t *smem, int tid) {
     uint8_t *qs = smem + p.act_offset;
     float *d = reinterpret_cast<float *>(qs + MT * p.groups * 2048);
     int32_t *s8 = reinterpret_cast<int32_t *>(d + MT * nbp);
-    const int total = MT * nbp;  // a multiple of 64: every warp iteration covers 4 live blocks
-    const int lane = tid & 31, warp = tid >> 5, g = lane & 7;
-    constexpr int kBatch = 4;    // iterations whose loads are issued together
-    for (int wb0 = warp * 4; wb0 < total; wb0 += kBatch * kConsumerWarps * 4) {
-        // 1) issue the loads of kBatch iterations (one memory round trip)
-        uint32_t raw_q[kBatch], raw_d[kBatch];
-        float v[kBatch][4];
+    const int total = MT * nbp;  // a multiple of 64
+    const int lane = tid & 31, warp = tid >> 5;
+    if constexpr (kF32) {
+        // 4 lanes per block (8 values each), 8 blocks per warp and item
+        const int c = lane & 3;
+        constexpr int kBatch = 2;  // items whose loads are issued together
+        for (int wb0 = warp * 8; wb0 < total; wb0 += kBatch * kConsumerWarps * 8) {
+            float v[kBatch][8];
 #pragma unroll
-        for (int it = 0; it < kBatch; ++it) {
-            const int wb = wb0 + it * kConsumerWarps * 4;
-            const int bi = wb + (lane >> 3);
-            const int row = bi / nbp, j = bi % nbp;
-            const bool valid = wb < total && row < p.m && j < nb;
-            v[it][0] = v[it][1] = v[it][2] = v[it][3] = 0.0f;
-            raw_q[it] = raw_d[it] = 0;
-            if (valid) {
-                if constexpr (kF32) {
-                    const float *src = p.x + row * p.ldx + j * 32 + 4 * g;
+            for (int it = 0; it < kBatch; ++it) {
+                const int bi = wb0 + it * kConsumerWarps * 8 + (lane >> 2);
+                const int row = bi / nbp, j = bi % nbp;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[it][i] = 0.0f;
+                if (bi < total && row < p.m && j < nb) {
+                    const float *src = p.x + row * p.ldx + j * 32 + 8 * c;
                     if (p.x_vec) {
-                        const float4 t = __ldg(reinterpret_cast<const float4 *>(src));
-                        v[it][0] = t.x, v[it][1] = t.y, v[it][2] = t.z, v[it][3] = t.w;
+                        const float4 t0 = __ldg(reinterpret_cast<const float4 *>(src));
+                        const float4 t1 = __ldg(reinterpret_cast<const float4 *>(src + 4));
+                        v[it][0] = t0.x, v[it][1] = t0.y, v[it][2] = t0.z, v[it][3] = t0.w;
+                        v[it][4] = t1.x, v[it][5] = t1.y, v[it][6] = t1.z, v[it][7] = t1.w;
                     } else {
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) v[it][i] = __ldg(src + i);
+                        for (int i = 0; i < 8; ++i) v[it][i] = __ldg(src + i);
                     }
-                } else {
+                }
+            }
+            Q8_0Quad qr[kBatch];
+            q8_0_quantize_quads<kBatch>(v, qr);
+#pragma unroll
+            for (int it = 0; it < kBatch; ++it) {
+                const int wb = wb0 + it * kConsumerWarps * 8;
+                if (wb >= total) break;
+                const int bi = wb + (lane >> 2);
+                const int row = bi / nbp, j = bi % nbp;
+                const bool valid = row < p.m && j < nb;
+                *reinterpret_cast<uint2 *>(qs + q4_0_act_qs_offset(row, p.groups, j, 8 * c)) =
+                    valid ? make_uint2(qr[it].q0, qr[it].q1) : make_uint2(0u, 0u);
+                if (c == 0) {
+                    d[row * nbp + j] = valid ? f16_bits_to_f32(qr[it].dbits) : 0.0f;
+                    s8[row * nbp + j] = valid ? 8 * qr[it].qsum : 0;
+                }
+            }
+        }
+    } else {
+        // caller's q8_0 blocks: 8 lanes per block (4 bytes each)
+        const int g = lane & 7;
+        constexpr int kBatch = 4;
+        for (int wb0 = warp * 4; wb0 < total; wb0 += kBatch * kConsumerWarps * 4) {
+            uint32_t raw_q[kBatch], raw_d[kBatch];
+#pragma unroll
+            for (int it = 0; it < kBatch; ++it) {
+                const int wb = wb0 + it * kConsumerWarps * 4;
+                const int bi = wb + (lane >> 3);
+                const int row = bi / nbp, j = bi % nbp;
+                raw_q[it] = raw_d[it] = 0;
+                if (wb < total && row < p.m && j < nb) {
                     const uint8_t *blk = p.a + (static_cast<int64_t>(row) * nb + j) * kQ8_0Bytes;
                     const uint16_t *h = reinterpret_cast<const uint16_t *>(blk + 2 + 4 * g);
                     raw_q[it] = static_cast<uint32_t>(__ldg(h)) | (static_cast<uint32_t>(__ldg(h + 1)) << 16);
                     raw_d[it] = __ldg(reinterpret_cast<const uint16_t *>(blk));
                 }
             }
-        }
-        // 2) quantize (the batch's chains interleaved) / reduce, and store
-        Q8_0Lane qr[kBatch];
-        if constexpr (kF32) q8_0_quantize_lanes<kBatch>(v, qr);
 #pragma unroll
-        for (int it = 0; it < kBatch; ++it) {
-            const int wb = wb0 + it * kConsumerWarps * 4;
-            if (wb >= total) break;
-            const int bi = wb + (lane >> 3);
-            const int row = bi / nbp, j = bi % nbp;
-            const bool valid = row < p.m && j < nb;
-            uint32_t q, dbits;
-            int qsum;
-            if constexpr (kF32) {
-                q = qr[it].q;
-                dbits = qr[it].dbits;
-                qsum = qr[it].qsum;
-            } else {
-                q = raw_q[it];
-                dbits = raw_d[it];
+            for (int it = 0; it < kBatch; ++it) {
+                const int wb = wb0 + it * kConsumerWarps * 4;
+                if (wb >= total) break;
+                const int bi = wb + (lane >> 3);
+                const int row = bi / nbp, j = bi % nbp;
+                const bool valid = row < p.m && j < nb;
+                const uint32_t q = raw_q[it];
                 int sm = __dp4a(static_cast<int>(q), 0x01010101, 0);
 #pragma unroll
                 for (int o = 1; o < 8; o <<= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
-                qsum = sm;
-            }
-            *reinterpret_cast<uint32_t *>(qs + q4_0_act_qs_offset(row, p.groups, j, 4 * g)) = valid ? q : 0u;
-            if (g == 0) {
-                d[row * nbp + j] = valid ? f16_bits_to_f32(dbits) : 0.0f;
-                s8[row * nbp + j] = valid ? 8 * qsum : 0;
+                *reinterpret_cast<uint32_t *>(qs + q4_0_act_qs_offset(row, p.groups, j, 4 * g)) = valid ? q : 0u;
+                if (g == 0) {
+                    d[row * nbp + j] = valid ? f16_bits_to_f32(raw_d[it]) : 0.0f;
+                    s8[row * nbp + j] = valid ? 8 * sm : 0;
+                }
             }
         }
     }
@@ -310,18 +344,37 @@ PFNG_DEV PairW load_pair(const uint8_t *tile, uint32_t off) {
 
 // m = 1, activations in registers (groups <= GM).  Rows row0 and row0 + 1
 // (the second only if nrows == 2) start at row_off and row_off + row_bytes.
-template <int GM, bool kPartials>
-PFNG_DEV void rows_q4_0_reg(const GemvParams &p, const Out &o, const ActRegs<GM> &ar, const uint8_t *tile,
-                            uint32_t row_off, int row0, int nrows, int lane) {
+// The weights are first copied to registers (load_rows_q4_0) so that the
+// stage can be handed back to the producer before the arithmetic.
+template <int GM>
+struct RowsW {
+    PairW w[GM][2];
+};
+
+template <int GM>
+PFNG_DEV void load_rows_q4_0(const GemvParams &p, const uint8_t *tile, uint32_t row_off, int nrows, int lane,
+                             RowsW<GM> &rw) {
     const int nb = p.k / 32;
     const uint32_t off1 = row_off + static_cast<uint32_t>(nrows > 1 ? p.row_bytes : 0);
-    float acc0 = 0.0f, acc1 = 0.0f;
 #pragma unroll
     for (int t = 0; t < GM; ++t) {
         if (t < p.groups && 64 * t + 2 * lane < nb) {
             const uint32_t o = 1152u * t + 36u * lane;
-            const PairW w0 = load_pair(tile, row_off + o);
-            const PairW w1 = load_pair(tile, off1 + o);
+            rw.w[t][0] = load_pair(tile, row_off + o);
+            rw.w[t][1] = load_pair(tile, off1 + o);
+        }
+    }
+}
+
+template <int GM, bool kPartials>
+PFNG_DEV void rows_q4_0_reg(const GemvParams &p, const Out &o, const ActRegs<GM> &ar, const RowsW<GM> &rw, int row0,
+                            int nrows, int lane) {
+    const int nb = p.k / 32;
+    float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll
+    for (int t = 0; t < GM; ++t) {
+        if (t < p.groups && 64 * t + 2 * lane < nb) {
+            const PairW &w0 = rw.w[t][0], &w1 = rw.w[t][1];
             const int ia0 = nibble_dot(w0.qa, ar.q[t][0], ar.q[t][1]) - ar.s8[t].x;
             const int ia1 = nibble_dot(w1.qa, ar.q[t][0], ar.q[t][1]) - ar.s8[t].x;
             const int ib0 = nibble_dot(w0.qb, ar.q[t][2], ar.q[t][3]) - ar.s8[t].y;
@@ -344,15 +397,14 @@ PFNG_DEV void rows_q4_0_reg(const GemvParams &p, const Out &o, const ActRegs<GM>
         }
     }
     if constexpr (!kPartials) {
+        // two rows in one butterfly: the first exchange leaves row 0's sums
+        // in lanes 0..15 and row 1's in lanes 16..31
+        const bool upper = (lane & 16) != 0;
+        float v = (upper ? acc1 : acc0) + __shfl_xor_sync(0xffffffffu, upper ? acc0 : acc1, 16);
 #pragma unroll
-        for (int sh = 16; sh > 0; sh >>= 1) {
-            acc0 += __shfl_xor_sync(0xffffffffu, acc0, sh);
-            acc1 += __shfl_xor_sync(0xffffffffu, acc1, sh);
-        }
-        if (lane == 0) {
-            o.c[row0] = acc0;
-            if (nrows > 1) o.c[row0 + 1] = acc1;
-        }
+        for (int sh = 8; sh > 0; sh >>= 1) v += __shfl_xor_sync(0xffffffffu, v, sh);
+        if (lane == 0) o.c[row0] = v;
+        if (lane == 16 && nrows > 1) o.c[row0 + 1] = v;
     }
 }
 
@@ -542,27 +594,47 @@ PFNG_DEV void row_iq2_xxs(const GemvParams &p, const Out &o, const uint8_t *act,
     if constexpr (!kPartials) warp_reduce_store<MT>(p, o, acc, row, lane);
 }
 
+// Waits until the producer has issued local tile i: 1 once it has, 0 if the
+// producer finished with fewer tiles, -1 (error recorded) if it never does.
+PFNG_DEV int wait_issued(const int *issued_count, const int *final_count, int i, int *err) {
+    const volatile int *ic = issued_count;
+    const volatile int *fc = final_count;
+    for (uint32_t n = 0; n < kWaitAttempts; ++n) {
+        if (*ic > i) return 1;
+        if (*fc >= 0) {
+            __threadfence_block();  // final_count before issued_count
+            return *ic > i ? 1 : 0;
+        }
+        __nanosleep(64);
+    }
+    report_error(err, kErrWaitIssue);
+    return -1;
+}
+
 // --------------------------------------------------------------------------
 // the kernel
 // --------------------------------------------------------------------------
 // RG > 0: q4_0 with m = 1 and the activations held in registers (RG groups).
 template <int WT, int MT, int RG, bool kPartials, bool kF32>
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t *full = reinterpret_cast<uint64_t *>(smem);
     uint64_t *empty = full + kMaxStages;
     __shared__ int abort_flag;
     __shared__ int next_tile;
+    __shared__ int stage_tile[kMaxStages];  // first row (launch row sequence) of each stage's tile
+    __shared__ int stage_rows[kMaxStages];  // and its number of rows
+    // Local tiles issued so far and, once the launch's tiles are all claimed,
+    // their final number.  A consumer waits on a stage's mbarrier only after
+    // its tile has been issued: the producer issues local tile i only after
+    // tile i - S left the stage, so the barrier is then in tile i's phase (a
+    // parity wait can only name the current or the previous phase).
+    __shared__ int issued_count;
+    __shared__ int final_count;
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
     const int S = p.stages;
 
-    // Programmatic dependent launch: let the next launch on the stream start
-    // as soon as this grid's CTAs are resident (it needs the other half of
-    // the SM's shared memory).  Only the weight stream runs before
-    // griddepcontrol.wait below; activations and outputs are ordered after
-    // the preceding grid as usual.
-    if (p.overlap) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (tid < S) {
         mbar_init(&full[tid], 1);
         mbar_init(&empty[tid], p.rows_per_tile / kPairRows);  // one arrival per row pair
@@ -571,41 +643,59 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     if (tid == 0) {
         abort_flag = 0;
         next_tile = 0;
+        issued_count = 0;
+        final_count = -1;
     }
     __syncthreads();
 
     if (warp == kConsumerWarps) {
-        // ---------------- producer: tiles blockIdx.x + i * gridDim.x, in order ----------------
+        // ---------------- producer ----------------
+        // The CTA streams one contiguous range of the launch's rows (all CTAs
+        // get the same number of rows, +-1), in tiles of up to rows_per_tile
+        // rows that do not cross a matrix boundary.  issued_count publishes
+        // how many tiles have been issued, final_count how many there are
+        // once the last one is.
         if (lane == 0) {
             const uint64_t policy = l2_policy_evict_first();
             int issued = 0, stage = 0;
             uint32_t phase = 0;
-            int g = 0;  // matrix of the current tile (tiles only increase)
-            for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
-                if (issued >= S && !mbar_wait(&empty[stage], phase ^ 1u, p.err, kErrWaitEmpty)) {
-                    abort_flag = 1;
+            int g = 0;  // matrix of the current tile (rows only increase)
+            bool ok = true;
+            const int r_begin = static_cast<int>(static_cast<int64_t>(p.total_rows) * blockIdx.x / gridDim.x);
+            const int r_end = static_cast<int>(static_cast<int64_t>(p.total_rows) * (blockIdx.x + 1) / gridDim.x);
+            for (int r = r_begin; r < r_end;) {
+                if ((issued >= S && !mbar_wait(&empty[stage], phase ^ 1u, p.err, kErrWaitEmpty)) ||
+                    *reinterpret_cast<volatile int *>(&abort_flag)) {
+                    ok = false;
                     break;
                 }
-                if (*reinterpret_cast<volatile int *>(&abort_flag)) break;
-                while (tile >= p.tile_base[g + 1]) ++g;
-                const int lt = tile - p.tile_base[g];
-                const int ng = p.ng[g];
-                const int64_t start = static_cast<int64_t>(lt) * p.rows_per_tile * p.row_bytes;
-                const int last = (lt + 1) * p.rows_per_tile < ng ? (lt + 1) * p.rows_per_tile : ng;
-                const int64_t end = static_cast<int64_t>(last) * p.row_bytes;
+                while (r >= p.row_base[g + 1]) ++g;
+                int rows = p.rows_per_tile;
+                if (rows > r_end - r) rows = r_end - r;
+                if (rows > p.row_base[g + 1] - r) rows = p.row_base[g + 1] - r;
+                const int lr = r - p.row_base[g];
+                const int64_t start = static_cast<int64_t>(lr) * p.row_bytes;
+                const int64_t end = static_cast<int64_t>(lr + rows) * p.row_bytes;
                 const int64_t ws = start & ~int64_t(15), we = (end + 15) & ~int64_t(15);
                 const uint32_t bytes = static_cast<uint32_t>(we - ws);
                 const uint8_t *src = p.wg[g] + ws;
                 uint8_t *dst = smem + p.stage_offset + static_cast<uint32_t>(stage) * p.stage_bytes;
+                stage_tile[stage] = r;
+                stage_rows[stage] = rows;
+                r += rows;
                 mbar_arrive_expect_tx(&full[stage], bytes);
                 bulk_copy_g2s(dst, src, bytes, &full[stage], policy);
-                ++issued;
+                *reinterpret_cast<volatile int *>(&issued_count) = ++issued;
                 if (++stage == S) stage = 0, phase ^= 1u;
             }
-            // Do not leave while copies into this CTA's shared memory are in
-            // flight (matters only when a consumer gave up early).
-            for (int i = issued - S > 0 ? issued - S : 0; i < issued; ++i)
-                mbar_wait(&full[i & (S - 1)], static_cast<uint32_t>((i >> p.stage_shift) & 1), p.err, kErrWaitFull);
+            __threadfence_block();  // issued_count before final_count
+            *reinterpret_cast<volatile int *>(&final_count) = issued;
+            if (!ok) {
+                abort_flag = 1;
+                // do not leave while copies into this CTA's shared memory are in flight
+                for (int i = issued - S > 0 ? issued - S : 0; i < issued; ++i)
+                    mbar_wait(&full[i % S], static_cast<uint32_t>((i / S) & 1), p.err, kErrWaitFull);
+            }
         }
         return;
     }
@@ -635,6 +725,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     else
         stage_act_q8_K<MT, kF32>(p, smem, tid);
     consumer_sync();
+    // Programmatic dependent launch: the next launch on the stream may start
+    // once every CTA of this one has its activations staged (it needs the
+    // other half of the SM's shared memory).  Triggering only now keeps the
+    // next launch's weight prefetch from competing with this launch's
+    // activation loads; only that prefetch runs before its
+    // griddepcontrol.wait, activations and outputs stay ordered after this
+    // grid as usual.
+    if (p.overlap && tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     ActRegs<(RG > 0 ? RG : 1)> ar;
     if constexpr (RG > 0) {
@@ -659,38 +757,52 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvParams 
     }
 
     int g = 0;  // matrix of the claimed tile (claims only increase)
+    // Each warp holds two claims: the pair it works on and the next one,
+    // taken while the current pair is processed so that the atomic's latency
+    // is off the critical path.
+    int q_next = 0;
+    if (lane == 0) q_next = atomicAdd(&next_tile, 1);
     for (;;) {
-        int q = 0;
-        if (lane == 0) q = atomicAdd(&next_tile, 1);
-        q = __shfl_sync(0xffffffffu, q, 0);
+        const int q = __shfl_sync(0xffffffffu, q_next, 0);
         const int i = q >> p.pair_shift;                   // local tile index
         const int pr = q & ((1 << p.pair_shift) - 1);      // pair within the tile
-        const int tile = blockIdx.x + i * gridDim.x;
-        if (tile >= p.num_tiles) break;
         if (*reinterpret_cast<volatile int *>(&abort_flag)) break;
-        const int stage = i & (S - 1);
-        if (!mbar_wait(&full[stage], static_cast<uint32_t>((i >> p.stage_shift) & 1), p.err, kErrWaitFull)) {
+        const int lap = i / S;
+        const int stage = i - lap * S;
+        const int avail = wait_issued(&issued_count, &final_count, i, p.err);
+        if (avail <= 0) {
+            if (avail < 0) abort_flag = 1;
+            break;  // 0: the CTA's tiles are all taken
+        }
+        if (!mbar_wait(&full[stage], static_cast<uint32_t>(lap & 1), p.err, kErrWaitFull)) {
             abort_flag = 1;
             break;
         }
-        while (tile >= p.tile_base[g + 1]) ++g;
-        const int lt = tile - p.tile_base[g];
+        const int tile_r = *reinterpret_cast<volatile int *>(&stage_tile[stage]);
+        const int tile_rows = *reinterpret_cast<volatile int *>(&stage_rows[stage]);
+        if (lane == 0) q_next = atomicAdd(&next_tile, 1);
+        while (tile_r >= p.row_base[g + 1]) ++g;
         const Out o{p.cg[g], p.ldcg[g]};
-        const int tile_row = lt * p.rows_per_tile;
+        const int tile_row = tile_r - p.row_base[g];  // first row of the tile in matrix g
         const int row0 = tile_row + kPairRows * pr;
-        const int nrows = p.ng[g] - row0 < kPairRows ? p.ng[g] - row0 : kPairRows;
+        const int nrows = tile_rows - kPairRows * pr < kPairRows ? tile_rows - kPairRows * pr : kPairRows;
+        // offset of row0 in the stage: the window starts at the tile's first
+        // byte rounded down to 16 (low bits from wrap-around math)
+        const uint32_t row_off = static_cast<uint32_t>(kPairRows * pr) * static_cast<uint32_t>(p.row_bytes) +
+                                 ((static_cast<uint32_t>(tile_row) * static_cast<uint32_t>(p.row_bytes)) & 15u);
+        const uint8_t *buf = smem + p.stage_offset + static_cast<uint32_t>(stage) * p.stage_bytes;
+        if constexpr (WT == 0 && RG > 0) {
+            // copy the pair's weights to registers, release the stage, then compute
+            RowsW<RG> rw;
+            if (nrows > 0) load_rows_q4_0<RG>(p, buf, row_off, nrows, lane, rw);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[stage]);
+            if (nrows > 0) rows_q4_0_reg<RG, kPartials>(p, o, ar, rw, row0, nrows, lane);
+            continue;
+        }
         if (nrows > 0) {
-            // offset of row0 in the stage: the window starts at the tile's
-            // first byte rounded down to 16 (low bits from wrap-around math)
-            const uint32_t row_off =
-                static_cast<uint32_t>(kPairRows * pr) * static_cast<uint32_t>(p.row_bytes) +
-                ((static_cast<uint32_t>(tile_row) * static_cast<uint32_t>(p.row_bytes)) & 15u);
-            const uint8_t *buf = smem + p.stage_offset + static_cast<uint32_t>(stage) * p.stage_bytes;
             if constexpr (WT == 0) {
-                if constexpr (RG > 0)
-                    rows_q4_0_reg<RG, kPartials>(p, o, ar, buf, row_off, row0, nrows, lane);
-                else
-                    rows_q4_0_smem<MT, kPartials>(p, o, act, buf, row_off, row0, nrows, lane);
+                rows_q4_0_smem<MT, kPartials>(p, o, act, buf, row_off, row0, nrows, lane);
             } else {
                 for (int r = 0; r < nrows; ++r) {
                     const uint32_t off = row_off + static_cast<uint32_t>(r * p.row_bytes);
@@ -734,18 +846,20 @@ bool plan(int wtype, int64_t m, int count, const int64_t *ns, int64_t k, GemvPar
     const int mt = mt_of(m);
     const int64_t rb = row_bytes_of(wtype, k);
     p.row_bytes = static_cast<int>(rb);
-    p.rows_per_tile = rb >= 2048 ? 4 : 8;
-    p.pair_shift = p.rows_per_tile == 4 ? 1 : 2;
+    p.rows_per_tile = rb >= 2048 ? kTileRowsLong : 8;
+    p.pair_shift = 0;
+    while ((kPairRows << p.pair_shift) < p.rows_per_tile) ++p.pair_shift;
     p.count = count;
-    int64_t tiles = 0;
+    int64_t rows = 0;
     for (int g = 0; g < count; ++g) {
         p.ng[g] = static_cast<int>(ns[g]);
-        p.tile_base[g] = static_cast<int>(tiles);
-        tiles += (ns[g] + p.rows_per_tile - 1) / p.rows_per_tile;
+        p.row_base[g] = static_cast<int>(rows);
+        rows += ns[g];
     }
-    for (int g = count; g <= kMaxGroup; ++g) p.tile_base[g] = static_cast<int>(tiles);
-    if (tiles > 0x7fffffff) return false;
-    p.num_tiles = static_cast<int>(tiles);
+    if (rows > 0x3fffffff) return false;
+    for (int g = count; g <= kMaxGroup; ++g) p.row_base[g] = static_cast<int>(rows);
+    p.total_rows = static_cast<int>(rows);
+    p.num_tiles = static_cast<int>((rows + p.rows_per_tile - 1) / p.rows_per_tile);
     p.groups = static_cast<int>((k / 32 + 63) / 64);
     p.stage_bytes = align_up_u32(static_cast<uint32_t>(p.rows_per_tile * rb) + 16 + kStageSlack, 128);
     p.grid_offset = kBarrierBytes;
@@ -754,13 +868,10 @@ bool plan(int wtype, int64_t m, int count, const int64_t *ns, int64_t k, GemvPar
     // at most half the SM's shared memory, so that the next launch's CTA can
     // be resident beside this one (overlapped decode launches)
     const size_t optin = device_smem_optin();
-    const size_t budget = (optin + 1024) / 2 - 2048;
+    const size_t budget = (optin + 1024) / kCtasPerSm - 2048;
     if (p.stage_offset + 4 * static_cast<size_t>(p.stage_bytes) > budget) return false;
     const size_t fit = (budget - p.stage_offset) / p.stage_bytes;
-    int stages = 4, shift = 2;
-    while (stages * 2 <= kMaxStages && static_cast<size_t>(stages * 2) <= fit) stages *= 2, ++shift;
-    p.stages = stages;
-    p.stage_shift = shift;
+    p.stages = static_cast<int>(fit < static_cast<size_t>(kMaxStages) ? fit : kMaxStages);
     smem_bytes = p.stage_offset + static_cast<uint32_t>(p.stages) * p.stage_bytes;
     return true;
 }

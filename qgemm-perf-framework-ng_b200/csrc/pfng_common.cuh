@@ -34,6 +34,7 @@ PFNG_DEV float f16_bits_to_f32(uint32_t h) { return __half2float(__ushort_as_hal
 // and clears it with pfng_b200_check_kernel_error().
 constexpr int kErrWaitFull = 1;
 constexpr int kErrWaitEmpty = 2;
+constexpr int kErrWaitIssue = 3;
 
 PFNG_DEV void report_error(int *flag, int code) {
     if (flag) atomicCAS(flag, 0, code);
@@ -53,16 +54,31 @@ PFNG_DEV void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
 }
-// One bounded attempt: the hardware suspends the thread for up to ~1 us.
+// One bounded attempt: the hardware may suspend the thread for a while
+// (at most PFNG_WAIT_HINT_NS when that is non-zero, else a system-dependent
+// limit) or until the phase completes.
+#ifndef PFNG_WAIT_HINT_NS
+#define PFNG_WAIT_HINT_NS 1000
+#endif
 PFNG_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t done;
+#if PFNG_WAIT_HINT_NS > 0
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 1000;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity), "n"(PFNG_WAIT_HINT_NS)
+        : "memory");
+#else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(done)
         : "r"(smem_u32(bar)), "r"(parity)
         : "memory");
+#endif
     return done != 0;
 }
 // Every wait in this library is bounded: about 2^20 attempts of <= ~1 us, so

@@ -10,6 +10,72 @@
 
 namespace pfng {
 
+// roundf(y) (round half away from zero) as an int, for |y| < 2^22, on the FMA
+// and integer pipes: y + 1.5 * 2^23 rounds y to the nearest integer with ties
+// to even (the integer is the low bits of the sum), and a tie that went
+// toward zero is moved one step away.  Same result as (int)roundf(y).
+PFNG_DEV int round_half_away(float y) {
+    constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+    const float t = __fadd_rn(y, kMagic);
+    const int r = __float_as_int(t) - 0x4B400000;
+    const float diff = __fsub_rn(y, __fsub_rn(t, kMagic));  // exact, in [-0.5, 0.5]
+    return r + ((diff == 0.5f && y > 0.0f) ? 1 : 0) - ((diff == -0.5f && y < 0.0f) ? 1 : 0);
+}
+
+// ---------------------------------------------------------------------------
+// q8_0 with 4 lanes per 32-value block, lane c of the group holding values
+// 8c..8c+7 (llama_reference.cpp:38-52).  Two shuffle levels per reduction;
+// the rounding uses no conversion instructions.
+// ---------------------------------------------------------------------------
+struct Q8_0Quad {
+    uint32_t q0, q1;  // 8 packed int8
+    uint16_t dbits;   // fp16 scale
+    int qsum;         // sum of the whole block's int8 values (all 4 lanes)
+};
+
+template <int N>
+PFNG_DEV void q8_0_quantize_quads(const float (&v)[N][8], Q8_0Quad (&r)[N]) {
+    float amax[N], scale[N], inv[N];
+    int s[N];
+#pragma unroll
+    for (int b = 0; b < N; ++b) {
+        amax[b] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax[b] = fmaxf(amax[b], fabsf(v[b][i]));
+    }
+#pragma unroll
+    for (int o = 1; o < 4; o <<= 1)
+#pragma unroll
+        for (int b = 0; b < N; ++b) amax[b] = fmaxf(amax[b], __shfl_xor_sync(0xffffffffu, amax[b], o));
+#pragma unroll
+    for (int b = 0; b < N; ++b) scale[b] = __fdiv_rn(amax[b], 127.0f);
+#pragma unroll
+    for (int b = 0; b < N; ++b) inv[b] = scale[b] != 0.0f ? __fdiv_rn(1.0f, scale[b]) : 0.0f;
+#pragma unroll
+    for (int b = 0; b < N; ++b) {
+        r[b].q0 = r[b].q1 = 0;
+        s[b] = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int qi = round_half_away(__fmul_rn(v[b][i], inv[b]));
+            s[b] += qi;
+            if (i < 4)
+                r[b].q0 |= (static_cast<uint32_t>(qi) & 0xffu) << (8 * i);
+            else
+                r[b].q1 |= (static_cast<uint32_t>(qi) & 0xffu) << (8 * (i - 4));
+        }
+    }
+#pragma unroll
+    for (int o = 1; o < 4; o <<= 1)
+#pragma unroll
+        for (int b = 0; b < N; ++b) s[b] += __shfl_xor_sync(0xffffffffu, s[b], o);
+#pragma unroll
+    for (int b = 0; b < N; ++b) {
+        r[b].qsum = s[b];
+        r[b].dbits = f32_to_f16_bits(scale[b]);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // q8_0: 8 lanes per 32-value block, lane g of the group holds values 4g..4g+3.
 // llama_reference.cpp:38-52.
