@@ -21,10 +21,10 @@
 //     the block scales in fp32 and reduce across the warp.  For q4_0 at
 //     m = 1 a warp copies its pair's weights to registers and releases the
 //     pair before computing, so stages return to the producer early.
-//   Measured on B200 (decode step of two matrices, 35 MB): 14 consumer warps
-//   with 8-row (18 KB) tiles and one CTA per SM stream fastest; fewer warps
-//   leave the consumers latency-bound, more add staging and scheduling cost,
-//   and 4-row tiles double the producer's per-tile work.
+//   Measured on B200 (decode step of two matrices, 35 MB): 12-16 consumer
+//   warps with 8-row (18 KB) tiles and one CTA per SM stream fastest; fewer
+//   warps leave the consumers latency-bound, more add staging and scheduling
+//   cost, and 4-row tiles double the producer's per-tile work.
 //
 // q4_0 lane mapping: lane l of a warp takes the block PAIR (2l, 2l+1) of each
 // group of 64 blocks.  A pair is 36 contiguous bytes = 9 aligned words at word
@@ -45,7 +45,7 @@ namespace pfng {
 namespace {
 
 #ifndef PFNG_GEMV_CONSUMER_WARPS
-#define PFNG_GEMV_CONSUMER_WARPS 14
+#define PFNG_GEMV_CONSUMER_WARPS 12
 #endif
 #ifndef PFNG_GEMV_CTAS_PER_SM
 #define PFNG_GEMV_CTAS_PER_SM 1
@@ -55,12 +55,13 @@ constexpr int kCtasPerSm = PFNG_GEMV_CTAS_PER_SM;  // 2: half the shared memory,
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kGemvThreads = kConsumerThreads + 32;
 constexpr int kMaxStages = 32;
-constexpr int kPairRows = 2;         // rows a warp claims at a time
+constexpr int kPairRows = 2;         // rows a warp processes together
+constexpr int kClaimRows = 4;        // rows a warp claims at a time (two pairs)
 #ifndef PFNG_GEMV_TILE_ROWS
 #define PFNG_GEMV_TILE_ROWS 8
 #endif
 constexpr int kTileRowsLong = PFNG_GEMV_TILE_ROWS;  // rows per tile when a row is >= 2 KB
-static_assert(kTileRowsLong >= kPairRows && (kTileRowsLong & (kTileRowsLong - 1)) == 0, "tile rows");
+static_assert(kTileRowsLong >= kClaimRows && (kTileRowsLong & (kTileRowsLong - 1)) == 0, "tile rows");
 constexpr int kMaxGroup = kGemvMaxGroup;
 constexpr uint32_t kBarrierBytes = 2 * kMaxStages * 8;
 constexpr uint32_t kGridTableBytes = 256 * 8;
@@ -76,8 +77,8 @@ struct GemvParams {
     int m, n, k;       // n: rows of matrix 0 (partials indexing)
     int x_vec;         // fp32 rows are 16-byte aligned with ldx % 4 == 0
     int row_bytes;
-    int rows_per_tile;  // kPairRows times a power of two
-    int pair_shift;     // log2(rows_per_tile / kPairRows)
+    int rows_per_tile;  // kClaimRows times a power of two
+    int claim_shift;    // log2(rows_per_tile / kClaimRows)
     int num_tiles;      // ceil(total_rows / rows_per_tile): CTAs beyond it would be idle
     int stages;        // ring depth (any count up to kMaxStages)
     uint32_t stage_bytes;
@@ -622,8 +623,8 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
     uint64_t *empty = full + kMaxStages;
     __shared__ int abort_flag;
     __shared__ int next_tile;
-    __shared__ int stage_tile[kMaxStages];  // first row (launch row sequence) of each stage's tile
-    __shared__ int stage_rows[kMaxStages];  // and its number of rows
+    // per stage: {matrix, first row of the tile in that matrix, rows, 0}
+    __shared__ int4 stage_info[kMaxStages];
     // Local tiles issued so far and, once the launch's tiles are all claimed,
     // their final number.  A consumer waits on a stage's mbarrier only after
     // its tile has been issued: the producer issues local tile i only after
@@ -637,7 +638,7 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
 
     if (tid < S) {
         mbar_init(&full[tid], 1);
-        mbar_init(&empty[tid], p.rows_per_tile / kPairRows);  // one arrival per row pair
+        mbar_init(&empty[tid], p.rows_per_tile / kClaimRows);  // one arrival per claim
         fence_mbar_init();
     }
     if (tid == 0) {
@@ -680,8 +681,7 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
                 const uint32_t bytes = static_cast<uint32_t>(we - ws);
                 const uint8_t *src = p.wg[g] + ws;
                 uint8_t *dst = smem + p.stage_offset + static_cast<uint32_t>(stage) * p.stage_bytes;
-                stage_tile[stage] = r;
-                stage_rows[stage] = rows;
+                stage_info[stage] = make_int4(g, lr, rows, 0);
                 r += rows;
                 mbar_arrive_expect_tx(&full[stage], bytes);
                 bulk_copy_g2s(dst, src, bytes, &full[stage], policy);
@@ -756,65 +756,74 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
         }
     }
 
-    int g = 0;  // matrix of the claimed tile (claims only increase)
-    // Each warp holds two claims: the pair it works on and the next one,
-    // taken while the current pair is processed so that the atomic's latency
-    // is off the critical path.
+    // Each warp holds two claims: the rows it works on and the next ones,
+    // taken while the current ones are processed so that the atomic's
+    // latency is off the critical path.  A claim is kClaimRows rows of one
+    // tile, processed as two pairs.
     int q_next = 0;
     if (lane == 0) q_next = atomicAdd(&next_tile, 1);
+    int cur_i = 0, stage = 0, lap = 0;  // ring position of the last claim (claims only increase)
     for (;;) {
         const int q = __shfl_sync(0xffffffffu, q_next, 0);
-        const int i = q >> p.pair_shift;                   // local tile index
-        const int pr = q & ((1 << p.pair_shift) - 1);      // pair within the tile
-        if (*reinterpret_cast<volatile int *>(&abort_flag)) break;
-        const int lap = i / S;
-        const int stage = i - lap * S;
+        const int i = q >> p.claim_shift;                   // local tile index
+        const int qr = q & ((1 << p.claim_shift) - 1);      // claim within the tile
+        stage += i - cur_i;
+        cur_i = i;
+        while (stage >= S) stage -= S, ++lap;
         const int avail = wait_issued(&issued_count, &final_count, i, p.err);
         if (avail <= 0) {
             if (avail < 0) abort_flag = 1;
             break;  // 0: the CTA's tiles are all taken
         }
+        if (*reinterpret_cast<volatile int *>(&abort_flag)) break;
         if (!mbar_wait(&full[stage], static_cast<uint32_t>(lap & 1), p.err, kErrWaitFull)) {
             abort_flag = 1;
             break;
         }
-        const int tile_r = *reinterpret_cast<volatile int *>(&stage_tile[stage]);
-        const int tile_rows = *reinterpret_cast<volatile int *>(&stage_rows[stage]);
+        const int4 info = stage_info[stage];  // ordered after the mbarrier wait (memory clobber)
         if (lane == 0) q_next = atomicAdd(&next_tile, 1);
-        while (tile_r >= p.row_base[g + 1]) ++g;
+        const int g = info.x, tile_row = info.y, tile_rows = info.z;
         const Out o{p.cg[g], p.ldcg[g]};
-        const int tile_row = tile_r - p.row_base[g];  // first row of the tile in matrix g
-        const int row0 = tile_row + kPairRows * pr;
-        const int nrows = tile_rows - kPairRows * pr < kPairRows ? tile_rows - kPairRows * pr : kPairRows;
-        // offset of row0 in the stage: the window starts at the tile's first
-        // byte rounded down to 16 (low bits from wrap-around math)
-        const uint32_t row_off = static_cast<uint32_t>(kPairRows * pr) * static_cast<uint32_t>(p.row_bytes) +
-                                 ((static_cast<uint32_t>(tile_row) * static_cast<uint32_t>(p.row_bytes)) & 15u);
+        // the stage's window starts at the tile's first byte rounded down to 16
+        const uint32_t mis = (static_cast<uint32_t>(tile_row) * static_cast<uint32_t>(p.row_bytes)) & 15u;
         const uint8_t *buf = smem + p.stage_offset + static_cast<uint32_t>(stage) * p.stage_bytes;
-        if constexpr (WT == 0 && RG > 0) {
-            // copy the pair's weights to registers, release the stage, then compute
-            RowsW<RG> rw;
-            if (nrows > 0) load_rows_q4_0<RG>(p, buf, row_off, nrows, lane, rw);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[stage]);
-            if (nrows > 0) rows_q4_0_reg<RG, kPartials>(p, o, ar, rw, row0, nrows, lane);
-            continue;
-        }
-        if (nrows > 0) {
-            if constexpr (WT == 0) {
-                rows_q4_0_smem<MT, kPartials>(p, o, act, buf, row_off, row0, nrows, lane);
+#pragma unroll 1
+        for (int h = 0; h < kClaimRows / kPairRows; ++h) {
+            const int first = kClaimRows * qr + kPairRows * h;  // first row of the pair in the tile
+            const int row0 = tile_row + first;
+            const int nrows = tile_rows - first < kPairRows ? tile_rows - first : kPairRows;
+            const uint32_t row_off = static_cast<uint32_t>(first) * static_cast<uint32_t>(p.row_bytes) + mis;
+            const bool last = h == kClaimRows / kPairRows - 1;
+            if constexpr (WT == 0 && RG > 0) {
+                // copy the pair's weights to registers; after the claim's last
+                // pair is copied, release the stage, then compute
+                RowsW<RG> rw;
+                if (nrows > 0) load_rows_q4_0<RG>(p, buf, row_off, nrows, lane, rw);
+                if (last) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[stage]);
+                }
+                if (nrows > 0) rows_q4_0_reg<RG, kPartials>(p, o, ar, rw, row0, nrows, lane);
             } else {
-                for (int r = 0; r < nrows; ++r) {
-                    const uint32_t off = row_off + static_cast<uint32_t>(r * p.row_bytes);
-                    if constexpr (WT == 1)
-                        row_q4_K<MT, kPartials>(p, o, act, buf, off, row0 + r, lane);
-                    else
-                        row_iq2_xxs<MT, kPartials>(p, o, act, buf, off, row0 + r, lane, grid);
+                if (nrows > 0) {
+                    if constexpr (WT == 0) {
+                        rows_q4_0_smem<MT, kPartials>(p, o, act, buf, row_off, row0, nrows, lane);
+                    } else {
+                        for (int r = 0; r < nrows; ++r) {
+                            const uint32_t off = row_off + static_cast<uint32_t>(r * p.row_bytes);
+                            if constexpr (WT == 1)
+                                row_q4_K<MT, kPartials>(p, o, act, buf, off, row0 + r, lane);
+                            else
+                                row_iq2_xxs<MT, kPartials>(p, o, act, buf, off, row0 + r, lane, grid);
+                        }
+                    }
+                }
+                if (last) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[stage]);
                 }
             }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[stage]);
     }
 }
 
@@ -847,8 +856,8 @@ bool plan(int wtype, int64_t m, int count, const int64_t *ns, int64_t k, GemvPar
     const int64_t rb = row_bytes_of(wtype, k);
     p.row_bytes = static_cast<int>(rb);
     p.rows_per_tile = rb >= 2048 ? kTileRowsLong : 8;
-    p.pair_shift = 0;
-    while ((kPairRows << p.pair_shift) < p.rows_per_tile) ++p.pair_shift;
+    p.claim_shift = 0;
+    while ((kClaimRows << p.claim_shift) < p.rows_per_tile) ++p.claim_shift;
     p.count = count;
     int64_t rows = 0;
     for (int g = 0; g < count; ++g) {

@@ -10,22 +10,23 @@
 
 namespace pfng {
 
-// roundf(y) (round half away from zero) as an int, for |y| < 2^22, on the FMA
-// and integer pipes: y + 1.5 * 2^23 rounds y to the nearest integer with ties
-// to even (the integer is the low bits of the sum), and a tie that went
-// toward zero is moved one step away.  Same result as (int)roundf(y).
+// roundf(y) (round half away from zero) as an int, for |y| < 2^22: the
+// integer part of |y| + 0.5, sign restored.  |y| + 0.5 is rounded to float
+// before the truncation, which changes the result for exactly one magnitude:
+// 0.49999997 (the largest float below 0.5), whose sum with 0.5 is a tie that
+// rounds up to 1.0.  Every other |y| < 2^22 either adds exactly or rounds to
+// a value with the same integer part.  Same result as (int)roundf(y).
 PFNG_DEV int round_half_away(float y) {
-    constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-    const float t = __fadd_rn(y, kMagic);
-    const int r = __float_as_int(t) - 0x4B400000;
-    const float diff = __fsub_rn(y, __fsub_rn(t, kMagic));  // exact, in [-0.5, 0.5]
-    return r + ((diff == 0.5f && y > 0.0f) ? 1 : 0) - ((diff == -0.5f && y < 0.0f) ? 1 : 0);
+    const float a = fabsf(y);
+    int r = __float2int_rz(__fadd_rn(a, 0.5f));
+    if (a == 0.49999997f) r = 0;
+    return y < 0.0f ? -r : r;
 }
 
 // ---------------------------------------------------------------------------
 // q8_0 with 4 lanes per 32-value block, lane c of the group holding values
 // 8c..8c+7 (llama_reference.cpp:38-52).  Two shuffle levels per reduction;
-// the rounding uses no conversion instructions.
+// the rounding is round_half_away above.
 // ---------------------------------------------------------------------------
 struct Q8_0Quad {
     uint32_t q0, q1;  // 8 packed int8
@@ -50,7 +51,7 @@ PFNG_DEV void q8_0_quantize_quads(const float (&v)[N][8], Q8_0Quad (&r)[N]) {
 #pragma unroll
     for (int b = 0; b < N; ++b) scale[b] = __fdiv_rn(amax[b], 127.0f);
 #pragma unroll
-    for (int b = 0; b < N; ++b) inv[b] = scale[b] != 0.0f ? __fdiv_rn(1.0f, scale[b]) : 0.0f;
+    for (int b = 0; b < N; ++b) inv[b] = scale[b] != 0.0f ? __frcp_rn(scale[b]) : 0.0f;
 #pragma unroll
     for (int b = 0; b < N; ++b) {
         r[b].q0 = r[b].q1 = 0;
