@@ -175,7 +175,7 @@ int run_matmul(int wtype, const void *w, const void *a, const float *x, int64_t 
         else
             e = f32 ? launch_quantize_q8_K_split(x, ldx, sa, m, k, s) : launch_convert_q8_K_split(a, sa, m, k, s);
         if (e == cudaSuccess) {
-            GemmArgs g{wtype, w, sa, c, ldc, partials, m, n, k};
+            GemmArgs g{wtype, w, sa, c, ldc, partials, m, n, k, info->error_word};
             e = launch_gemm(g, s);
         }
     } else {
@@ -211,6 +211,11 @@ size_t query_workspace(int wtype, int64_t m, int64_t n, int64_t k, int path, boo
 int device_sm_count() {
     DeviceInfo *info = current_info();
     return info ? info->sm_count : 148;
+}
+
+int *device_error_word() {
+    DeviceInfo *info = current_info();
+    return info ? info->error_word : nullptr;
 }
 
 size_t device_smem_optin() {

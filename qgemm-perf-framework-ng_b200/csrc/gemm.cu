@@ -27,6 +27,9 @@
 // are exact (int32 tensor-core accumulation); the fp32 fold follows the
 // reference's block order (k ascending), so results differ from the
 // reference only by where fp32 rounding happens.
+#include <cstdlib>
+#include <cstring>
+
 #include "iq2xxs_grid_codes.h"
 #include "pfng_common.cuh"
 #include "pfng_internal.h"
@@ -36,6 +39,7 @@ namespace {
 
 constexpr int BK = 256;
 constexpr int kThreads = 256;
+constexpr bool kTcDefault = false;
 constexpr int kStages = 3;
 constexpr uint32_t kMagicBits = 0x4B400000u;  // float 12582912 = 2^23 + 2^22
 constexpr float kMagic = 12582912.0f;
@@ -541,7 +545,18 @@ bool gemm_supported(int wtype, int64_t m, int64_t n, int64_t k, const void *w) {
     return Cfg<128, 128>::kSmem <= device_smem_optin();
 }
 
+// The q4_0 product runs on the tcgen05 kernel (gemm_tc.cu) unless the
+// environment variable PFNG_B200_GEMM is "mma" (or the shape is unsupported);
+// "tc" / "mma" select either kernel explicitly, for comparisons.
+static bool use_tc(const GemmArgs &args) {
+    if (args.wtype != 0 || args.partials) return false;
+    const char *e = std::getenv("PFNG_B200_GEMM");
+    const bool want = e ? std::strcmp(e, "tc") == 0 : kTcDefault;
+    return want && gemm_tc_supported(args.wtype, args.m, args.n, args.k, args.w);
+}
+
 cudaError_t launch_gemm(const GemmArgs &args, cudaStream_t s) {
+    if (use_tc(args)) return launch_gemm_tc(args, args.err, s);
     GemmParams p{};
     p.w = static_cast<const uint8_t *>(args.w);
     p.a = args.a;

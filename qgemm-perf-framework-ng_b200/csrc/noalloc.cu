@@ -88,6 +88,6 @@ extern "C" int pfng_b200_compute_q4_0_noalloc(const void *w, const float *x, int
     const SplitA sa = split_a_carve(scratch, m, k, 32);
     cudaError_t e = launch_quantize_q8_0_split(x, ldx, sa, m, k, s);
     if (e != cudaSuccess) return status_of(e);
-    GemmArgs g{PFNG_B200_Q4_0, w, sa, c, ldc, nullptr, m, n, k};
+    GemmArgs g{PFNG_B200_Q4_0, w, sa, c, ldc, nullptr, m, n, k, device_error_word()};
     return status_of(launch_gemm(g, s));
 }

@@ -81,6 +81,18 @@ PFNG_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 #endif
     return done != 0;
 }
+// Non-blocking probe of the phase with the given parity.
+PFNG_DEV bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
 // Every wait in this library is bounded: about 2^20 attempts of <= ~1 us, so
 // a wait that can never complete ends in about a second with `code` recorded.
 constexpr uint32_t kWaitAttempts = 1u << 20;

@@ -71,9 +71,14 @@ struct GemmArgs {
     int64_t ldc;
     int32_t *partials;
     int64_t m, n, k;
+    int *err = nullptr;  // library error word for bounded waits (tensor-memory kernel)
 };
 bool gemm_supported(int wtype, int64_t m, int64_t n, int64_t k, const void *w);
 cudaError_t launch_gemm(const GemmArgs &args, cudaStream_t s);
+
+// gemm_tc.cu -- q4_0 on tcgen05 / TMEM (k % 256 == 0, 16-byte aligned W)
+bool gemm_tc_supported(int wtype, int64_t m, int64_t n, int64_t k, const void *w);
+cudaError_t launch_gemm_tc(const GemmArgs &args, int *err, cudaStream_t s);
 
 // simple.cu -- one thread per output element, any k multiple of the block.
 struct SimpleArgs {
@@ -93,5 +98,6 @@ cudaError_t launch_unshard_columns(const float *slices, float *c, int64_t m, int
 
 int device_sm_count();
 size_t device_smem_optin();
+int *device_error_word();  // the current device's error word, nullptr if unavailable
 
 }  // namespace pfng

@@ -312,3 +312,26 @@ def test_grouped_overlap_keeps_order(oracle):
     for g, n in enumerate(ns):
         single = host(pb.compute("q4_0", dsets[2][g], xs[2], n, path="gemv"))
         np.testing.assert_array_equal(got[g].view(np.uint32), single.view(np.uint32))
+
+
+# ------------------------------------------------- tcgen05 / TMEM q4_0 kernel
+@pytest.mark.parametrize("m,n,k", [(9, 129, 256), (130, 300, 1536), (64, 128, 512), (480, 1536, 1536),
+                                   (1000, 520, 2048)])
+def test_q4_0_tcgen05_kernel(oracle, monkeypatch, m, n, k):
+    # The tensor-memory kernel (selected with PFNG_B200_GEMM=tc) against the
+    # oracle within tolerance, and bit-identical to the mma.sync kernel: both
+    # fold the same integer sub-block sums in the same order.
+    rng = np.random.default_rng(m * 31 + n + k)
+    w = oracle.quantize("q4_0", rng.standard_normal((n, k)).astype(np.float32))
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    a = oracle.quantize("q8_0", x)
+    ref = oracle.mm("q4_0", w, a, m, n, k)
+    bound = oracle.bound("q4_0", w, a, m, n, k)
+    wd, xd = dev_bytes(w), dev(x)
+    monkeypatch.setenv("PFNG_B200_GEMM", "tc")
+    c_tc = host(pb.compute("q4_0", wd, xd, n, path="mma"))
+    pb.check_kernel_error()
+    monkeypatch.setenv("PFNG_B200_GEMM", "mma")
+    c_mma = host(pb.compute("q4_0", wd, xd, n, path="mma"))
+    check_close(c_tc, ref, bound, f"tcgen05 q4_0 {m}x{n}x{k}")
+    np.testing.assert_array_equal(c_tc.view(np.uint32), c_mma.view(np.uint32))
