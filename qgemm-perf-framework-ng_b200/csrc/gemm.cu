@@ -527,6 +527,12 @@ cudaError_t launch_t(const GemmParams &p, cudaStream_t s) {
 template <int WT, bool kPartials>
 cudaError_t launch_tile(const GemmParams &p, cudaStream_t s) {
     // the largest tile that still gives every SM at least ~1.5 CTAs
+    // (PFNG_B200_GEMM_TILE = "128x128" / "64x128" / "64x64" forces one, for comparisons)
+    if (const char *t = std::getenv("PFNG_B200_GEMM_TILE")) {
+        if (std::strcmp(t, "128x128") == 0) return launch_t<WT, Cfg<128, 128>, kPartials>(p, s);
+        if (std::strcmp(t, "64x128") == 0) return launch_t<WT, Cfg<64, 128>, kPartials>(p, s);
+        if (std::strcmp(t, "64x64") == 0) return launch_t<WT, Cfg<64, 64>, kPartials>(p, s);
+    }
     const int64_t sms = device_sm_count();
     auto ctas = [&](int bm, int bn) { return ((p.n + bn - 1) / bn) * ((p.m + bm - 1) / bm); };
     if (ctas(128, 128) * 2 >= 3 * sms) return launch_t<WT, Cfg<128, 128>, kPartials>(p, s);

@@ -105,7 +105,7 @@ PFNG_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, int *flag, int code) {
 
 // Bulk (non-tensor) TMA copy global -> this CTA's shared memory, completing
 // `bytes` of transaction count on `bar`.  dst, src and bytes must be
-// multiples of 16.  No multicast.
+// multiples of 16.  The destination is this CTA's own shared memory.
 PFNG_DEV void bulk_copy_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar, uint64_t policy) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
