@@ -526,8 +526,7 @@ cudaError_t launch_t(const GemmParams &p, cudaStream_t s) {
 
 template <int WT, bool kPartials>
 cudaError_t launch_tile(const GemmParams &p, cudaStream_t s) {
-    // the largest tile that still gives every SM at least ~1.5 CTAs
-    // (PFNG_B200_GEMM_TILE = "128x128" / "64x128" / "64x64" forces one, for comparisons)
+    // tile choice by CTA count (PFNG_B200_GEMM_TILE = "128x128" / "64x128" / "64x64" forces one, for comparisons)
     if (const char *t = std::getenv("PFNG_B200_GEMM_TILE")) {
         if (std::strcmp(t, "128x128") == 0) return launch_t<WT, Cfg<128, 128>, kPartials>(p, s);
         if (std::strcmp(t, "64x128") == 0) return launch_t<WT, Cfg<64, 128>, kPartials>(p, s);
@@ -535,8 +534,11 @@ cudaError_t launch_tile(const GemmParams &p, cudaStream_t s) {
     }
     const int64_t sms = device_sm_count();
     auto ctas = [&](int bm, int bn) { return ((p.n + bn - 1) / bn) * ((p.m + bm - 1) / bm); };
-    if (ctas(128, 128) * 2 >= 3 * sms) return launch_t<WT, Cfg<128, 128>, kPartials>(p, s);
-    if (ctas(64, 128) * 2 >= 3 * sms) return launch_t<WT, Cfg<64, 128>, kPartials>(p, s);
+    // measured on B200: 128x128 wins once it fills ~80% of the SMs (512x4096x4096:
+    // 86 us vs 111 us with 64x128); below that the smaller tiles' extra CTAs win
+    // (480x1536x1536: 64x128 25 us, 128x128 36 us)
+    if (ctas(128, 128) * 5 >= 4 * sms) return launch_t<WT, Cfg<128, 128>, kPartials>(p, s);
+    if (ctas(64, 128) * 2 >= sms) return launch_t<WT, Cfg<64, 128>, kPartials>(p, s);
     return launch_t<WT, Cfg<64, 64>, kPartials>(p, s);
 }
 

@@ -6,7 +6,7 @@
 // compute_q4_0, bench/llama_reference/llama_reference.cpp:133-148 and :165-205.
 //
 // Tile: 128 weight rows (the MMA's M, one TMEM lane each) x 64 activation
-// rows (the MMA's N), k-steps of 256.  Warp roles (448 threads, one CTA/SM):
+// rows (the MMA's N), k-steps of 256.  Warp roles (384 threads, one CTA/SM):
 //   warp 0      loads: raw W rows, activation int8 rows (written straight
 //               into the 128-byte-swizzled K-major operand layout) and the
 //               activation scales, with cp.async into a 3-stage ring whose
@@ -14,22 +14,22 @@
 //   warp 1      TMEM owner and MMA issuer: one tcgen05.mma (M 128, N 64,
 //               K 32) per 32-deep sub-block, each into its own TMEM buffer
 //               (8 buffers, a whole k-step), completion signalled with
-//               tcgen05.commit;
-//   warps 2,3,12,13  decode: raw q4_0 blocks -> int8 (q - 8) operand rows in
+//               tcgen05.commit; each MMA overwrites its buffer (no
+//               accumulate), the fold reads it;
+//   warps 2,3   decode: raw q4_0 blocks -> int8 (q - 8) operand rows in
 //               the swizzled layout, the per-(row, sub-block) weight scales,
 //               and the activation scales transposed to [sub-block][row];
 //   warps 4-11  fold, thread = weight row, warps 4-7 activation rows 0-31 and
 //               warps 8-11 rows 32-63 (two warps per scheduler hide the TMEM
 //               load latency).  For each sub-block, tcgen05.ld the 32 int32
-//               partials, fold them into 32 fp32 accumulators in registers,
-//               write the TMEM columns back to the constant 0x4B400000 and
-//               release the buffer.
-// The fold is the exact two-FMA scheme of gemm.cu: every TMEM buffer holds
-// 0x4B400000 before its MMA accumulates into it, so the int32 result read
-// back is the float 2^23 + 2^22 + P exactly; t = fma(y, s, -(2^23+2^22) s)
+//               partials, release the buffer at once, and fold them into 32
+//               fp32 accumulators in registers.
+// The fold is the exact two-FMA scheme of gemm.cu: the int32 partial P read
+// back plus the integer 0x4B400000 is the float 2^23 + 2^22 + P exactly (one
+// integer add, no conversion); t = fma(y, s, -(2^23+2^22) s)
 // = round(P s) with s = d_w (fp16, exact products), acc = fma(t, d_a, acc).
-// Each output element costs one packed FMA pair per sub-block on the FMA
-// pipe; the MMAs, operand fetch and accumulation run beside it.
+// Each output element costs an integer add and one packed FMA pair per
+// sub-block; the MMAs, operand fetch and accumulation run beside them.
 //
 // Every wait is bounded; a wait that gives up records an error, raises the
 // CTA's abort flag (which ends every other role's waits at once) and the CTA
@@ -47,9 +47,9 @@ constexpr int kLoadStages = 3;
 constexpr int kABufs = 2;      // decoded weight operand buffers
 constexpr int kTmemBufs = 8;   // sub-block accumulators in TMEM
 constexpr uint32_t kTmemCols = kTmemBufs * TN;  // 512: all of TMEM
-constexpr int kThreads = 448;
+constexpr int kThreads = 384;
 constexpr int kFoldWarps = 8;
-constexpr int kDecodeWarps = 4;
+constexpr int kDecodeWarps = 2;
 constexpr uint32_t kRawSlot = 160;  // bytes per raw weight row per stage (144 used)
 constexpr uint32_t kMagicBits = 0x4B400000u;
 constexpr float kMagic = 12582912.0f;
@@ -135,15 +135,6 @@ PFNG_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         : "r"(taddr)
         : "memory");
 }
-// The same 32 columns all set to `v`.
-PFNG_DEV void tmem_st32_const(uint32_t taddr, uint32_t v) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
-        "%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
-        "r"(v)
-        : "memory");
-}
-PFNG_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 #undef PFNG_R32
 
 // Shared-memory matrix descriptor, K-major operand with the 128-byte swizzle:
@@ -171,15 +162,13 @@ PFNG_DEV uint32_t op_off(uint32_t rows, uint32_t row, uint32_t c) {
 
 PFNG_DEV bool aborted(const int *abort_flag) { return *reinterpret_cast<const volatile int *>(abort_flag) != 0; }
 
-// Bounded wait that also returns (false) as soon as the CTA's abort flag is
-// up.  Between attempts the warp sleeps briefly, so that the many waiting
-// warps of this kernel leave the issue slots to the working ones.
+// Bounded wait that also gives up (false) once the CTA's abort flag is up.
+// Each attempt is a hardware-suspended try_wait, so a waiting warp issues
+// almost nothing; the abort flag is looked at every 16 attempts.
 PFNG_DEV bool wait_bar(uint64_t *bar, uint32_t parity, const int *abort_flag, int *err, int code) {
-    if (mbar_test_wait(bar, parity)) return true;
     for (uint32_t i = 0; i < kWaitAttempts; ++i) {
-        __nanosleep(32);
-        if (mbar_test_wait(bar, parity)) return true;
-        if (*reinterpret_cast<const volatile int *>(abort_flag)) return false;
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 15u) == 15u && *reinterpret_cast<const volatile int *>(abort_flag)) return false;
     }
     report_error(err, code);
     return false;
@@ -190,8 +179,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4_0_kernel(const TcParam
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kOffBar);
     uint64_t *ld_full = bars;                              // [kLoadStages] cp.async landed (32 lane arrivals)
-    uint64_t *ld_empty = ld_full + kLoadStages;            // [kLoadStages] decode (4) + MMA commit (1)
-    uint64_t *dec_full = ld_empty + kLoadStages;           // [kABufs] decode done (4)
+    uint64_t *ld_empty = ld_full + kLoadStages;            // [kLoadStages] decode warps + MMA commit (1)
+    uint64_t *dec_full = ld_empty + kLoadStages;           // [kABufs] decode warps done
     uint64_t *dec_empty = dec_full + kABufs;               // [kABufs] MMA commit (1) + fold warps
     uint64_t *tm_full = dec_empty + kABufs;                // [kTmemBufs] MMA commit (1)
     uint64_t *tm_empty = tm_full + kTmemBufs;              // [kTmemBufs] fold warps
@@ -208,10 +197,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4_0_kernel(const TcParam
         abort_flag = 0;
         for (int s = 0; s < kLoadStages; ++s) {
             mbar_init(&ld_full[s], 32);
-            mbar_init(&ld_empty[s], 5);
+            mbar_init(&ld_empty[s], kDecodeWarps + 1);
         }
         for (int a = 0; a < kABufs; ++a) {
-            mbar_init(&dec_full[a], 4);
+            mbar_init(&dec_full[a], kDecodeWarps);
             mbar_init(&dec_empty[a], 1 + kFoldWarps);
         }
         for (int b = 0; b < kTmemBufs; ++b) {
@@ -292,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4_0_kernel(const TcParam
                     const uint32_t koff = (sb & 3) * 32u;  // k offset inside the 128-byte swizzled row
                     const uint64_t da = sw128_desc(aop + (sb >> 2) * (TM * 128u) + koff);
                     const uint64_t db = sw128_desc(bop + (sb >> 2) * (TN * 128u) + koff);
-                    umma_i8(tmem_base + static_cast<uint32_t>(buf * TN), da, db, kIdesc, 1u);
+                    umma_i8(tmem_base + static_cast<uint32_t>(buf * TN), da, db, kIdesc, 0u);
                     umma_commit(&tm_full[buf]);
                 }
                 if (!ok) {
@@ -307,9 +296,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4_0_kernel(const TcParam
             if (!mbar_wait(mma_done, 0, p.err, kErrWaitFull)) abort_flag = 1;
         }
         __syncwarp();
-    } else if (warp == 2 || warp == 3 || warp == 12 || warp == 13) {
+    } else if (warp == 2 || warp == 3) {
         // ---------------- decode: 8 threads per weight row, one block each ----------------
-        const int dt = (warp < 12 ? warp - 2 : warp - 10) * 32 + lane;  // 0..127
+        const int dt = (warp - 2) * 32 + lane;  // 0..63
         for (int ks = 0; ks < ksteps; ++ks) {
             const int s = ks % kLoadStages, a = ks % kABufs;
             if (!wait_bar(&ld_full[s], (ks / kLoadStages) & 1, &abort_flag, p.err, kErrWaitFull) ||
@@ -365,11 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4_0_kernel(const TcParam
         const int half = (warp - 4) >> 2;        // activation rows 32 * half .. + 31
         const int row = qtr * 32 + lane;         // weight row of this thread in the tile
         const uint32_t my_cols = tmem_base + (static_cast<uint32_t>(qtr * 32) << 16) + half * 32;
-        // every TMEM buffer starts as the magic constant
-        for (int b = 0; b < kTmemBufs; ++b) tmem_st32_const(my_cols + b * TN, kMagicBits);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
+        // every TMEM buffer starts free
         if (lane == 0)
             for (int b = 0; b < kTmemBufs; ++b) mbar_arrive(&tm_empty[b]);
 
@@ -398,20 +383,26 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4_0_kernel(const TcParam
                 tc_fence_after();
                 uint32_t r[32];
                 tmem_ld32(my_cols + buf * TN, r);
-                const float2 ss = make_float2(sv[sb], sv[sb]);
-                const float2 cm = make_float2(-kMagic * sv[sb], -kMagic * sv[sb]);
-                const float2 *dap = reinterpret_cast<const float2 *>(dat + sb * TN);
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const float2 y = make_float2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
-                    const float2 t = __ffma2_rn(y, ss, cm);
-                    acc[j] = __ffma2_rn(t, dap[j], acc[j]);
-                }
-                tmem_st32_const(my_cols + buf * TN, kMagicBits);
-                tmem_wait_st();
+                // the partials are in registers: hand the buffer back to the MMA
+                // issuer before the arithmetic
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tm_empty[buf]);
+                const float2 ss = make_float2(sv[sb], sv[sb]);
+                const float2 cm = make_float2(-kMagic * sv[sb], -kMagic * sv[sb]);
+                const float4 *dap = reinterpret_cast<const float4 *>(dat + sb * TN);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float4 d4 = dap[j];  // activation scales of columns 4j .. 4j + 3
+                    // P + 0x4B400000 as an integer is the float 2^23 + 2^22 + P
+                    const float2 y0 = make_float2(__uint_as_float(r[4 * j] + kMagicBits),
+                                                  __uint_as_float(r[4 * j + 1] + kMagicBits));
+                    const float2 y1 = make_float2(__uint_as_float(r[4 * j + 2] + kMagicBits),
+                                                  __uint_as_float(r[4 * j + 3] + kMagicBits));
+                    const float2 t0 = __ffma2_rn(y0, ss, cm), t1 = __ffma2_rn(y1, ss, cm);
+                    acc[2 * j] = __ffma2_rn(t0, make_float2(d4.x, d4.y), acc[2 * j]);
+                    acc[2 * j + 1] = __ffma2_rn(t1, make_float2(d4.z, d4.w), acc[2 * j + 1]);
+                }
             }
             gsb += 8;
             if (!ok) break;
