@@ -56,7 +56,13 @@ constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kGemvThreads = kConsumerThreads + 32;
 constexpr int kMaxStages = 32;
 constexpr int kPairRows = 2;         // rows a warp processes together
-constexpr int kClaimRows = 4;        // rows a warp claims at a time (two pairs)
+#ifndef PFNG_GEMV_CLAIM_ROWS
+#define PFNG_GEMV_CLAIM_ROWS 4
+#endif
+constexpr int kClaimRows = PFNG_GEMV_CLAIM_ROWS;  // rows a warp claims at a time (pairs of rows)
+#ifndef PFNG_GEMV_EARLY_TRIGGER
+#define PFNG_GEMV_EARLY_TRIGGER 0
+#endif
 #ifndef PFNG_GEMV_TILE_ROWS
 #define PFNG_GEMV_TILE_ROWS 8
 #endif
@@ -636,6 +642,7 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
     const int warp = tid >> 5, lane = tid & 31;
     const int S = p.stages;
 
+    if (PFNG_GEMV_EARLY_TRIGGER && p.overlap && tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     if (tid < S) {
         mbar_init(&full[tid], 1);
         mbar_init(&empty[tid], p.rows_per_tile / kClaimRows);  // one arrival per claim
@@ -726,13 +733,11 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
         stage_act_q8_K<MT, kF32>(p, smem, tid);
     consumer_sync();
     // Programmatic dependent launch: the next launch on the stream may start
-    // once every CTA of this one has its activations staged (it needs the
-    // other half of the SM's shared memory).  Triggering only now keeps the
-    // next launch's weight prefetch from competing with this launch's
-    // activation loads; only that prefetch runs before its
-    // griddepcontrol.wait, activations and outputs stay ordered after this
-    // grid as usual.
-    if (p.overlap && tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // once every CTA of this one has its activations staged; its CTAs take
+    // SMs as this launch's CTAs exit and prefetch their weights.  Only that
+    // prefetch runs before its griddepcontrol.wait; activations and outputs
+    // stay ordered after this grid as usual.
+    if (!PFNG_GEMV_EARLY_TRIGGER && p.overlap && tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     ActRegs<(RG > 0 ? RG : 1)> ar;
     if constexpr (RG > 0) {
