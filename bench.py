@@ -208,11 +208,13 @@ def reference_arm(args) -> int:
     return 0
 
 
-def workload_config():
+def workload_config(layout: str = "ggml"):
     return {
         "workload": "configs[1]: q4_0 x q8_0 decode GEMV, M=1, (N,K) = (4096,4096) + (11008,4096), "
                     "activation quantized on device (fused)",
         "m": 1, "n": list(N_DIMS), "k": K_DIM, "weight_type": "q4_0", "activation_type": "q8_0",
+        "weight_layout": "ggml block_q4_0 rows" if layout == "ggml" else
+                         "q4_0 planar rows (same bytes, repacked once on the device before timing)",
         "l2": "inputs larger than L2: weights rotate over copies totalling > 4x the 126 MB L2",
     }
 
@@ -234,13 +236,18 @@ def ours(args) -> int:
     torch.cuda.set_stream(stream)  # graph capture needs a non-default stream
     copies = max(2, -(-4 * L2_BYTES // step_weight_bytes()))
     gen = torch.Generator(device="cuda").manual_seed(1 + rank)
+    planar = args.layout == "planar"
+    wt = pb.Q4_0_PLANAR if planar else pb.Q4_0
     weights = []
     for _ in range(copies):
         per = []
         for n in N_DIMS:
             wf = torch.randn((n, K_DIM), generator=gen, device="cuda", dtype=torch.float32)
-            per.append(pb.quantize_q4_0(wf))
+            q = pb.quantize_q4_0(wf)
             del wf
+            # planar: the one-time repack a reference adapter does in prepare
+            per.append(pb.pack_q4_0_planar(q, n, K_DIM) if planar else q)
+            del q
         weights.append(per)
     x = torch.randn((1, K_DIM), generator=torch.Generator(device="cuda").manual_seed(2), device="cuda")
     outs = [torch.empty((1, n), device="cuda") for n in N_DIMS]
@@ -251,7 +258,7 @@ def ours(args) -> int:
     # The weights are constant, so consecutive steps may overlap: each launch
     # starts streaming its weights while the previous one drains
     # (PFNG_B200_OVERLAP_WEIGHTS); activations and outputs stay ordered.
-    calls = [pb.GroupedCall(pb.Q4_0, weights[r], N_DIMS, outs, x, overlap_weights=True) for r in range(copies)]
+    calls = [pb.GroupedCall(wt, weights[r], N_DIMS, outs, x, overlap_weights=True) for r in range(copies)]
 
     def step(i: int, xin=None):
         calls[i % copies](x=xin, stream=stream)
@@ -312,7 +319,7 @@ def ours(args) -> int:
     for n in N_DIMS:
         cols.append(out_dev[:, o:o + n])
         o += n
-    e2e_calls = [pb.GroupedCall(pb.Q4_0, weights[r], N_DIMS, cols, x_dev, overlap_weights=True) for r in range(copies)]
+    e2e_calls = [pb.GroupedCall(wt, weights[r], N_DIMS, cols, x_dev, overlap_weights=True) for r in range(copies)]
 
     def e2e_step(i):
         x_dev.copy_(x_host, non_blocking=True)
@@ -352,12 +359,14 @@ def ours(args) -> int:
             "warmup": args.warmup, "ms_per_step": elapsed_max / args.steps * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8/int32 dot, fp32 fold (q4_0 x q8_0)",
             "data": "synthetic: seeded N(0,1) fp32 weights (quantized to q4_0 on device) and activations",
-            "config": dict(workload_config(), parallelism=f"replicas x{world}" if world > 1 else "single GPU",
+            "config": dict(workload_config(args.layout), parallelism=f"replicas x{world}" if world > 1 else "single GPU",
                            weight_copies=copies, weight_bytes_resident=copies * step_weight_bytes()),
             "weight_GBps": world * args.steps * step_weight_bytes() / elapsed_max / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": profile_traffic("gemv_q4_0_decode"),
-                         "kernel": "gemv_kernel<q4_0, m=1, fp32 activations>, both matrices in one launch",
+                         "frac": achieved / peak,
+                         "traffic": profile_traffic("gemv_q4_0_planar_decode" if planar else "gemv_q4_0_decode"),
+                         "kernel": f"gemv_kernel<{'q4_0 planar' if planar else 'q4_0'}, m=1, fp32 activations>, "
+                                   "both matrices in one launch",
                          "bytes_per_launch": bytes_launch, "avg_launch_us": avg_launch * 1e6,
                          "timing": "CUDA events around K back-to-back launches on the launching stream, / K",
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
@@ -561,6 +570,8 @@ def main() -> int:
     ap.add_argument("--workload", choices=["decode", "prefill", "llama"], default="decode",
                     help="decode: configs[1] (the bench line); prefill: configs[0]/[2]/[3]; llama: configs[4]")
     ap.add_argument("--wtype", choices=["q4_0", "q4_K", "iq2_xxs"], default="q4_0")
+    ap.add_argument("--layout", choices=["ggml", "planar"], default="ggml",
+                    help="decode: q4_0 weights as ggml blocks or repacked once into the planar row layout")
     ap.add_argument("--m", type=int, default=None)
     ap.add_argument("--n", type=int, default=1536)
     ap.add_argument("--k", type=int, default=1536)

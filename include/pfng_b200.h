@@ -57,6 +57,10 @@ extern "C" {
 #define PFNG_B200_Q4_0 0
 #define PFNG_B200_Q4_K 1
 #define PFNG_B200_IQ2_XXS 2
+/* q4_0 weights in the planar row layout (see pfng_b200_pack_q4_0_planar);
+ * activations q8_0 as for PFNG_B200_Q4_0.  Accepted wherever a weight type
+ * code is taken (workspace queries, pfng_b200_compute_grouped). */
+#define PFNG_B200_Q4_0_PLANAR 3
 
 /* Library version, and a readable name for a status code. */
 int pfng_b200_version(void);
@@ -133,6 +137,30 @@ int pfng_b200_compute_iq2_xxs(const void *w, const float *x, int64_t ldx, float 
 int pfng_b200_compute_grouped(int wtype, int count, const void *const *w, const int64_t *n, float *const *c,
                               const int64_t *ldc, const float *x, int64_t ldx, int64_t m, int64_t k, unsigned flags,
                               void *stream);
+
+/* ---- q4_0 in the planar row layout ---------------------------------------
+ * A weight row of nb = k / 32 blocks holds the 16-byte nibble fields of
+ * blocks 0..nb-1 (block j at byte 16 j), then their fp16 scales (block j at
+ * byte 16 nb + 2 j): the same 18 nb bytes and row stride as block_q4_0,
+ * reordered so that the kernels read every nibble field with one aligned
+ * 16-byte load.  Requires k % 256 == 0 and a 16-byte aligned planar buffer
+ * (PFNG_B200_ERR_SHAPE / PFNG_B200_ERR_ALIGNMENT otherwise); source and
+ * destination must not overlap.  unpack(pack(W)) == W byte for byte.
+ * The reference's adapters repack W once in KernelCallbacks::prepare
+ * (kernels/common/types.h:9-63;
+ * kernels/q4_0-q8_0-IME-m8b/implementations/smt-ime2/adapter.cpp:95-112);
+ * this is that step for these kernels, run on the device.
+ * The *_q4_0p entry points take planar W and behave as their q4_0
+ * counterparts (same arguments, paths, workspace sizes and checks): integer
+ * partials bit-identical, fp32 outputs within the same bound. */
+int pfng_b200_pack_q4_0_planar(const void *w, void *w_planar, int64_t n, int64_t k, void *stream);
+int pfng_b200_unpack_q4_0_planar(const void *w_planar, void *w, int64_t n, int64_t k, void *stream);
+int pfng_b200_mm_q4_0p_q8_0(const void *w_planar, const void *a, float *c, int64_t m, int64_t n, int64_t k,
+                            int64_t ldc, void *workspace, size_t workspace_bytes, int path, void *stream);
+int pfng_b200_compute_q4_0p(const void *w_planar, const float *x, int64_t ldx, float *c, int64_t m, int64_t n,
+                            int64_t k, int64_t ldc, void *workspace, size_t workspace_bytes, int path, void *stream);
+int pfng_b200_partials_q4_0p_q8_0(const void *w_planar, const void *a, int32_t *out, int64_t m, int64_t n, int64_t k,
+                                  void *workspace, size_t workspace_bytes, int path, void *stream);
 
 /* ---- integer partials (verification) ------------------------------------
  * out: int32 [m][n][k / 32], the integer dot product of every 32-value

@@ -470,3 +470,28 @@ void oracle_bound_iq2_xxs_q8_K(const void *w, const void *a, double *out, size_t
             out[i * n + j] = total;
         }
 }
+
+/* ---- q4_0 planar row layout (a permutation of each row's bytes) ---------- */
+void oracle_pack_q4_0_planar(const void *w, void *w_planar, size_t n, size_t k) {
+    const size_t nb = k / ORACLE_QK4_0, rb = nb * sizeof(oracle_block_q4_0);
+    for (size_t row = 0; row < n; ++row) {
+        const oracle_block_q4_0 *src = (const oracle_block_q4_0 *)((const uint8_t *)w + row * rb);
+        uint8_t *dst = (uint8_t *)w_planar + row * rb;
+        for (size_t j = 0; j < nb; ++j) {
+            memcpy(dst + 16 * j, src[j].qs, 16);
+            memcpy(dst + 16 * nb + 2 * j, &src[j].d, 2);
+        }
+    }
+}
+
+void oracle_unpack_q4_0_planar(const void *w_planar, void *w, size_t n, size_t k) {
+    const size_t nb = k / ORACLE_QK4_0, rb = nb * sizeof(oracle_block_q4_0);
+    for (size_t row = 0; row < n; ++row) {
+        const uint8_t *src = (const uint8_t *)w_planar + row * rb;
+        oracle_block_q4_0 *dst = (oracle_block_q4_0 *)((uint8_t *)w + row * rb);
+        for (size_t j = 0; j < nb; ++j) {
+            memcpy(dst[j].qs, src + 16 * j, 16);
+            memcpy(&dst[j].d, src + 16 * nb + 2 * j, 2);
+        }
+    }
+}

@@ -92,6 +92,15 @@ void oracle_bound_q4_0_q8_0(const void *w, const void *a, double *out, size_t m,
 void oracle_bound_q4_K_q8_K(const void *w, const void *a, double *out, size_t m, size_t n, size_t k);
 void oracle_bound_iq2_xxs_q8_K(const void *w, const void *a, double *out, size_t m, size_t n, size_t k);
 
+/* q4_0 planar row layout of the B200 library (no reference counterpart: a
+ * byte permutation of block_q4_0 rows, the device form of the W repack the
+ * reference's adapters do in prepare, kernels/common/types.h:9-63).  Row of
+ * nb = k / 32 blocks: nibble fields of blocks 0..nb-1 at 16 j, then their
+ * fp16 scales at 16 nb + 2 j.  Matmul parity on planar W is checked against
+ * oracle_mm_q4_0_q8_0 on the ggml-layout W. */
+void oracle_pack_q4_0_planar(const void *w, void *w_planar, size_t n, size_t k);
+void oracle_unpack_q4_0_planar(const void *w_planar, void *w, size_t n, size_t k);
+
 /* iq2_xxs decode of one 32-value group (kernels/common/iq2_xxs.h:29-41, with
  * the full 256-entry grid of the upstream kernel's tables.h:8-73). */
 void oracle_iq2_xxs_decode_group(const uint8_t *packed8, int8_t *values32, int *scale);

@@ -67,18 +67,27 @@ DeviceInfo *current_info() {
 
 bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
-int block_k(int wtype) { return wtype == PFNG_B200_Q4_0 ? 32 : 256; }
-size_t a_block_bytes(int wtype) { return wtype == PFNG_B200_Q4_0 ? kQ8_0Bytes : kQ8_KBytes; }
-uintptr_t w_align(int wtype) { return wtype == PFNG_B200_Q4_K ? 4 : 2; }
-uintptr_t a_align(int wtype) { return wtype == PFNG_B200_Q4_0 ? 2 : 4; }
+static_assert(PFNG_B200_Q4_0 == kWQ4_0 && PFNG_B200_Q4_K == kWQ4_K && PFNG_B200_IQ2_XXS == kWIQ2 &&
+                  PFNG_B200_Q4_0_PLANAR == kWQ4_0P,
+              "weight type codes");
+bool valid_wtype(int wtype) { return wtype >= PFNG_B200_Q4_0 && wtype <= PFNG_B200_Q4_0_PLANAR; }
+// q4_0 (either layout) pairs with q8_0 activations, the others with q8_K
+bool q8_0_act(int wtype) { return wtype == PFNG_B200_Q4_0 || wtype == PFNG_B200_Q4_0_PLANAR; }
+int block_k(int wtype) { return q8_0_act(wtype) ? 32 : 256; }
+size_t a_block_bytes(int wtype) { return q8_0_act(wtype) ? kQ8_0Bytes : kQ8_KBytes; }
+uintptr_t w_align(int wtype) {
+    return wtype == PFNG_B200_Q4_0_PLANAR ? 16 : wtype == PFNG_B200_Q4_K ? 4 : 2;
+}
+uintptr_t a_align(int wtype) { return q8_0_act(wtype) ? 2 : 4; }
 
 // Common shape/pointer checks for the matmul-family entry points.
 int check_mm(int wtype, const void *w, const void *a_or_x, const void *out, int64_t m, int64_t n, int64_t k,
              int64_t ldc, int64_t ldx, bool f32_input, bool partials, int path) {
-    if (wtype < 0 || wtype > 2) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    if (!valid_wtype(wtype)) return PFNG_B200_ERR_INVALID_ARGUMENT;
     if (m < 0 || n < 0 || k < 0) return PFNG_B200_ERR_INVALID_ARGUMENT;
     if (path < PFNG_B200_PATH_AUTO || path > PFNG_B200_PATH_SIMPLE) return PFNG_B200_ERR_INVALID_ARGUMENT;
     if (k % block_k(wtype) != 0) return PFNG_B200_ERR_SHAPE;
+    if (wtype == PFNG_B200_Q4_0_PLANAR && k % 256 != 0) return PFNG_B200_ERR_SHAPE;
     if (!partials && m > 0 && ldc < n) return PFNG_B200_ERR_SHAPE;
     if (f32_input && m > 0 && ldx < k) return PFNG_B200_ERR_SHAPE;
     if (m == 0 || n == 0) return PFNG_B200_OK;
@@ -168,9 +177,9 @@ int run_matmul(int wtype, const void *w, const void *a, const float *x, int64_t 
         g.k = k;
         e = launch_gemv(g, s);
     } else if (resolved == PFNG_B200_PATH_MMA) {
-        const int qk = wtype == PFNG_B200_Q4_0 ? 32 : 256;
+        const int qk = block_k(wtype);
         const SplitA sa = split_a_carve(workspace, m, k, qk);
-        if (wtype == PFNG_B200_Q4_0)
+        if (q8_0_act(wtype))
             e = f32 ? launch_quantize_q8_0_split(x, ldx, sa, m, k, s) : launch_convert_q8_0_split(a, sa, m, k, s);
         else
             e = f32 ? launch_quantize_q8_K_split(x, ldx, sa, m, k, s) : launch_convert_q8_K_split(a, sa, m, k, s);
@@ -182,8 +191,8 @@ int run_matmul(int wtype, const void *w, const void *a, const float *x, int64_t 
         const void *araw = a;
         if (f32) {
             void *buf = align_ptr(workspace, 256);
-            e = wtype == PFNG_B200_Q4_0 ? launch_quantize_q8_0(x, ldx, buf, m, k, s)
-                                        : launch_quantize_q8_K(x, ldx, buf, m, k, s);
+            e = q8_0_act(wtype) ? launch_quantize_q8_0(x, ldx, buf, m, k, s)
+                                : launch_quantize_q8_K(x, ldx, buf, m, k, s);
             araw = buf;
         }
         if (e == cudaSuccess) {
@@ -195,7 +204,7 @@ int run_matmul(int wtype, const void *w, const void *a, const float *x, int64_t 
 }
 
 size_t query_workspace(int wtype, int64_t m, int64_t n, int64_t k, int path, bool f32) {
-    if (wtype < 0 || wtype > 2 || m <= 0 || n <= 0 || k <= 0) return 0;
+    if (!valid_wtype(wtype) || m <= 0 || n <= 0 || k <= 0) return 0;
     if (path == PFNG_B200_PATH_AUTO) {
         // AUTO may take the tensor-core or the simple path depending on the
         // pointers' alignment, so ask for what either needs.
@@ -365,7 +374,7 @@ int pfng_b200_compute_iq2_xxs(const void *w, const float *x, int64_t ldx, float 
 int pfng_b200_compute_grouped(int wtype, int count, const void *const *w, const int64_t *n, float *const *c,
                               const int64_t *ldc, const float *x, int64_t ldx, int64_t m, int64_t k, unsigned flags,
                               void *stream) {
-    if (wtype < 0 || wtype > 2 || count < 1 || !w || !n || !c || !ldc) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    if (!valid_wtype(wtype) || count < 1 || !w || !n || !c || !ldc) return PFNG_B200_ERR_INVALID_ARGUMENT;
     if (flags & ~static_cast<unsigned>(PFNG_B200_OVERLAP_WEIGHTS)) return PFNG_B200_ERR_INVALID_ARGUMENT;
     if (count > kGemvMaxGroup) return PFNG_B200_ERR_UNSUPPORTED;
     for (int g = 0; g < count; ++g) {
@@ -418,6 +427,52 @@ int pfng_b200_partials_iq2_xxs_q8_K(const void *w, const void *a, int32_t *out, 
                                     void *workspace, size_t workspace_bytes, int path, void *stream) {
     return run_matmul(PFNG_B200_IQ2_XXS, w, a, nullptr, 0, nullptr, n, out, m, n, k, workspace, workspace_bytes,
                       path, static_cast<cudaStream_t>(stream));
+}
+
+int pfng_b200_mm_q4_0p_q8_0(const void *w_planar, const void *a, float *c, int64_t m, int64_t n, int64_t k,
+                            int64_t ldc, void *workspace, size_t workspace_bytes, int path, void *stream) {
+    return run_matmul(PFNG_B200_Q4_0_PLANAR, w_planar, a, nullptr, 0, c, ldc, nullptr, m, n, k, workspace,
+                      workspace_bytes, path, static_cast<cudaStream_t>(stream));
+}
+
+int pfng_b200_compute_q4_0p(const void *w_planar, const float *x, int64_t ldx, float *c, int64_t m, int64_t n,
+                            int64_t k, int64_t ldc, void *workspace, size_t workspace_bytes, int path, void *stream) {
+    return run_matmul(PFNG_B200_Q4_0_PLANAR, w_planar, nullptr, x, ldx, c, ldc, nullptr, m, n, k, workspace,
+                      workspace_bytes, path, static_cast<cudaStream_t>(stream));
+}
+
+int pfng_b200_partials_q4_0p_q8_0(const void *w_planar, const void *a, int32_t *out, int64_t m, int64_t n, int64_t k,
+                                  void *workspace, size_t workspace_bytes, int path, void *stream) {
+    return run_matmul(PFNG_B200_Q4_0_PLANAR, w_planar, a, nullptr, 0, nullptr, n, out, m, n, k, workspace,
+                      workspace_bytes, path, static_cast<cudaStream_t>(stream));
+}
+
+// Shared checks of pack / unpack: raw side 2-byte aligned, planar side 16.
+static int planar_copy(bool to_planar, const void *src, void *dst, int64_t n, int64_t k, void *stream) {
+    if (n < 0 || k < 0) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    if (k % 256 != 0) return PFNG_B200_ERR_SHAPE;
+    if (n == 0 || k == 0) return PFNG_B200_OK;
+    if (!src || !dst) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    const void *raw = to_planar ? src : dst;
+    const void *planar = to_planar ? dst : src;
+    if (!aligned(raw, 2) || !aligned(planar, 16)) return PFNG_B200_ERR_ALIGNMENT;
+    const uintptr_t bytes = static_cast<uintptr_t>(n) * static_cast<uintptr_t>(k / 32) * kQ4_0Bytes;
+    const uintptr_t a0 = reinterpret_cast<uintptr_t>(src), b0 = reinterpret_cast<uintptr_t>(dst);
+    if (a0 < b0 + bytes && b0 < a0 + bytes) return PFNG_B200_ERR_INVALID_ARGUMENT;  // overlapping buffers
+    DeviceInfo *info = nullptr;
+    int st = device_info(&info);
+    if (st != PFNG_B200_OK) return st;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return status_of(to_planar ? launch_pack_q4_0_planar(src, dst, n, k, s)
+                               : launch_unpack_q4_0_planar(src, dst, n, k, s));
+}
+
+int pfng_b200_pack_q4_0_planar(const void *w, void *w_planar, int64_t n, int64_t k, void *stream) {
+    return planar_copy(true, w, w_planar, n, k, stream);
+}
+
+int pfng_b200_unpack_q4_0_planar(const void *w_planar, void *w, int64_t n, int64_t k, void *stream) {
+    return planar_copy(false, w_planar, w, n, k, stream);
 }
 
 int pfng_b200_shard_rows(int64_t n, int world, int rank, int64_t granule, int64_t *begin, int64_t *end) {

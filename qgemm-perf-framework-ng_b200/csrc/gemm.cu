@@ -1,7 +1,8 @@
 // gemm.cu -- batched-m block-quantized matmul on the int8 tensor cores.
 //
-// C[m][n] = A[m][k] . W[n][k]^T with W in the raw ggml layout and A in the
-// split layout (int8 rows + per-block scales) produced by quantize.cu.
+// C[m][n] = A[m][k] . W[n][k]^T with W in the raw ggml layout (or q4_0 in
+// the planar row layout) and A in the split layout (int8 rows + per-block
+// scales) produced by quantize.cu.
 // Semantics: compute_q4_0 / compute_q4_K / compute_iq2_xxs,
 // bench/llama_reference/llama_reference.cpp:113-205.
 //
@@ -43,6 +44,9 @@ constexpr bool kTcDefault = false;
 constexpr int kStages = 3;
 constexpr uint32_t kMagicBits = 0x4B400000u;  // float 12582912 = 2^23 + 2^22
 constexpr float kMagic = 12582912.0f;
+// true when the activations are q8_0 (one fp32 scale per 32 values)
+template <int WT>
+constexpr bool kQ8_0Act = WT == kWQ4_0 || WT == kWQ4_0P;
 constexpr uint32_t kWRowSlot = 160;          // >= 144 raw bytes + 8 window slack, multiple of 16
 constexpr int kAScaleStride = 12;
 
@@ -151,16 +155,27 @@ PFNG_DEV void load_stage(const GemmParams &p, const Smem<C> &sm, int s, int64_t 
     }
     if (tid < C::BM * 2) {
         const int row = tid >> 1, half = tid & 1;
-        const void *src = WT == 0 ? static_cast<const void *>(p.a.d + (m0 + row) * (K / 32) + ks * 8 + half * 4)
+        const void *src = kQ8_0Act<WT> ? static_cast<const void *>(p.a.d + (m0 + row) * (K / 32) + ks * 8 + half * 4)
                                   : static_cast<const void *>(p.a.aux + (m0 + row) * (K / 32) + ks * 8 + half * 4);
         cp_async16(sm.a_scale(s) + row * kAScaleStride + half * 4, src, 16);
     }
-    if constexpr (WT != 0) {
+    if constexpr (!kQ8_0Act<WT>) {
         if (tid < C::BM) cp_async4(sm.a_d8k(s) + tid, p.a.d + (m0 + tid) * (K / 256) + ks, 4);
     }
     // raw W: BN rows x step_bytes, each row into a kWRowSlot-byte slot
     uint8_t *wr = sm.w_raw(s);
-    if (p.w_vec16) {
+    if constexpr (WT == kWQ4_0P) {
+        // planar rows: the k-step's 8 nibble fields (128 B) into slot bytes
+        // 0..127, their 8 fp16 scales (16 B) into bytes 128..143
+        for (int q = tid; q < C::BN * 9; q += kThreads) {
+            const int row = q / 9, ch = q % 9;
+            const int64_t n = n0 + row;
+            const bool ok = n < p.n;
+            const int64_t off = ch < 8 ? ks * 128 + ch * 16 : K / 2 + ks * 16;
+            const uint8_t *src = p.w + (ok ? n * p.row_bytes + off : 0);
+            cp_async16(wr + row * kWRowSlot + ch * 16, src, ok ? 16u : 0u);
+        }
+    } else if (p.w_vec16) {
         const int chunks = static_cast<int>(p.step_bytes / 16);
         for (int q = tid; q < C::BN * chunks; q += kThreads) {
             const int row = q / chunks, ch = q % chunks;
@@ -210,10 +225,16 @@ PFNG_DEV void decode_w(const GemmParams &p, const Smem<C> &sm, int s, int64_t ks
         const int row = task >> 3, u = task & 7;
         const uint32_t mis = p.w_vec16 ? 0u : static_cast<uint32_t>((n0 + row) * p.row_bytes + ks * p.step_bytes) & 3u;
         const uint32_t base = row * kWRowSlot + mis;
-        if constexpr (WT == 0) {
+        if constexpr (WT == kWQ4_0 || WT == kWQ4_0P) {
             // block u of the row
             uint32_t q[4], dbits;
-            load_q4_0_block_smem(wr, base + 18u * u, q, dbits);
+            if constexpr (WT == kWQ4_0) {
+                load_q4_0_block_smem(wr, base + 18u * u, q, dbits);
+            } else {
+                const uint4 v = *reinterpret_cast<const uint4 *>(wr + base + 16u * u);
+                q[0] = v.x, q[1] = v.y, q[2] = v.z, q[3] = v.w;
+                dbits = *reinterpret_cast<const uint16_t *>(wr + base + 128u + 2u * u);
+            }
             uint4 lo, hi;
             lo.x = __vsub4(q[0] & 0x0f0f0f0fu, 0x08080808u);
             lo.y = __vsub4(q[1] & 0x0f0f0f0fu, 0x08080808u);
@@ -226,7 +247,7 @@ PFNG_DEV void decode_w(const GemmParams &p, const Smem<C> &sm, int s, int64_t ks
             store_pair(bt, row, 2 * u, lo, 2 * u + 1, hi, u >= 4);
             const float dw = f16_bits_to_f32(dbits);
             fold[u * C::BN + row] = make_float2(dw, -kMagic * dw);
-        } else if constexpr (WT == 1) {
+        } else if constexpr (WT == kWQ4_K) {
             // u = (nibble pair pr, half h): 16 payload bytes -> 16 values of sub-blocks 2pr and 2pr+1
             const uint8_t *blk = wr + base;
             const int pr = u >> 1, h = u & 1;
@@ -287,7 +308,7 @@ PFNG_DEV void decode_w(const GemmParams &p, const Smem<C> &sm, int s, int64_t ks
             fold[u * C::BN + row] = make_float2(sv, -kMagic * sv);
         }
     }
-    if constexpr (WT == 1) {
+    if constexpr (WT == kWQ4_K) {
         // A side: bsum32 of each row split into 6-bit low bytes and high bytes
         for (int r = tid; r < C::BM; r += kThreads) {
             const int32_t *bsum = reinterpret_cast<const int32_t *>(sm.a_scale(s)) + r * kAScaleStride;
@@ -335,7 +356,7 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
     const int64_t KT = p.k / BK;
     constexpr int MT = C::MT, NT = C::NT;
 
-    if constexpr (WT == 2) {
+    if constexpr (WT == kWIQ2) {
         uint2 *grid = sm.grid();
         for (int i = tid; i < 256; i += kThreads) {
             const uint32_t code = pfng_iq2xxs_grid_codes[i];
@@ -380,7 +401,7 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
         const int8_t *bt = sm.b_tile();
         // activation block scales of this thread's rows (q8_K: one per 256 block)
         float da8k[MT][2];
-        if constexpr (WT != 0) {
+        if constexpr (!kQ8_0Act<WT>) {
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -428,7 +449,7 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
                 for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
                     for (int h = 0; h < 2; ++h)
-                        da[mt][h] = WT == 0 ? sm.a_scale(s)[(wm * C::WM + mt * 16 + g + 8 * h) * kAScaleStride + kb]
+                        da[mt][h] = kQ8_0Act<WT> ? sm.a_scale(s)[(wm * C::WM + mt * 16 + g + 8 * h) * kAScaleStride + kb]
                                             : da8k[mt][h];
                 const float2 *fold = sm.fold() + kb * C::BN;
 #pragma unroll
@@ -451,7 +472,7 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
             }
         }
 
-        if constexpr (!kPartials && WT == 1) {
+        if constexpr (!kPartials && WT == kWQ4_K) {
             // once per 256 block: acc -= a_d * dmin * sum_sb min_sb * bsum_sb
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt)
@@ -502,7 +523,8 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
 
 int64_t row_bytes_of(int wtype, int64_t k) {
     switch (wtype) {
-    case 0: return k / 32 * kQ4_0Bytes;
+    case kWQ4_0:
+    case kWQ4_0P: return k / 32 * kQ4_0Bytes;
     case 1: return k / 256 * kQ4_KBytes;
     default: return k / 256 * kIQ2Bytes;
     }
@@ -557,7 +579,7 @@ bool gemm_supported(int wtype, int64_t m, int64_t n, int64_t k, const void *w) {
 // environment variable PFNG_B200_GEMM is "mma" (or the shape is unsupported);
 // "tc" / "mma" select either kernel explicitly, for comparisons.
 static bool use_tc(const GemmArgs &args) {
-    if (args.wtype != 0 || args.partials) return false;
+    if (args.wtype != kWQ4_0 || args.partials) return false;
     const char *e = std::getenv("PFNG_B200_GEMM");
     const bool want = e ? std::strcmp(e, "tc") == 0 : kTcDefault;
     return want && gemm_tc_supported(args.wtype, args.m, args.n, args.k, args.w);
@@ -580,9 +602,10 @@ cudaError_t launch_gemm(const GemmArgs &args, cudaStream_t s) {
     p.w_vec16 = (p.row_bytes % 16 == 0 && p.step_bytes % 16 == 0) ? 1 : 0;
     const bool part = args.partials != nullptr;
     switch (args.wtype) {
-    case 0: return part ? launch_tile<0, true>(p, s) : launch_tile<0, false>(p, s);
-    case 1: return part ? launch_tile<1, true>(p, s) : launch_tile<1, false>(p, s);
-    default: return part ? launch_tile<2, true>(p, s) : launch_tile<2, false>(p, s);
+    case kWQ4_0: return part ? launch_tile<kWQ4_0, true>(p, s) : launch_tile<kWQ4_0, false>(p, s);
+    case kWQ4_K: return part ? launch_tile<kWQ4_K, true>(p, s) : launch_tile<kWQ4_K, false>(p, s);
+    case kWQ4_0P: return part ? launch_tile<kWQ4_0P, true>(p, s) : launch_tile<kWQ4_0P, false>(p, s);
+    default: return part ? launch_tile<kWIQ2, true>(p, s) : launch_tile<kWIQ2, false>(p, s);
     }
 }
 

@@ -14,17 +14,20 @@
 //   * the consumer warps first stage the activation rows in shared memory
 //     (either the caller's q8 blocks, or fp32 rows quantized in place with
 //     the same rounding as the standalone quantizer), then each repeatedly
-//     claims the next PAIR of rows of the CTA's tile sequence (a shared
-//     counter, so warps that finish early take more work) and processes it:
-//     lanes walk the rows' blocks, unpack 4-bit / grid weights to int8, dot
-//     them against the activations with dp4a, fold the integer partials with
-//     the block scales in fp32 and reduce across the warp.  For q4_0 at
-//     m = 1 a warp copies its pair's weights to registers and releases the
-//     pair before computing, so stages return to the producer early.
-//   Measured on B200 (decode step of two matrices, 35 MB): 12-16 consumer
-//   warps with 8-row (18 KB) tiles and one CTA per SM stream fastest; fewer
-//   warps leave the consumers latency-bound, more add staging and scheduling
-//   cost, and 4-row tiles double the producer's per-tile work.
+//     claims the next four rows of the CTA's tile sequence (a shared
+//     counter, so warps that finish early take more work) and processes
+//     them: lanes walk the rows' blocks, unpack 4-bit / grid weights to
+//     int8, dot them against the activations with dp4a, fold the integer
+//     partials with the block scales in fp32 and reduce across the warp.
+//     For q4_0 at m = 1 a warp copies its claim's four rows of weights to
+//     registers and releases the stage before computing, so stages return to
+//     the producer early, and reduces the four rows in one butterfly.
+//   Measured on B200 (decode step of two matrices, 35 MB): 11 consumer warps
+//   with 8-row (18 KB) tiles and one CTA per SM stream fastest (7.3 us per
+//   step).  The CTA's 12 warps put at most 3 on each SM sub-partition, which
+//   leaves 168 registers per thread for a claim's four rows in registers;
+//   with 13 or more warps the cap is 128 and the four-row path spills
+//   (9.1 us).  Two-row claims with 12 warps: 7.8 us; 4-row tiles: 10.5 us.
 //
 // q4_0 lane mapping: lane l of a warp takes the block PAIR (2l, 2l+1) of each
 // group of 64 blocks.  A pair is 36 contiguous bytes = 9 aligned words at word
@@ -45,7 +48,7 @@ namespace pfng {
 namespace {
 
 #ifndef PFNG_GEMV_CONSUMER_WARPS
-#define PFNG_GEMV_CONSUMER_WARPS 12
+#define PFNG_GEMV_CONSUMER_WARPS 11
 #endif
 #ifndef PFNG_GEMV_CTAS_PER_SM
 #define PFNG_GEMV_CTAS_PER_SM 1
@@ -54,15 +57,33 @@ constexpr int kConsumerWarps = PFNG_GEMV_CONSUMER_WARPS;
 constexpr int kCtasPerSm = PFNG_GEMV_CTAS_PER_SM;  // 2: half the shared memory, so two launches can overlap
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kGemvThreads = kConsumerThreads + 32;
-constexpr int kMaxStages = 32;
+#ifndef PFNG_GEMV_MAX_STAGES
+#define PFNG_GEMV_MAX_STAGES 32
+#endif
+constexpr int kMaxStages = PFNG_GEMV_MAX_STAGES;
 constexpr int kPairRows = 2;         // rows a warp processes together
 #ifndef PFNG_GEMV_CLAIM_ROWS
 #define PFNG_GEMV_CLAIM_ROWS 4
 #endif
 constexpr int kClaimRows = PFNG_GEMV_CLAIM_ROWS;  // rows a warp claims at a time (pairs of rows)
+#ifndef PFNG_GEMV_CLAIM4
+#define PFNG_GEMV_CLAIM4 1  // m = 1: a claim's four rows computed together
+#endif
+#ifndef PFNG_GEMV_FOLD2
+#define PFNG_GEMV_FOLD2 1  // m = 1 four-row path: bias-started dp4a chains and packed fmas
+#endif
 #ifndef PFNG_GEMV_EARLY_TRIGGER
 #define PFNG_GEMV_EARLY_TRIGGER 0
 #endif
+// Copies a CTA may keep in flight (issued, not yet landed); at least the
+// ring depth means no limit beyond the ring.  Measured on B200 (decode step,
+// 35 MB): 2 / 4 / 8 in flight 9.8 / 8.9 / 8.5 us per step, unlimited 7.8 --
+// under a full-chip stream the loaded HBM latency is long enough that every
+// tile of the ring has to be requested at once to keep HBM busy.
+#ifndef PFNG_GEMV_INFLIGHT
+#define PFNG_GEMV_INFLIGHT 32
+#endif
+constexpr int kInflight = PFNG_GEMV_INFLIGHT;
 #ifndef PFNG_GEMV_TILE_ROWS
 #define PFNG_GEMV_TILE_ROWS 8
 #endif
@@ -119,8 +140,8 @@ PFNG_DEV int dp4a_us(uint32_t a, int b, int c) {
 
 // sum over 16 weights (4 words of nibbles: low nibbles are k 0..15, high
 // nibbles k 16..31 of a q4_0 block) times the activations, without the -8.
-PFNG_DEV int nibble_dot(const uint32_t (&q)[4], const uint4 &alo, const uint4 &ahi) {
-    int lo = dp4a_us(q[0] & 0x0f0f0f0fu, static_cast<int>(alo.x), 0);
+PFNG_DEV int nibble_dot(const uint32_t (&q)[4], const uint4 &alo, const uint4 &ahi, int bias = 0) {
+    int lo = dp4a_us(q[0] & 0x0f0f0f0fu, static_cast<int>(alo.x), bias);
     int hi = dp4a_us(q[0] & 0xf0f0f0f0u, static_cast<int>(ahi.x), 0);
     lo = dp4a_us(q[1] & 0x0f0f0f0fu, static_cast<int>(alo.y), lo);
     hi = dp4a_us(q[1] & 0xf0f0f0f0u, static_cast<int>(ahi.y), hi);
@@ -145,14 +166,32 @@ PFNG_DEV uint32_t q4_0_act_qs_offset(int m, int groups, int j, int byte_in_block
     return static_cast<uint32_t>((((m * groups + t) * 4 + c) * 32 + l) * 16 + (byte_in_block & 15));
 }
 
-template <int MT, bool kF32>
+// Planar-layout weights (see rows_q4_0p_reg): per row m and group t of 32
+// blocks, chunk c (bytes 16 c .. 16 c + 15 of block 32 t + l) at lane slot l.
+PFNG_DEV uint32_t q4_0p_act_qs_offset(int m, int groups, int j, int byte_in_block) {
+    const int t = j >> 5, l = j & 31, c = byte_in_block >> 4;
+    return static_cast<uint32_t>((((m * groups + t) * 2 + c) * 32 + l) * 16 + (byte_in_block & 15));
+}
+
+constexpr int kMagicBits = 0x4B400000;  // float 12582912 = 2^23 + 2^22
+constexpr float kMagic = 12582912.0f;
+
+// kPlanar: the planar layout's staging; its per-block integer is the fold
+// bias 0x4B400000 - 8 * sum(q) instead of 8 * sum(q).
+template <int MT, bool kF32, bool kPlanar>
 PFNG_DEV void stage_act_q8_0(const GemvParams &p, uint8_t *smem, int tid) {
     const int nb = p.k / 32;
-    const int nbp = p.groups * 64;
+    const int nbp = p.groups * (kPlanar ? 32 : 64);
     uint8_t *qs = smem + p.act_offset;
-    float *d = reinterpret_cast<float *>(qs + MT * p.groups * 2048);
+    float *d = reinterpret_cast<float *>(qs + MT * nbp * 32);
     int32_t *s8 = reinterpret_cast<int32_t *>(d + MT * nbp);
-    const int total = MT * nbp;  // a multiple of 64
+    const int total = MT * nbp;  // a multiple of 32
+    auto qs_offset = [&](int row, int j, int byte) {
+        return kPlanar ? q4_0p_act_qs_offset(row, p.groups, j, byte) : q4_0_act_qs_offset(row, p.groups, j, byte);
+    };
+    auto aux_of = [](bool valid, int qsum) {
+        return kPlanar ? (valid ? kMagicBits - 8 * qsum : kMagicBits) : (valid ? 8 * qsum : 0);
+    };
     const int lane = tid & 31, warp = tid >> 5;
     if constexpr (kF32) {
         // 4 lanes per block (8 values each), 8 blocks per warp and item
@@ -188,11 +227,11 @@ PFNG_DEV void stage_act_q8_0(const GemvParams &p, uint8_t *smem, int tid) {
                 const int bi = wb + (lane >> 2);
                 const int row = bi / nbp, j = bi % nbp;
                 const bool valid = row < p.m && j < nb;
-                *reinterpret_cast<uint2 *>(qs + q4_0_act_qs_offset(row, p.groups, j, 8 * c)) =
+                *reinterpret_cast<uint2 *>(qs + qs_offset(row, j, 8 * c)) =
                     valid ? make_uint2(qr[it].q0, qr[it].q1) : make_uint2(0u, 0u);
                 if (c == 0) {
                     d[row * nbp + j] = valid ? f16_bits_to_f32(qr[it].dbits) : 0.0f;
-                    s8[row * nbp + j] = valid ? 8 * qr[it].qsum : 0;
+                    s8[row * nbp + j] = aux_of(valid, qr[it].qsum);
                 }
             }
         }
@@ -226,10 +265,10 @@ PFNG_DEV void stage_act_q8_0(const GemvParams &p, uint8_t *smem, int tid) {
                 int sm = __dp4a(static_cast<int>(q), 0x01010101, 0);
 #pragma unroll
                 for (int o = 1; o < 8; o <<= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
-                *reinterpret_cast<uint32_t *>(qs + q4_0_act_qs_offset(row, p.groups, j, 4 * g)) = valid ? q : 0u;
+                *reinterpret_cast<uint32_t *>(qs + qs_offset(row, j, 4 * g)) = valid ? q : 0u;
                 if (g == 0) {
                     d[row * nbp + j] = valid ? f16_bits_to_f32(raw_d[it]) : 0.0f;
-                    s8[row * nbp + j] = valid ? 8 * sm : 0;
+                    s8[row * nbp + j] = aux_of(valid, sm);
                 }
             }
         }
@@ -415,6 +454,50 @@ PFNG_DEV void rows_q4_0_reg(const GemvParams &p, const Out &o, const ActRegs<GM>
     }
 }
 
+// Sum four rows' lane partials across the warp and store them (rows beyond
+// nrows are not stored).  The first exchange splits rows {0, 1} / {2, 3}
+// between the half-warps, the second rows 0 / 1 (2 / 3) between lane
+// octets; each row's partials meet in the same tree as in a pair's or a
+// single row's butterfly.
+PFNG_DEV void reduce_store4(const Out &o, float a0, float a1, float a2, float a3, int row0, int nrows, int lane) {
+    const bool up = (lane & 16) != 0, b8 = (lane & 8) != 0;
+    const float v0 = (up ? a2 : a0) + __shfl_xor_sync(0xffffffffu, up ? a0 : a2, 16);
+    const float v1 = (up ? a3 : a1) + __shfl_xor_sync(0xffffffffu, up ? a1 : a3, 16);
+    float v = (b8 ? v1 : v0) + __shfl_xor_sync(0xffffffffu, b8 ? v0 : v1, 8);
+#pragma unroll
+    for (int sh = 4; sh > 0; sh >>= 1) v += __shfl_xor_sync(0xffffffffu, v, sh);
+    // lane 0: row 0, lane 8: row 1, lane 16: row 2, lane 24: row 3
+    const int r = (up ? 2 : 0) + (b8 ? 1 : 0);
+    if ((lane & 7) == 0 && r < nrows) o.c[row0 + r] = v;
+}
+
+// m = 1, four rows (a whole claim): rows 0, 1 in r01 and 2, 3 in r23.  More
+// independent dot-product chains than a pair, and one transposed butterfly
+// for the four sums: the first exchange splits rows {0, 1} / {2, 3} between
+// the half-warps, the second rows 0 / 1 (2 / 3) between lane octets.  Every
+// row's lane sums meet in the same tree as in rows_q4_0_reg, so the results
+// are bit-identical to processing the claim as two pairs.
+template <int GM>
+PFNG_DEV void rows4_q4_0_reg(const GemvParams &p, const Out &o, const ActRegs<GM> &ar, const RowsW<GM> &r01,
+                             const RowsW<GM> &r23, int row0, int nrows, int lane) {
+    const int nb = p.k / 32;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int t = 0; t < GM; ++t) {
+        if (t < p.groups && 64 * t + 2 * lane < nb) {
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const PairW &w = r < 2 ? r01.w[t][r] : r23.w[t][r - 2];
+                const int ia = nibble_dot(w.qa, ar.q[t][0], ar.q[t][1]) - ar.s8[t].x;
+                const int ib = nibble_dot(w.qb, ar.q[t][2], ar.q[t][3]) - ar.s8[t].y;
+                acc[r] = __fmaf_rn(__fmul_rn(static_cast<float>(ia), w.da), ar.d[t].x, acc[r]);
+                acc[r] = __fmaf_rn(__fmul_rn(static_cast<float>(ib), w.db), ar.d[t].y, acc[r]);
+            }
+        }
+    }
+    reduce_store4(o, acc[0], acc[1], acc[2], acc[3], row0, nrows, lane);
+}
+
 // any m <= 8, activations in shared memory; two rows as above.
 template <int MT, bool kPartials>
 PFNG_DEV void rows_q4_0_smem(const GemvParams &p, const Out &o, const uint8_t *act, const uint8_t *tile,
@@ -462,6 +545,214 @@ PFNG_DEV void rows_q4_0_smem(const GemvParams &p, const Out &o, const uint8_t *a
         }
     }
     if constexpr (!kPartials) {
+        warp_reduce_store<MT>(p, o, acc0, row0, lane);
+        if (nrows > 1) warp_reduce_store<MT>(p, o, acc1, row0 + 1, lane);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// q4_0 in the planar row layout (pfng_b200_pack_q4_0_planar): a row of nb
+// blocks holds the 16-byte nibble fields of blocks 0..nb-1 (block j at byte
+// 16 j), then their fp16 scales (block j at byte 16 nb + 2 j) -- 18 nb bytes
+// as in the ggml layout, with rows 16-byte aligned (nb % 8 == 0).  Lane l
+// takes blocks j = 32 t + l: one 16-byte read per block, and a warp's reads
+// of one t are 512 contiguous bytes (conflict-free, no funnel shifts).
+// Fold without an int -> float conversion: the low-nibble dp4a chain starts
+// at the bias 0x4B400000 - 8 sum(q), so the chain's end y, read as a float,
+// is 2^23 + 2^22 + P exactly (|P| < 2^22), and
+//   t = fma(y, d_w, -(2^23 + 2^22) d_w) = round(P d_w)
+// (the product (2^23 + 2^22) d_w is exact: d_w has 11 significant bits) --
+// the same value as float(P) * d_w; then acc = fma(t, d_a, acc).  Two rows
+// share each packed fma.rn.f32x2.
+// ---------------------------------------------------------------------------
+// Activations of one lane for the m = 1 register path, GT groups of 32 blocks.
+template <int GT>
+struct ActRegsP {
+    uint4 lo[GT], hi[GT];  // bytes 0..15 and 16..31 of the lane's block 32 t + l
+    float d[GT];
+    int bias[GT];          // 0x4B400000 - 8 * sum(q)
+};
+
+// Weights of one row pair for the lane's blocks.
+template <int GT>
+struct RowsWP {
+    uint4 q[GT][2];  // nibbles, rows 0 and 1
+    uint32_t d[GT];  // fp16 scales: row 0 in the low half, row 1 in the high half
+};
+
+// sum over the block of nibble * a, plus the bias
+PFNG_DEV int nibble_dot_biased(const uint4 &q, const uint4 &alo, const uint4 &ahi, int bias) {
+    int lo = dp4a_us(q.x & 0x0f0f0f0fu, static_cast<int>(alo.x), bias);
+    int hi = dp4a_us(q.x & 0xf0f0f0f0u, static_cast<int>(ahi.x), 0);
+    lo = dp4a_us(q.y & 0x0f0f0f0fu, static_cast<int>(alo.y), lo);
+    hi = dp4a_us(q.y & 0xf0f0f0f0u, static_cast<int>(ahi.y), hi);
+    lo = dp4a_us(q.z & 0x0f0f0f0fu, static_cast<int>(alo.z), lo);
+    hi = dp4a_us(q.z & 0xf0f0f0f0u, static_cast<int>(ahi.z), hi);
+    lo = dp4a_us(q.w & 0x0f0f0f0fu, static_cast<int>(alo.w), lo);
+    hi = dp4a_us(q.w & 0xf0f0f0f0u, static_cast<int>(ahi.w), hi);
+    return lo + (hi >> 4);  // hi holds 16 x the high-nibble dot product exactly
+}
+
+PFNG_DEV float2 f16x2_bits_to_f32x2(uint32_t h) {
+    return __half22float2(__halves2half2(__ushort_as_half(static_cast<unsigned short>(h & 0xffffu)),
+                                         __ushort_as_half(static_cast<unsigned short>(h >> 16))));
+}
+
+// Fold of one block for two rows: y01 are the biased dot products.
+PFNG_DEV float2 fold_pair(int y0, int y1, float2 dw, float da, float2 acc) {
+    const float2 nm = __fmul2_rn(dw, make_float2(-kMagic, -kMagic));
+    const float2 t = __ffma2_rn(make_float2(__int_as_float(y0), __int_as_float(y1)), dw, nm);
+    return __ffma2_rn(t, make_float2(da, da), acc);
+}
+
+// rows4_q4_0_reg with the fold above: the low-nibble chain starts at the
+// bias 0x4B400000 - 8 sum(q) and rows (0, 1) / (2, 3) share packed fmas.
+// Same values as rows4_q4_0_reg (round(P d_w) either way).
+template <int GM>
+PFNG_DEV void rows4_q4_0_reg_f2(const GemvParams &p, const Out &o, const ActRegs<GM> &ar, const RowsW<GM> &r01,
+                                const RowsW<GM> &r23, int row0, int nrows, int lane) {
+    const int nb = p.k / 32;
+    float2 acc01 = make_float2(0.0f, 0.0f), acc23 = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int t = 0; t < GM; ++t) {
+        if (t < p.groups && 64 * t + 2 * lane < nb) {
+            const int ba = kMagicBits - ar.s8[t].x, bb = kMagicBits - ar.s8[t].y;
+            const PairW &w0 = r01.w[t][0], &w1 = r01.w[t][1], &w2 = r23.w[t][0], &w3 = r23.w[t][1];
+            const int y0a = nibble_dot(w0.qa, ar.q[t][0], ar.q[t][1], ba);
+            const int y1a = nibble_dot(w1.qa, ar.q[t][0], ar.q[t][1], ba);
+            const int y2a = nibble_dot(w2.qa, ar.q[t][0], ar.q[t][1], ba);
+            const int y3a = nibble_dot(w3.qa, ar.q[t][0], ar.q[t][1], ba);
+            const int y0b = nibble_dot(w0.qb, ar.q[t][2], ar.q[t][3], bb);
+            const int y1b = nibble_dot(w1.qb, ar.q[t][2], ar.q[t][3], bb);
+            const int y2b = nibble_dot(w2.qb, ar.q[t][2], ar.q[t][3], bb);
+            const int y3b = nibble_dot(w3.qb, ar.q[t][2], ar.q[t][3], bb);
+            acc01 = fold_pair(y0a, y1a, make_float2(w0.da, w1.da), ar.d[t].x, acc01);
+            acc23 = fold_pair(y2a, y3a, make_float2(w2.da, w3.da), ar.d[t].x, acc23);
+            acc01 = fold_pair(y0b, y1b, make_float2(w0.db, w1.db), ar.d[t].y, acc01);
+            acc23 = fold_pair(y2b, y3b, make_float2(w2.db, w3.db), ar.d[t].y, acc23);
+        }
+    }
+    reduce_store4(o, acc01.x, acc01.y, acc23.x, acc23.y, row0, nrows, lane);
+}
+
+template <int GT>
+PFNG_DEV void load_rows_q4_0p(const GemvParams &p, const uint8_t *tile, uint32_t row_off, int nrows, int lane,
+                              RowsWP<GT> &rw) {
+    const int nb = p.k / 32;
+    const uint32_t off1 = row_off + static_cast<uint32_t>(nrows > 1 ? p.row_bytes : 0);
+    const uint32_t dplane = 16u * static_cast<uint32_t>(nb);
+#pragma unroll
+    for (int t = 0; t < GT; ++t) {
+        const int j = 32 * t + lane;
+        if (t < p.groups && j < nb) {
+            rw.q[t][0] = *reinterpret_cast<const uint4 *>(tile + row_off + 16u * j);
+            rw.q[t][1] = *reinterpret_cast<const uint4 *>(tile + off1 + 16u * j);
+            const uint32_t d0 = *reinterpret_cast<const uint16_t *>(tile + row_off + dplane + 2u * j);
+            const uint32_t d1 = *reinterpret_cast<const uint16_t *>(tile + off1 + dplane + 2u * j);
+            rw.d[t] = d0 | (d1 << 16);
+        }
+    }
+}
+
+// Reduce the two rows' lane sums in one butterfly and store them.
+PFNG_DEV void reduce_store_pair(const Out &o, float2 acc, int row0, int nrows, int lane) {
+    // the first exchange leaves row 0's sums in lanes 0..15 and row 1's in 16..31
+    const bool upper = (lane & 16) != 0;
+    float v = (upper ? acc.y : acc.x) + __shfl_xor_sync(0xffffffffu, upper ? acc.x : acc.y, 16);
+#pragma unroll
+    for (int sh = 8; sh > 0; sh >>= 1) v += __shfl_xor_sync(0xffffffffu, v, sh);
+    if (lane == 0) o.c[row0] = v;
+    if (lane == 16 && nrows > 1) o.c[row0 + 1] = v;
+}
+
+template <int GT, bool kPartials>
+PFNG_DEV void rows_q4_0p_reg(const GemvParams &p, const Out &o, const ActRegsP<GT> &ar, const RowsWP<GT> &rw,
+                             int row0, int nrows, int lane) {
+    const int nb = p.k / 32;
+    float2 acc = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int t = 0; t < GT; ++t) {
+        const int j = 32 * t + lane;
+        if (t < p.groups && j < nb) {
+            const int y0 = nibble_dot_biased(rw.q[t][0], ar.lo[t], ar.hi[t], ar.bias[t]);
+            const int y1 = nibble_dot_biased(rw.q[t][1], ar.lo[t], ar.hi[t], ar.bias[t]);
+            if constexpr (kPartials) {
+                int32_t *out = p.partials + static_cast<int64_t>(row0) * nb + j;
+                out[0] = y0 - kMagicBits;
+                if (nrows > 1) out[nb] = y1 - kMagicBits;
+            } else {
+                acc = fold_pair(y0, y1, f16x2_bits_to_f32x2(rw.d[t]), ar.d[t], acc);
+            }
+        }
+    }
+    if constexpr (!kPartials) reduce_store_pair(o, acc, row0, nrows, lane);
+}
+
+// m = 1, four rows (a whole claim), planar layout: rows 0, 1 in r01 and
+// 2, 3 in r23.
+template <int GT>
+PFNG_DEV void rows4_q4_0p_reg(const GemvParams &p, const Out &o, const ActRegsP<GT> &ar, const RowsWP<GT> &r01,
+                              const RowsWP<GT> &r23, int row0, int nrows, int lane) {
+    const int nb = p.k / 32;
+    float2 acc01 = make_float2(0.0f, 0.0f), acc23 = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int t = 0; t < GT; ++t) {
+        const int j = 32 * t + lane;
+        if (t < p.groups && j < nb) {
+            const int y0 = nibble_dot_biased(r01.q[t][0], ar.lo[t], ar.hi[t], ar.bias[t]);
+            const int y1 = nibble_dot_biased(r01.q[t][1], ar.lo[t], ar.hi[t], ar.bias[t]);
+            const int y2 = nibble_dot_biased(r23.q[t][0], ar.lo[t], ar.hi[t], ar.bias[t]);
+            const int y3 = nibble_dot_biased(r23.q[t][1], ar.lo[t], ar.hi[t], ar.bias[t]);
+            acc01 = fold_pair(y0, y1, f16x2_bits_to_f32x2(r01.d[t]), ar.d[t], acc01);
+            acc23 = fold_pair(y2, y3, f16x2_bits_to_f32x2(r23.d[t]), ar.d[t], acc23);
+        }
+    }
+    reduce_store4(o, acc01.x, acc01.y, acc23.x, acc23.y, row0, nrows, lane);
+}
+
+// any m <= 8, activations in shared memory; two rows as above.
+template <int MT, bool kPartials>
+PFNG_DEV void rows_q4_0p_smem(const GemvParams &p, const Out &o, const uint8_t *act, const uint8_t *tile,
+                              uint32_t row_off, int row0, int nrows, int lane) {
+    const int nb = p.k / 32;
+    const int nbp = p.groups * 32;
+    const float *ad = reinterpret_cast<const float *>(act + MT * nbp * 32);
+    const int32_t *abias = reinterpret_cast<const int32_t *>(ad + MT * nbp);
+    const uint32_t off1 = row_off + static_cast<uint32_t>(nrows > 1 ? p.row_bytes : 0);
+    const uint32_t dplane = 16u * static_cast<uint32_t>(nb);
+    float2 acc[MT];
+#pragma unroll
+    for (int mi = 0; mi < MT; ++mi) acc[mi] = make_float2(0.0f, 0.0f);
+    for (int t = 0; t < p.groups; ++t) {
+        const int j = 32 * t + lane;
+        if (j >= nb) break;
+        const uint4 q0 = *reinterpret_cast<const uint4 *>(tile + row_off + 16u * j);
+        const uint4 q1 = *reinterpret_cast<const uint4 *>(tile + off1 + 16u * j);
+        const uint32_t d0 = *reinterpret_cast<const uint16_t *>(tile + row_off + dplane + 2u * j);
+        const uint32_t d1 = *reinterpret_cast<const uint16_t *>(tile + off1 + dplane + 2u * j);
+        const float2 dw = f16x2_bits_to_f32x2(d0 | (d1 << 16));
+#pragma unroll
+        for (int mi = 0; mi < MT; ++mi) {
+            const uint4 *aq = reinterpret_cast<const uint4 *>(act + (mi * p.groups + t) * 1024) + lane;
+            const uint4 alo = aq[0], ahi = aq[32];
+            const int bias = abias[mi * nbp + j];
+            const int y0 = nibble_dot_biased(q0, alo, ahi, bias);
+            const int y1 = nibble_dot_biased(q1, alo, ahi, bias);
+            if constexpr (kPartials) {
+                if (mi < p.m) {
+                    int32_t *out = p.partials + (static_cast<int64_t>(mi) * p.n + row0) * nb + j;
+                    out[0] = y0 - kMagicBits;
+                    if (nrows > 1) out[nb] = y1 - kMagicBits;
+                }
+            } else {
+                acc[mi] = fold_pair(y0, y1, dw, ad[mi * nbp + j], acc[mi]);
+            }
+        }
+    }
+    if constexpr (!kPartials) {
+        float acc0[MT], acc1[MT];
+#pragma unroll
+        for (int mi = 0; mi < MT; ++mi) acc0[mi] = acc[mi].x, acc1[mi] = acc[mi].y;
         warp_reduce_store<MT>(p, o, acc0, row0, lane);
         if (nrows > 1) warp_reduce_store<MT>(p, o, acc1, row0 + 1, lane);
     }
@@ -672,7 +963,12 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
             const int r_begin = static_cast<int>(static_cast<int64_t>(p.total_rows) * blockIdx.x / gridDim.x);
             const int r_end = static_cast<int>(static_cast<int64_t>(p.total_rows) * (blockIdx.x + 1) / gridDim.x);
             for (int r = r_begin; r < r_end;) {
-                if ((issued >= S && !mbar_wait(&empty[stage], phase ^ 1u, p.err, kErrWaitEmpty)) ||
+                // tile issued - kInflight must have landed: its stage still
+                // holds it (it is refilled only by tile issued - kInflight + S);
+                // with kInflight >= S the empty-stage wait below bounds it
+                const int old = kInflight < S ? issued - kInflight : -1;
+                if ((old >= 0 && !mbar_wait(&full[old % S], static_cast<uint32_t>((old / S) & 1), p.err, kErrWaitFull)) ||
+                    (issued >= S && !mbar_wait(&empty[stage], phase ^ 1u, p.err, kErrWaitEmpty)) ||
                     *reinterpret_cast<volatile int *>(&abort_flag)) {
                     ok = false;
                     break;
@@ -709,7 +1005,7 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
 
     // ---------------- consumers ----------------
     uint2 *grid = reinterpret_cast<uint2 *>(smem + p.grid_offset);
-    if constexpr (WT == 2) {
+    if constexpr (WT == kWIQ2) {
         for (int i = tid; i < 256; i += kConsumerThreads) {
             const uint32_t code = pfng_iq2xxs_grid_codes[i];
             uint32_t lo = 0, hi = 0;
@@ -727,8 +1023,8 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
     }
     const uint8_t *act = smem + p.act_offset;
     if (p.overlap) asm volatile("griddepcontrol.wait;" ::: "memory");
-    if constexpr (WT == 0)
-        stage_act_q8_0<MT, kF32>(p, smem, tid);
+    if constexpr (WT == kWQ4_0 || WT == kWQ4_0P)
+        stage_act_q8_0<MT, kF32, WT == kWQ4_0P>(p, smem, tid);
     else
         stage_act_q8_K<MT, kF32>(p, smem, tid);
     consumer_sync();
@@ -740,7 +1036,26 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
     if (!PFNG_GEMV_EARLY_TRIGGER && p.overlap && tid == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     ActRegs<(RG > 0 ? RG : 1)> ar;
-    if constexpr (RG > 0) {
+    ActRegsP<(RG > 0 ? RG : 1)> arp;
+    if constexpr (WT == kWQ4_0P && RG > 0) {
+        const int nbp = p.groups * 32;
+        const float *ad = reinterpret_cast<const float *>(act + nbp * 32);
+        const int32_t *abias = reinterpret_cast<const int32_t *>(ad + nbp);
+#pragma unroll
+        for (int t = 0; t < RG; ++t) {
+            if (t < p.groups) {
+                const uint4 *aq = reinterpret_cast<const uint4 *>(act + t * 1024) + lane;
+                arp.lo[t] = aq[0];
+                arp.hi[t] = aq[32];
+                arp.d[t] = ad[32 * t + lane];
+                arp.bias[t] = abias[32 * t + lane];
+            } else {
+                arp.lo[t] = arp.hi[t] = make_uint4(0, 0, 0, 0);
+                arp.d[t] = 0.0f;
+                arp.bias[t] = kMagicBits;
+            }
+        }
+    } else if constexpr (RG > 0) {
         const int nbp = p.groups * 64;
         const float *ad = reinterpret_cast<const float *>(act + p.groups * 2048);
         const int32_t *as8 = reinterpret_cast<const int32_t *>(ad + nbp);
@@ -792,6 +1107,41 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
         // the stage's window starts at the tile's first byte rounded down to 16
         const uint32_t mis = (static_cast<uint32_t>(tile_row) * static_cast<uint32_t>(p.row_bytes)) & 15u;
         const uint8_t *buf = smem + p.stage_offset + static_cast<uint32_t>(stage) * p.stage_bytes;
+        if constexpr (WT == kWQ4_0P && RG > 0 && !kPartials && kClaimRows == 4 && PFNG_GEMV_CLAIM4) {
+            const int first = kClaimRows * qr;
+            const int nrows = tile_rows - first < kClaimRows ? tile_rows - first : kClaimRows;
+            const uint32_t row_off = static_cast<uint32_t>(first) * static_cast<uint32_t>(p.row_bytes) + mis;
+            RowsWP<RG> r01, r23;
+            if (nrows > 0) load_rows_q4_0p<RG>(p, buf, row_off, nrows < 2 ? nrows : 2, lane, r01);
+            if (nrows > 2)
+                load_rows_q4_0p<RG>(p, buf, row_off + 2u * static_cast<uint32_t>(p.row_bytes), nrows - 2, lane, r23);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[stage]);
+            if (nrows > 2)
+                rows4_q4_0p_reg<RG>(p, o, arp, r01, r23, tile_row + first, nrows, lane);
+            else if (nrows > 0)
+                rows_q4_0p_reg<RG, kPartials>(p, o, arp, r01, tile_row + first, nrows, lane);
+        } else if constexpr (WT == kWQ4_0 && RG > 0 && !kPartials && kClaimRows == 4 && PFNG_GEMV_CLAIM4) {
+            // the claim's four rows at once: all weights to registers, release
+            // the stage, then compute
+            const int first = kClaimRows * qr;
+            const int nrows = tile_rows - first < kClaimRows ? tile_rows - first : kClaimRows;
+            const uint32_t row_off = static_cast<uint32_t>(first) * static_cast<uint32_t>(p.row_bytes) + mis;
+            RowsW<RG> r01, r23;
+            if (nrows > 0) load_rows_q4_0<RG>(p, buf, row_off, nrows < 2 ? nrows : 2, lane, r01);
+            if (nrows > 2)
+                load_rows_q4_0<RG>(p, buf, row_off + 2u * static_cast<uint32_t>(p.row_bytes), nrows - 2, lane, r23);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[stage]);
+            if (nrows > 2) {
+                if constexpr (PFNG_GEMV_FOLD2)
+                    rows4_q4_0_reg_f2<RG>(p, o, ar, r01, r23, tile_row + first, nrows, lane);
+                else
+                    rows4_q4_0_reg<RG>(p, o, ar, r01, r23, tile_row + first, nrows, lane);
+            }
+            else if (nrows > 0)
+                rows_q4_0_reg<RG, kPartials>(p, o, ar, r01, tile_row + first, nrows, lane);
+        } else {
 #pragma unroll 1
         for (int h = 0; h < kClaimRows / kPairRows; ++h) {
             const int first = kClaimRows * qr + kPairRows * h;  // first row of the pair in the tile
@@ -799,7 +1149,15 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
             const int nrows = tile_rows - first < kPairRows ? tile_rows - first : kPairRows;
             const uint32_t row_off = static_cast<uint32_t>(first) * static_cast<uint32_t>(p.row_bytes) + mis;
             const bool last = h == kClaimRows / kPairRows - 1;
-            if constexpr (WT == 0 && RG > 0) {
+            if constexpr (WT == kWQ4_0P && RG > 0) {
+                RowsWP<RG> rw;
+                if (nrows > 0) load_rows_q4_0p<RG>(p, buf, row_off, nrows, lane, rw);
+                if (last) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[stage]);
+                }
+                if (nrows > 0) rows_q4_0p_reg<RG, kPartials>(p, o, arp, rw, row0, nrows, lane);
+            } else if constexpr (WT == kWQ4_0 && RG > 0) {
                 // copy the pair's weights to registers; after the claim's last
                 // pair is copied, release the stage, then compute
                 RowsW<RG> rw;
@@ -811,12 +1169,14 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
                 if (nrows > 0) rows_q4_0_reg<RG, kPartials>(p, o, ar, rw, row0, nrows, lane);
             } else {
                 if (nrows > 0) {
-                    if constexpr (WT == 0) {
+                    if constexpr (WT == kWQ4_0) {
                         rows_q4_0_smem<MT, kPartials>(p, o, act, buf, row_off, row0, nrows, lane);
+                    } else if constexpr (WT == kWQ4_0P) {
+                        rows_q4_0p_smem<MT, kPartials>(p, o, act, buf, row_off, row0, nrows, lane);
                     } else {
                         for (int r = 0; r < nrows; ++r) {
                             const uint32_t off = row_off + static_cast<uint32_t>(r * p.row_bytes);
-                            if constexpr (WT == 1)
+                            if constexpr (WT == kWQ4_K)
                                 row_q4_K<MT, kPartials>(p, o, act, buf, off, row0 + r, lane);
                             else
                                 row_iq2_xxs<MT, kPartials>(p, o, act, buf, off, row0 + r, lane, grid);
@@ -829,13 +1189,15 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
                 }
             }
         }
+        }
     }
 }
 
 int64_t row_bytes_of(int wtype, int64_t k) {
     switch (wtype) {
-    case 0: return k / 32 * kQ4_0Bytes;
-    case 1: return k / 256 * kQ4_KBytes;
+    case kWQ4_0:
+    case kWQ4_0P: return k / 32 * kQ4_0Bytes;
+    case kWQ4_K: return k / 256 * kQ4_KBytes;
     default: return k / 256 * kIQ2Bytes;
     }
 }
@@ -843,9 +1205,13 @@ int64_t row_bytes_of(int wtype, int64_t k) {
 int mt_of(int64_t m) { return m <= 1 ? 1 : m <= 2 ? 2 : m <= 4 ? 4 : 8; }
 
 uint32_t act_bytes_of(int wtype, int mt, int64_t k) {
-    if (wtype == 0) {
+    if (wtype == kWQ4_0) {
         const int64_t groups = (k / 32 + 63) / 64;
         return static_cast<uint32_t>(mt * groups * (2048 + 64 * 8));
+    }
+    if (wtype == kWQ4_0P) {
+        const int64_t groups = (k / 32 + 31) / 32;
+        return static_cast<uint32_t>(mt * groups * (1024 + 32 * 8));
     }
     return static_cast<uint32_t>(mt * (k + (k / 256) * 4 + (k / 16) * 2));
 }
@@ -874,10 +1240,10 @@ bool plan(int wtype, int64_t m, int count, const int64_t *ns, int64_t k, GemvPar
     for (int g = count; g <= kMaxGroup; ++g) p.row_base[g] = static_cast<int>(rows);
     p.total_rows = static_cast<int>(rows);
     p.num_tiles = static_cast<int>((rows + p.rows_per_tile - 1) / p.rows_per_tile);
-    p.groups = static_cast<int>((k / 32 + 63) / 64);
+    p.groups = static_cast<int>(wtype == kWQ4_0P ? (k / 32 + 31) / 32 : (k / 32 + 63) / 64);
     p.stage_bytes = align_up_u32(static_cast<uint32_t>(p.rows_per_tile * rb) + 16 + kStageSlack, 128);
     p.grid_offset = kBarrierBytes;
-    p.act_offset = align_up_u32(p.grid_offset + (wtype == 2 ? kGridTableBytes : 0), 128);
+    p.act_offset = align_up_u32(p.grid_offset + (wtype == kWIQ2 ? kGridTableBytes : 0), 128);
     p.stage_offset = align_up_u32(p.act_offset + act_bytes_of(wtype, mt, k), 128);
     // at most half the SM's shared memory, so that the next launch's CTA can
     // be resident beside this one (overlapped decode launches)
@@ -930,7 +1296,14 @@ cudaError_t dispatch_flags(const GemvParams &p, uint32_t smem, bool partials, bo
 
 template <int WT>
 cudaError_t dispatch_mt(const GemvParams &p, uint32_t smem, bool partials, bool f32, cudaStream_t s) {
-    if constexpr (WT == 0) {
+    if constexpr (WT == kWQ4_0P) {
+        if (p.m == 1) {
+            if (p.groups <= 1) return dispatch_flags<WT, 1, 1>(p, smem, partials, f32, s);
+            if (p.groups <= 2) return dispatch_flags<WT, 1, 2>(p, smem, partials, f32, s);
+            if (p.groups <= 4) return dispatch_flags<WT, 1, 4>(p, smem, partials, f32, s);
+        }
+    }
+    if constexpr (WT == kWQ4_0) {
         if (p.m == 1) {
             if (p.groups <= 1) return dispatch_flags<WT, 1, 1>(p, smem, partials, f32, s);
             if (p.groups <= 2) return dispatch_flags<WT, 1, 2>(p, smem, partials, f32, s);
@@ -949,7 +1322,8 @@ cudaError_t dispatch_mt(const GemvParams &p, uint32_t smem, bool partials, bool 
 
 bool gemv_supported(int wtype, int64_t m, int count, const int64_t *n, int64_t k, const void *const *w) {
     if (m < 1 || m > 8 || count < 1 || count > kMaxGroup) return false;
-    if (wtype == 0 && (k / 32) % 2 != 0) return false;  // block pairs
+    if (wtype == kWQ4_0 && (k / 32) % 2 != 0) return false;  // block pairs
+    if (wtype == kWQ4_0P && k % 256 != 0) return false;     // 16-byte aligned planar rows
     const int64_t rb = row_bytes_of(wtype, k);
     for (int g = 0; g < count; ++g)
         if (n[g] < 1 || (reinterpret_cast<uintptr_t>(w[g]) & 15u) != 0 || (n[g] * rb) % 16 != 0) return false;
@@ -980,9 +1354,10 @@ cudaError_t launch_gemv(const GemvArgs &args, cudaStream_t s) {
     const bool partials = args.partials != nullptr;
     const bool f32 = args.x != nullptr;
     switch (args.wtype) {
-    case 0: return dispatch_mt<0>(p, smem, partials, f32, s);
-    case 1: return dispatch_mt<1>(p, smem, partials, f32, s);
-    default: return dispatch_mt<2>(p, smem, partials, f32, s);
+    case kWQ4_0: return dispatch_mt<kWQ4_0>(p, smem, partials, f32, s);
+    case kWQ4_K: return dispatch_mt<kWQ4_K>(p, smem, partials, f32, s);
+    case kWQ4_0P: return dispatch_mt<kWQ4_0P>(p, smem, partials, f32, s);
+    default: return dispatch_mt<kWIQ2>(p, smem, partials, f32, s);
     }
 }
 

@@ -18,6 +18,11 @@ constexpr int kQ8_0Bytes = 34;   // fp16 d, 32 x int8
 constexpr int kQ8_KBytes = 292;  // fp32 d, 256 x int8, 16 x int16 bsums
 constexpr int kQ4_KBytes = 144;  // fp16 d, fp16 dmin, 12 B 6-bit scales/mins, 128 B nibbles
 constexpr int kIQ2Bytes = 66;    // fp16 d, 32 x uint16 (8 B per 32-value group)
+// Weight type codes (the PFNG_B200_* weight types of the C ABI).  kWQ4_0P
+// is q4_0 in the planar row layout: per weight row of nb blocks, the 16-byte
+// nibble fields of blocks 0..nb-1 (block j at byte 16 j), then their fp16
+// scales (block j at byte 16 nb + 2 j); 18 nb bytes per row, like ggml's.
+constexpr int kWQ4_0 = 0, kWQ4_K = 1, kWIQ2 = 2, kWQ4_0P = 3;
 constexpr int kQ8_KQsOffset = 4;
 constexpr int kQ8_KBsumsOffset = 260;
 

@@ -92,6 +92,10 @@ struct SimpleArgs {
 };
 cudaError_t launch_simple(const SimpleArgs &args, cudaStream_t s);
 
+// planar.cu -- q4_0 between the ggml and the planar row layout (k % 256 == 0)
+cudaError_t launch_pack_q4_0_planar(const void *w, void *w_planar, int64_t n, int64_t k, cudaStream_t s);
+cudaError_t launch_unpack_q4_0_planar(const void *w_planar, void *w, int64_t n, int64_t k, cudaStream_t s);
+
 // shard.cu
 cudaError_t launch_unshard_columns(const float *slices, float *c, int64_t m, int64_t n, int64_t ldc, int world,
                                    int64_t granule, int64_t slice_width, cudaStream_t s);

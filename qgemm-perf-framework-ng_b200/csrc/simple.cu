@@ -16,7 +16,9 @@ namespace {
 PFNG_DEV uint32_t ld_u8(const uint8_t *p) { return __ldg(p); }
 PFNG_DEV uint32_t ld_u16(const uint8_t *p) { return __ldg(reinterpret_cast<const uint16_t *>(p)); }
 
-template <bool kPartials>
+// kPlanar: W in the planar row layout (block b's nibbles at 16 b of the row,
+// its scale at 16 nb + 2 b); otherwise raw 18-byte blocks.
+template <bool kPartials, bool kPlanar>
 __global__ void simple_q4_0(SimpleArgs a) {
     const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (e >= a.m * a.n) return;
@@ -25,17 +27,19 @@ __global__ void simple_q4_0(SimpleArgs a) {
     const uint8_t *A = static_cast<const uint8_t *>(a.a) + i * nb * kQ8_0Bytes;
     float sum = 0.0f;
     for (int64_t b = 0; b < nb; ++b) {
-        const uint8_t *wb = W + b * kQ4_0Bytes, *ab = A + b * kQ8_0Bytes;
+        const uint8_t *wq = kPlanar ? W + 16 * b : W + b * kQ4_0Bytes + 2;
+        const uint8_t *wd = kPlanar ? W + 16 * nb + 2 * b : W + b * kQ4_0Bytes;
+        const uint8_t *ab = A + b * kQ8_0Bytes;
         int32_t isum = 0;
         for (int t = 0; t < 16; ++t) {
-            const int q = static_cast<int>(ld_u8(wb + 2 + t));
+            const int q = static_cast<int>(ld_u8(wq + t));
             isum += ((q & 15) - 8) * static_cast<int8_t>(ld_u8(ab + 2 + t));
             isum += ((q >> 4) - 8) * static_cast<int8_t>(ld_u8(ab + 18 + t));
         }
         if constexpr (kPartials) {
             a.partials[e * nb + b] = isum;
         } else {
-            const float dw = f16_bits_to_f32(ld_u16(wb)), da = f16_bits_to_f32(ld_u16(ab));
+            const float dw = f16_bits_to_f32(ld_u16(wd)), da = f16_bits_to_f32(ld_u16(ab));
             sum = __fadd_rn(sum, __fmul_rn(__fmul_rn(static_cast<float>(isum), dw), da));
         }
     }
@@ -134,11 +138,15 @@ cudaError_t launch_simple(const SimpleArgs &args, cudaStream_t s) {
     if (blocks > 0x7fffffff) return cudaErrorInvalidValue;
     const bool part = args.partials != nullptr;
     switch (args.wtype) {
-    case 0:
-        if (part) simple_q4_0<true><<<blocks, threads, 0, s>>>(args);
-        else simple_q4_0<false><<<blocks, threads, 0, s>>>(args);
+    case kWQ4_0:
+        if (part) simple_q4_0<true, false><<<blocks, threads, 0, s>>>(args);
+        else simple_q4_0<false, false><<<blocks, threads, 0, s>>>(args);
         break;
-    case 1:
+    case kWQ4_0P:
+        if (part) simple_q4_0<true, true><<<blocks, threads, 0, s>>>(args);
+        else simple_q4_0<false, true><<<blocks, threads, 0, s>>>(args);
+        break;
+    case kWQ4_K:
         if (part) simple_q4_K<true><<<blocks, threads, 0, s>>>(args);
         else simple_q4_K<false><<<blocks, threads, 0, s>>>(args);
         break;

@@ -23,8 +23,8 @@ REPO_ROOT = PACKAGE_DIR.parent
 LIB_PATH = PACKAGE_DIR / "libpfng_b200.so"
 HEADER_PATH = REPO_ROOT / "include" / "pfng_b200.h"
 
-Q4_0, Q4_K, IQ2_XXS = 0, 1, 2
-WTYPES = {"q4_0": Q4_0, "q4_K": Q4_K, "iq2_xxs": IQ2_XXS}
+Q4_0, Q4_K, IQ2_XXS, Q4_0_PLANAR = 0, 1, 2, 3
+WTYPES = {"q4_0": Q4_0, "q4_K": Q4_K, "iq2_xxs": IQ2_XXS, "q4_0_planar": Q4_0_PLANAR}
 PATH_AUTO, PATH_GEMV, PATH_MMA, PATH_SIMPLE = 0, 1, 2, 3
 PATHS = {"auto": PATH_AUTO, "gemv": PATH_GEMV, "mma": PATH_MMA, "simple": PATH_SIMPLE}
 
@@ -34,6 +34,7 @@ LAYOUT = {
     Q4_0: (Q4_0_BYTES, 32, Q8_0_BYTES, 32),
     Q4_K: (Q4_K_BYTES, 256, Q8_K_BYTES, 256),
     IQ2_XXS: (IQ2_XXS_BYTES, 256, Q8_K_BYTES, 256),
+    Q4_0_PLANAR: (Q4_0_BYTES, 32, Q8_0_BYTES, 32),  # same bytes per row as q4_0, reordered
 }
 
 OK = 0
@@ -78,17 +79,21 @@ def _declare(L: ctypes.CDLL) -> None:
         f = getattr(L, f"pfng_b200_{name}")
         f.restype = S
         f.argtypes = [I, I64, I64, I64, I]
-    for t in ("q4_0_q8_0", "q4_K_q8_K", "iq2_xxs_q8_K"):
+    for t in ("q4_0_q8_0", "q4_K_q8_K", "iq2_xxs_q8_K", "q4_0p_q8_0"):
         f = getattr(L, f"pfng_b200_mm_{t}")
         f.restype = I
         f.argtypes = [P, P, P, I64, I64, I64, I64, P, S, I, P]
         f = getattr(L, f"pfng_b200_partials_{t}")
         f.restype = I
         f.argtypes = [P, P, P, I64, I64, I64, P, S, I, P]
-    for t in ("q4_0", "q4_K", "iq2_xxs"):
+    for t in ("q4_0", "q4_K", "iq2_xxs", "q4_0p"):
         f = getattr(L, f"pfng_b200_compute_{t}")
         f.restype = I
         f.argtypes = [P, P, I64, P, I64, I64, I64, I64, P, S, I, P]
+    for name in ("pack_q4_0_planar", "unpack_q4_0_planar"):
+        f = getattr(L, f"pfng_b200_{name}")
+        f.restype = I
+        f.argtypes = [P, P, I64, I64, P]
     L.pfng_b200_compute_grouped.restype = I
     L.pfng_b200_compute_grouped.argtypes = [I, I, ctypes.POINTER(P), ctypes.POINTER(I64), ctypes.POINTER(P),
                                             ctypes.POINTER(I64), P, I64, I64, I64, ctypes.c_uint, P]
@@ -124,7 +129,7 @@ def _stream(stream) -> int:
 
 
 def _suffix(wtype: int) -> str:
-    return {Q4_0: "q4_0_q8_0", Q4_K: "q4_K_q8_K", IQ2_XXS: "iq2_xxs_q8_K"}[wtype]
+    return {Q4_0: "q4_0_q8_0", Q4_K: "q4_K_q8_K", IQ2_XXS: "iq2_xxs_q8_K", Q4_0_PLANAR: "q4_0p_q8_0"}[wtype]
 
 
 def _wt(wtype) -> int:
@@ -167,7 +172,26 @@ def quantize_q4_K(x, out=None, stream=None):
 
 
 def quantize_activation(wtype, x, out=None, stream=None):
-    return quantize_q8_0(x, out, stream) if _wt(wtype) == Q4_0 else quantize_q8_K(x, out, stream)
+    q8_0 = _wt(wtype) in (Q4_0, Q4_0_PLANAR)
+    return quantize_q8_0(x, out, stream) if q8_0 else quantize_q8_K(x, out, stream)
+
+
+def pack_q4_0_planar(w, n: int, k: int, out=None, stream=None):
+    """block_q4_0 bytes [n][k/32] -> the planar row layout (same size; k % 256 == 0)."""
+    import torch
+    if out is None:
+        out = torch.empty(n * (k // 32) * Q4_0_BYTES, dtype=torch.uint8, device=w.device)
+    _check(lib().pfng_b200_pack_q4_0_planar(_ptr(w), _ptr(out), n, k, _stream(stream)), "pack_q4_0_planar")
+    return out
+
+
+def unpack_q4_0_planar(wp, n: int, k: int, out=None, stream=None):
+    """Planar row layout -> block_q4_0 bytes (the inverse of pack_q4_0_planar)."""
+    import torch
+    if out is None:
+        out = torch.empty(n * (k // 32) * Q4_0_BYTES, dtype=torch.uint8, device=wp.device)
+    _check(lib().pfng_b200_unpack_q4_0_planar(_ptr(wp), _ptr(out), n, k, _stream(stream)), "unpack_q4_0_planar")
+    return out
 
 
 # ------------------------------------------------------------------- matmul
@@ -211,7 +235,7 @@ def compute(wtype, w, x, n: int, out=None, path="auto", workspace=None, stream=N
         out = torch.empty((m, n), dtype=torch.float32, device=w.device)
     ws = _workspace(compute_workspace_size(wt, m, n, k, p), w.device, workspace)
     nbytes = 0 if ws is None else ws.numel()
-    name = {Q4_0: "q4_0", Q4_K: "q4_K", IQ2_XXS: "iq2_xxs"}[wt]
+    name = {Q4_0: "q4_0", Q4_K: "q4_K", IQ2_XXS: "iq2_xxs", Q4_0_PLANAR: "q4_0p"}[wt]
     _check(getattr(lib(), f"pfng_b200_compute_{name}")(
         _ptr(w), _ptr(x), x.stride(0), _ptr(out), m, n, k, out.stride(0), _ptr(ws), nbytes, p,
         _stream(stream)), f"compute_{name}")

@@ -74,6 +74,10 @@ class Oracle:
             f = getattr(L, f"oracle_compute_{t}")
             f.restype = None
             f.argtypes = [_P, _P, _P, _S, _S, _S]
+        for name in ("pack", "unpack"):
+            f = getattr(L, f"oracle_{name}_q4_0_planar")
+            f.restype = None
+            f.argtypes = [_P, _P, _S, _S]
         L.oracle_iq2_xxs_grid.restype = ctypes.c_uint64
         L.oracle_iq2_xxs_grid.argtypes = [ctypes.c_uint]
         L.oracle_iq2_xxs_sign_mask.restype = ctypes.c_uint8
@@ -119,6 +123,19 @@ class Oracle:
     def bound(self, wtype: str, w: np.ndarray, a: np.ndarray, m: int, n: int, k: int) -> np.ndarray:
         out = np.zeros((m, n), np.float64)
         getattr(self.lib, f"oracle_bound_{self._suffix(wtype)}")(ptr(w), ptr(a), ptr(out), m, n, k)
+        return out
+
+    # -- q4_0 planar row layout: w is (n, k / 32) block_q4_0, the result raw bytes (n, 18 k / 32)
+    def pack_q4_0_planar(self, w: np.ndarray, n: int, k: int) -> np.ndarray:
+        w = np.ascontiguousarray(w)
+        out = np.zeros((n, k // 32 * 18), np.uint8)
+        self.lib.oracle_pack_q4_0_planar(ptr(w), ptr(out), n, k)
+        return out
+
+    def unpack_q4_0_planar(self, wp: np.ndarray, n: int, k: int) -> np.ndarray:
+        wp = np.ascontiguousarray(wp, np.uint8)
+        out = np.zeros((n, k // 32), BLOCK_Q4_0)
+        self.lib.oracle_unpack_q4_0_planar(ptr(wp), ptr(out), n, k)
         return out
 
     def iq2_grid(self) -> np.ndarray:

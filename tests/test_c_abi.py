@@ -107,3 +107,33 @@ def test_shard_rows_partition(n, world, granule):
 def test_shard_rows_rejects_bad_rank():
     with pytest.raises(pb.PfngError):
         pb.shard_rows(10, 2, 2, 1)
+
+
+def test_planar_argument_checks(L):
+    pack, unpack = L.pfng_b200_pack_q4_0_planar, L.pfng_b200_unpack_q4_0_planar
+    big = FAKE * 16
+    assert pack(FAKE, big, 4, 96, None) == SHAPE            # k % 256 != 0
+    assert pack(FAKE, big + 2, 4, 256, None) == ALIGN       # planar side 16-byte aligned
+    assert pack(FAKE + 1, big, 4, 256, None) == ALIGN       # ggml side 2-byte aligned
+    assert unpack(big + 8, FAKE, 4, 256, None) == ALIGN
+    assert pack(FAKE, FAKE + 16, 4, 256, None) == INVALID   # overlapping buffers
+    assert pack(None, big, 4, 256, None) == INVALID
+    assert pack(None, None, 0, 256, None) == OK
+    assert pack(FAKE, big, -1, 256, None) == INVALID
+    mm = L.pfng_b200_mm_q4_0p_q8_0
+    assert mm(FAKE, FAKE, FAKE, 4, 4, 32, 4, None, 0, 0, None) == SHAPE      # planar needs k % 256 == 0
+    assert mm(FAKE + 2, FAKE, FAKE, 4, 4, 256, 4, None, 0, 0, None) == ALIGN  # planar W 16-byte aligned
+    assert mm(FAKE, FAKE + 1, FAKE, 4, 4, 256, 4, None, 0, 0, None) == ALIGN  # q8_0 blocks 2-aligned
+    comp = L.pfng_b200_compute_q4_0p
+    assert comp(FAKE, FAKE, 128, FAKE, 4, 4, 256, 4, None, 0, 0, None) == SHAPE  # ldx < k
+    part = L.pfng_b200_partials_q4_0p_q8_0
+    assert part(None, None, None, 0, 4, 256, None, 0, 0, None) == OK
+    # weight type code 3 is the planar layout, 4 is unknown
+    assert pb.mm_workspace_size("q4_0_planar", 480, 1536, 1536) == pb.mm_workspace_size("q4_0", 480, 1536, 1536)
+    assert pb.mm_workspace_size(4, 480, 1536, 1536) == 0
+    grouped = L.pfng_b200_compute_grouped
+    n = (ctypes.c_int64 * 1)(4)
+    ptrs = (ctypes.c_void_p * 1)(FAKE)
+    ldc = (ctypes.c_int64 * 1)(4)
+    assert grouped(4, 1, ptrs, n, ptrs, ldc, FAKE, 256, 1, 256, 0, None) == INVALID
+    assert grouped(3, 1, ptrs, n, ptrs, ldc, FAKE, 256, 1, 96, 0, None) == SHAPE

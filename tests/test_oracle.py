@@ -143,3 +143,21 @@ def test_reference_threaded_matches_compute(reference):
         c1 = reference.mm_threads(wtype, w, a, m, n, k, threads=3)
         c2 = reference.compute(wtype, w, x, m, n, k)
         np.testing.assert_array_equal(c1.view(np.uint32), c2.view(np.uint32))
+
+
+def test_planar_layout_oracle(oracle, golden):
+    # the planar row layout is a per-row byte permutation of block_q4_0:
+    # nibble fields first (16 B per block), then the fp16 scales; checked on
+    # the reference generator's q4_0 weights (golden fixture) and on random bytes
+    import numpy as np
+    m, n, k = (int(v) for v in golden["ref_q4_0_seed1_shape"])
+    rng = np.random.default_rng(3)
+    for w, n, k in ((golden["ref_q4_0_seed1_w"], n, k),
+                    (rng.integers(0, 256, 7 * 48 * 18, dtype=np.uint8), 7, 1536)):
+        nb = k // 32
+        blocks = w.reshape(n, nb, 18)
+        planar = oracle.pack_q4_0_planar(w, n, k)
+        assert planar.shape == (n, nb * 18)
+        np.testing.assert_array_equal(planar[:, : 16 * nb].reshape(n, nb, 16), blocks[:, :, 2:])
+        np.testing.assert_array_equal(planar[:, 16 * nb:].reshape(n, nb, 2), blocks[:, :, :2])
+        assert oracle.unpack_q4_0_planar(planar, n, k).tobytes() == w.tobytes()
