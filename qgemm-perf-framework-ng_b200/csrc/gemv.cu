@@ -84,6 +84,12 @@ constexpr int kClaimRows = PFNG_GEMV_CLAIM_ROWS;  // rows a warp claims at a tim
 #define PFNG_GEMV_INFLIGHT 32
 #endif
 constexpr int kInflight = PFNG_GEMV_INFLIGHT;
+// First wave: the producer issues this many tiles, then waits for the first
+// to land before issuing the rest of the ring (0: no first wave).
+#ifndef PFNG_GEMV_FIRST_WAVE
+#define PFNG_GEMV_FIRST_WAVE 0
+#endif
+constexpr int kFirstWave = PFNG_GEMV_FIRST_WAVE;
 #ifndef PFNG_GEMV_TILE_ROWS
 #define PFNG_GEMV_TILE_ROWS 8
 #endif
@@ -966,7 +972,7 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
                 // tile issued - kInflight must have landed: its stage still
                 // holds it (it is refilled only by tile issued - kInflight + S);
                 // with kInflight >= S the empty-stage wait below bounds it
-                const int old = kInflight < S ? issued - kInflight : -1;
+                const int old = kInflight < S ? issued - kInflight : (kFirstWave > 0 && issued == kFirstWave ? 0 : -1);
                 if ((old >= 0 && !mbar_wait(&full[old % S], static_cast<uint32_t>((old / S) & 1), p.err, kErrWaitFull)) ||
                     (issued >= S && !mbar_wait(&empty[stage], phase ^ 1u, p.err, kErrWaitEmpty)) ||
                     *reinterpret_cast<volatile int *>(&abort_flag)) {
