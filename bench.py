@@ -445,10 +445,18 @@ def prefill(args) -> int:
     copies = max(2, -(-4 * L2_BYTES // per))
     ws_ = [make_weights_device(pb, torch, args.wtype, n, k, gen) for _ in range(copies)]
     xs = [torch.randn((m, k), generator=gen, device="cuda") for _ in range(copies)]
-    out = torch.empty((m, n), device="cuda")
-    wsp = torch.empty(max(1, pb.compute_workspace_size(args.wtype, m, n, k)), dtype=torch.uint8, device="cuda")
-    step = lambda i: pb.compute(args.wtype, ws_[i % copies], xs[i % copies], n, out=out, workspace=wsp,
-                                stream=stream)
+    if args.out == "f32":
+        out = torch.empty((m, n), device="cuda")
+        wsp = torch.empty(max(1, pb.compute_workspace_size(args.wtype, m, n, k)), dtype=torch.uint8, device="cuda")
+        step = lambda i: pb.compute(args.wtype, ws_[i % copies], xs[i % copies], n, out=out, workspace=wsp,
+                                    stream=stream)
+    else:
+        # the result in another format, converted in the GEMM's epilogue
+        out = pb._out_tensor(pb.OUT_FORMATS[args.out], m, n, "cuda")
+        wsp = torch.empty(max(1, pb.lib().pfng_b200_compute_out_workspace_size(
+            pb._wt(args.wtype), pb.OUT_FORMATS[args.out], m, n, k, 0)), dtype=torch.uint8, device="cuda")
+        step = lambda i: pb.compute_out(args.wtype, ws_[i % copies], xs[i % copies], n, args.out, out=out,
+                                        workspace=wsp, stream=stream)
     with ClockSampler(torch.cuda.current_device()) as clocks:
         elapsed = time_graph(torch, stream, step, args.steps, args.warmup)
     pb.check_kernel_error()
@@ -456,7 +464,8 @@ def prefill(args) -> int:
     peak, peak_src = int8_peak_tops()
     achieved = ops / (elapsed / args.steps) / 1e12
     print(json.dumps({
-        "metric": METRIC, "workload": f"{args.wtype} GEMM M={m} N={n} K={k} (quantize x + matmul, one step)",
+        "metric": METRIC, "workload": f"{args.wtype} GEMM M={m} N={n} K={k} (quantize x + matmul, one step)"
+                                      + ("" if args.out == "f32" else f", output {args.out} (fused epilogue)"),
         "value": args.steps * ops / elapsed / 1e9, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "us_per_step": elapsed / args.steps * 1e6,
         "weight_GBps": args.steps * weight_bytes(args.wtype, n, k) / elapsed / 1e9,
@@ -570,6 +579,8 @@ def main() -> int:
     ap.add_argument("--workload", choices=["decode", "prefill", "llama"], default="decode",
                     help="decode: configs[1] (the bench line); prefill: configs[0]/[2]/[3]; llama: configs[4]")
     ap.add_argument("--wtype", choices=["q4_0", "q4_K", "iq2_xxs"], default="q4_0")
+    ap.add_argument("--out", choices=["f32", "f16", "bf16", "q8_0"], default="f32",
+                    help="prefill: format of C, converted in the GEMM's epilogue")
     ap.add_argument("--layout", choices=["ggml", "planar"], default="ggml",
                     help="decode: q4_0 weights as ggml blocks or repacked once into the planar row layout")
     ap.add_argument("--m", type=int, default=None)

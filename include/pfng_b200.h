@@ -138,6 +138,38 @@ int pfng_b200_compute_grouped(int wtype, int count, const void *const *w, const 
                               const int64_t *ldc, const float *x, int64_t ldx, int64_t m, int64_t k, unsigned flags,
                               void *stream);
 
+/* ---- output formats: the result written by the matmul's epilogue ----------
+ * pfng_b200_mm_out / pfng_b200_compute_out are pfng_b200_mm_* /
+ * pfng_b200_compute_* (any weight type code, same paths and checks) whose
+ * result is written in `out_format`:
+ *   PFNG_B200_OUT_F32   fp32, row stride ldo floats (the plain entry points)
+ *   PFNG_B200_OUT_F16   fp16, round to nearest even, row stride ldo halves
+ *   PFNG_B200_OUT_BF16  bf16, round to nearest even, row stride ldo
+ *   PFNG_B200_OUT_Q8_0  C quantized along n into block_q8_0 -- the
+ *                       activation operand of a next layer with q4_0 weights
+ *                       -- row stride ldo blocks; requires n % 32 == 0
+ * Every format is the conversion of the fp32 C the same path computes: the
+ * q8_0 bytes equal pfng_b200_quantize_q8_0 applied to that C (the reference's
+ * quantize_row_q8_0, llama_reference.cpp:38-52).  On the tensor-core path the
+ * conversion is fused into the GEMM's epilogue (no fp32 C is written); the
+ * GEMV and SIMPLE paths write fp32 C to the workspace and convert it in a
+ * second launch (for decode, keep fp32 C and let the next layer's fused
+ * quantizer read it).  out is 2-byte aligned.  Workspace sizes:
+ * pfng_b200_mm_out_workspace_size / pfng_b200_compute_out_workspace_size.
+ * No reference counterpart (the reference's consumer is its fp32 export,
+ * bench/framework/kernel_registry.h:99). */
+#define PFNG_B200_OUT_F32 0
+#define PFNG_B200_OUT_F16 1
+#define PFNG_B200_OUT_BF16 2
+#define PFNG_B200_OUT_Q8_0 3
+size_t pfng_b200_mm_out_workspace_size(int wtype, int out_format, int64_t m, int64_t n, int64_t k, int path);
+size_t pfng_b200_compute_out_workspace_size(int wtype, int out_format, int64_t m, int64_t n, int64_t k, int path);
+int pfng_b200_mm_out(int wtype, const void *w, const void *a, void *out, int out_format, int64_t ldo, int64_t m,
+                     int64_t n, int64_t k, void *workspace, size_t workspace_bytes, int path, void *stream);
+int pfng_b200_compute_out(int wtype, const void *w, const float *x, int64_t ldx, void *out, int out_format,
+                          int64_t ldo, int64_t m, int64_t n, int64_t k, void *workspace, size_t workspace_bytes,
+                          int path, void *stream);
+
 /* ---- q4_0 in the planar row layout ---------------------------------------
  * A weight row of nb = k / 32 blocks holds the 16-byte nibble fields of
  * blocks 0..nb-1 (block j at byte 16 j), then their fp16 scales (block j at

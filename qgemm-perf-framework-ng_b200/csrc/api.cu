@@ -203,6 +203,91 @@ int run_matmul(int wtype, const void *w, const void *a, const float *x, int64_t 
     return status_of(e);
 }
 
+static_assert(PFNG_B200_OUT_F32 == kOutF32 && PFNG_B200_OUT_F16 == kOutF16 && PFNG_B200_OUT_BF16 == kOutBF16 &&
+                  PFNG_B200_OUT_Q8_0 == kOutQ8_0,
+              "output format codes");
+
+// fp32 C scratch the non-fused paths need for an output format.
+size_t c_scratch_bytes(int64_t m, int64_t n) { return static_cast<size_t>(m) * static_cast<size_t>(n) * 4 + 256; }
+
+// Workspace of a resolved path writing output format `fmt`: the MMA GEMM
+// converts in its epilogue; GEMV and SIMPLE write fp32 C to scratch first.
+size_t out_workspace_for(int wtype, int fmt, int64_t m, int64_t n, int64_t k, int resolved, bool f32) {
+    const size_t base = workspace_for(wtype, m, k, resolved, f32);
+    if (fmt == kOutF32 || resolved == PFNG_B200_PATH_MMA || m == 0 || n == 0) return base;
+    return round_up(static_cast<int64_t>(base), 256) + c_scratch_bytes(m, n);
+}
+
+// The shared body of mm_out / compute_out.
+int run_matmul_out(int wtype, const void *w, const void *a, const float *x, int64_t ldx, void *out, int fmt,
+                   int64_t ldo, int64_t m, int64_t n, int64_t k, void *workspace, size_t workspace_bytes, int path,
+                   cudaStream_t s) {
+    if (fmt < kOutF32 || fmt > kOutQ8_0) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    if (fmt == kOutF32)
+        return run_matmul(wtype, w, a, x, ldx, static_cast<float *>(out), ldo, nullptr, m, n, k, workspace,
+                          workspace_bytes, path, s);
+    const bool f32 = x != nullptr;
+    // the common checks, with a stand-in for C: ldo and the (2-byte)
+    // alignment of out are checked per format below
+    const void *c_probe = out ? reinterpret_cast<const void *>(uintptr_t{256}) : nullptr;
+    int st = check_mm(wtype, w, f32 ? static_cast<const void *>(x) : a, c_probe, m, n, k, n, ldx, f32, false, path);
+    if (st != PFNG_B200_OK) return st;
+    if (fmt == kOutQ8_0 && n % 32 != 0) return PFNG_B200_ERR_SHAPE;
+    if (m > 0 && ldo < (fmt == kOutQ8_0 ? n / 32 : n)) return PFNG_B200_ERR_SHAPE;
+    if (m == 0 || n == 0) return PFNG_B200_OK;
+    if (!aligned(out, 2)) return PFNG_B200_ERR_ALIGNMENT;
+    if (!w || !(f32 ? static_cast<const void *>(x) : a)) {
+        if (k != 0) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    }
+    DeviceInfo *info = nullptr;
+    if ((st = device_info(&info)) != PFNG_B200_OK) return st;
+    const int resolved = k == 0 ? PFNG_B200_PATH_SIMPLE : resolve_path(wtype, m, n, k, w, path);
+    if (resolved < 0) return PFNG_B200_ERR_UNSUPPORTED;
+    const size_t need = out_workspace_for(wtype, fmt, m, n, k, resolved, f32);
+    if (need > 0 && (!workspace || workspace_bytes < need)) return PFNG_B200_ERR_WORKSPACE;
+    cudaError_t e = cudaSuccess;
+    if (resolved == PFNG_B200_PATH_MMA) {
+        const int qk = block_k(wtype);
+        const SplitA sa = split_a_carve(workspace, m, k, qk);
+        if (q8_0_act(wtype))
+            e = f32 ? launch_quantize_q8_0_split(x, ldx, sa, m, k, s) : launch_convert_q8_0_split(a, sa, m, k, s);
+        else
+            e = f32 ? launch_quantize_q8_K_split(x, ldx, sa, m, k, s) : launch_convert_q8_K_split(a, sa, m, k, s);
+        if (e == cudaSuccess) {
+            GemmArgs g{wtype, w, sa, nullptr, 0, nullptr, m, n, k, info->error_word};
+            g.out_format = fmt;
+            g.out = out;
+            g.ldo = ldo;
+            e = launch_gemm(g, s);
+        }
+        return status_of(e);
+    }
+    // fp32 C into scratch behind the path's own workspace, then convert
+    const size_t base = workspace_for(wtype, m, k, resolved, f32);
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    float *cs = static_cast<float *>(align_ptr(ws + round_up(static_cast<int64_t>(base), 256), 256));
+    st = run_matmul(wtype, w, a, x, ldx, cs, n, nullptr, m, n, k, workspace, base, resolved, s);
+    if (st != PFNG_B200_OK) return st;
+    e = fmt == kOutQ8_0 ? launch_quantize_q8_0_strided(cs, n, out, ldo, m, n, s)
+                        : launch_convert_out(cs, n, out, ldo, fmt, m, n, s);
+    return status_of(e);
+}
+
+size_t query_out_workspace(int wtype, int fmt, int64_t m, int64_t n, int64_t k, int path, bool f32) {
+    if (!valid_wtype(wtype) || fmt < kOutF32 || fmt > kOutQ8_0 || m <= 0 || n <= 0 || k <= 0) return 0;
+    if (path == PFNG_B200_PATH_AUTO) {
+        size_t best = 0;
+        for (int cand : {PFNG_B200_PATH_GEMV, PFNG_B200_PATH_MMA, PFNG_B200_PATH_SIMPLE}) {
+            if (cand == PFNG_B200_PATH_GEMV && m > 8) continue;
+            if (cand == PFNG_B200_PATH_MMA && m <= 8) continue;
+            const size_t need = out_workspace_for(wtype, fmt, m, n, k, cand, f32);
+            best = need > best ? need : best;
+        }
+        return best;
+    }
+    return out_workspace_for(wtype, fmt, m, n, k, path, f32);
+}
+
 size_t query_workspace(int wtype, int64_t m, int64_t n, int64_t k, int path, bool f32) {
     if (!valid_wtype(wtype) || m <= 0 || n <= 0 || k <= 0) return 0;
     if (path == PFNG_B200_PATH_AUTO) {
@@ -427,6 +512,28 @@ int pfng_b200_partials_iq2_xxs_q8_K(const void *w, const void *a, int32_t *out, 
                                     void *workspace, size_t workspace_bytes, int path, void *stream) {
     return run_matmul(PFNG_B200_IQ2_XXS, w, a, nullptr, 0, nullptr, n, out, m, n, k, workspace, workspace_bytes,
                       path, static_cast<cudaStream_t>(stream));
+}
+
+size_t pfng_b200_mm_out_workspace_size(int wtype, int out_format, int64_t m, int64_t n, int64_t k, int path) {
+    return query_out_workspace(wtype, out_format, m, n, k, path, false);
+}
+
+size_t pfng_b200_compute_out_workspace_size(int wtype, int out_format, int64_t m, int64_t n, int64_t k, int path) {
+    return query_out_workspace(wtype, out_format, m, n, k, path, true);
+}
+
+int pfng_b200_mm_out(int wtype, const void *w, const void *a, void *out, int out_format, int64_t ldo, int64_t m,
+                     int64_t n, int64_t k, void *workspace, size_t workspace_bytes, int path, void *stream) {
+    return run_matmul_out(wtype, w, a, nullptr, 0, out, out_format, ldo, m, n, k, workspace, workspace_bytes, path,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int pfng_b200_compute_out(int wtype, const void *w, const float *x, int64_t ldx, void *out, int out_format,
+                          int64_t ldo, int64_t m, int64_t n, int64_t k, void *workspace, size_t workspace_bytes,
+                          int path, void *stream) {
+    if (!x && m > 0 && n > 0 && k > 0) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    return run_matmul_out(wtype, w, nullptr, x, ldx, out, out_format, ldo, m, n, k, workspace, workspace_bytes, path,
+                          static_cast<cudaStream_t>(stream));
 }
 
 int pfng_b200_mm_q4_0p_q8_0(const void *w_planar, const void *a, float *c, int64_t m, int64_t n, int64_t k,

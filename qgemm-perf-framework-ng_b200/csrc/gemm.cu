@@ -31,9 +31,12 @@
 #include <cstdlib>
 #include <cstring>
 
+#include <cuda_bf16.h>
+
 #include "iq2xxs_grid_codes.h"
 #include "pfng_common.cuh"
 #include "pfng_internal.h"
+#include "pfng_quant.cuh"
 
 namespace pfng {
 namespace {
@@ -83,6 +86,9 @@ struct GemmParams {
     uint32_t step_bytes;  // raw weight bytes per row per k-step
     int w_vec16;          // 1: every row chunk is 16-byte aligned
     int64_t w_total;      // bytes of W
+    int out_format;       // kOutF32 (C in c) or another output format (in out)
+    void *out;
+    int64_t ldo;          // elements (fp16 / bf16) or blocks (q8_0)
 };
 
 PFNG_DEV void cp_async16(void *dst, const void *src, uint32_t src_bytes) {
@@ -344,6 +350,11 @@ PFNG_DEV void load_frags(const int8_t *at, const int8_t *bt, int kb, int wm, int
     }
 }
 
+template <class C>
+PFNG_DEV void epilogue_q8_0(const GemmParams &p, uint8_t *smem, const float2 (&acc)[C::MT][C::NT][2], int64_t m0,
+                            int64_t n0, int tid);
+PFNG_DEV void store_out2(const GemmParams &p, int64_t r, int64_t c, float2 v);
+
 template <int WT, class C, bool kPartials>
 __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -506,6 +517,10 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
     cp_async_wait<0>();
 
     if constexpr (!kPartials) {
+        if (p.out_format == kOutQ8_0) {
+            epilogue_q8_0<C>(p, smem_raw, acc, m0, n0, tid);
+            return;
+        }
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -514,10 +529,66 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
                 for (int h = 0; h < 2; ++h) {
                     const int64_t r = m0 + wm * C::WM + mt * 16 + g + 8 * h;
                     const int64_t c = n0 + wn * C::WN + nt * 8 + 2 * t4;
-                    if (r >= p.m) continue;
-                    if (c < p.n) p.c[r * p.ldc + c] = acc[mt][nt][h].x;
-                    if (c + 1 < p.n) p.c[r * p.ldc + c + 1] = acc[mt][nt][h].y;
+                    if (r < p.m) store_out2(p, r, c, acc[mt][nt][h]);
                 }
+    }
+}
+
+// C tile of the CTA quantized to q8_0 along n: the tile is staged in shared
+// memory (the main loop's buffers are free by then), then each warp
+// quantizes four 32-column blocks at a time with the standalone quantizer's
+// core, so the bytes are those of pfng_b200_quantize_q8_0 on the fp32 C.
+template <class C>
+PFNG_DEV void epilogue_q8_0(const GemmParams &p, uint8_t *smem, const float2 (&acc)[C::MT][C::NT][2], int64_t m0,
+                            int64_t n0, int tid) {
+    constexpr int CS = C::BN + 4;  // row stride of the staged tile (floats)
+    static_assert(C::BM * CS * 4 <= C::kSmem, "staged C tile");
+    const int warp = tid >> 5, lane = tid & 31, wm = warp >> 2, wn = warp & 3, g = lane >> 2, t4 = lane & 3;
+    float *ct = reinterpret_cast<float *>(smem);
+    __syncthreads();  // every warp is past its last read of the stage buffers
+#pragma unroll
+    for (int mt = 0; mt < C::MT; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < C::NT; ++nt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int row = wm * C::WM + mt * 16 + g + 8 * h, col = wn * C::WN + nt * 8 + 2 * t4;
+                *reinterpret_cast<float2 *>(ct + row * CS + col) = acc[mt][nt][h];
+            }
+    __syncthreads();
+    constexpr int kBlocks = C::BM * C::BN / 32;  // a multiple of 32: every warp runs the same trip count
+    const int gl = lane & 7;
+    for (int b0 = warp * 4; b0 < kBlocks; b0 += (kThreads / 32) * 4) {
+        const int bi = b0 + (lane >> 3);
+        const int row = bi / (C::BN / 32), blk = bi % (C::BN / 32);
+        const float4 t = *reinterpret_cast<const float4 *>(ct + row * CS + blk * 32 + 4 * gl);
+        const float v[4] = {t.x, t.y, t.z, t.w};
+        const Q8_0Lane r = q8_0_quantize_lane(v);
+        const int64_t grow = m0 + row, gcol = n0 + blk * 32;
+        if (grow < p.m && gcol < p.n) {
+            uint8_t *b = static_cast<uint8_t *>(p.out) + (grow * p.ldo + gcol / 32) * kQ8_0Bytes;
+            uint16_t *hq = reinterpret_cast<uint16_t *>(b + 2 + 4 * gl);
+            hq[0] = static_cast<uint16_t>(r.q & 0xffffu);
+            hq[1] = static_cast<uint16_t>(r.q >> 16);
+            if (gl == 0) *reinterpret_cast<uint16_t *>(b) = r.dbits;
+        }
+    }
+}
+
+// Two adjacent outputs (r, c), (r, c + 1) in the requested format; c + 1 may
+// be past n.
+PFNG_DEV void store_out2(const GemmParams &p, int64_t r, int64_t c, float2 v) {
+    if (p.out_format == kOutF32) {
+        if (c < p.n) p.c[r * p.ldc + c] = v.x;
+        if (c + 1 < p.n) p.c[r * p.ldc + c + 1] = v.y;
+    } else if (p.out_format == kOutF16) {
+        __half *o = static_cast<__half *>(p.out) + r * p.ldo + c;
+        if (c < p.n) o[0] = __float2half_rn(v.x);
+        if (c + 1 < p.n) o[1] = __float2half_rn(v.y);
+    } else {
+        __nv_bfloat16 *o = static_cast<__nv_bfloat16 *>(p.out) + r * p.ldo + c;
+        if (c < p.n) o[0] = __float2bfloat16_rn(v.x);
+        if (c + 1 < p.n) o[1] = __float2bfloat16_rn(v.y);
     }
 }
 
@@ -579,7 +650,7 @@ bool gemm_supported(int wtype, int64_t m, int64_t n, int64_t k, const void *w) {
 // environment variable PFNG_B200_GEMM is "mma" (or the shape is unsupported);
 // "tc" / "mma" select either kernel explicitly, for comparisons.
 static bool use_tc(const GemmArgs &args) {
-    if (args.wtype != kWQ4_0 || args.partials) return false;
+    if (args.wtype != kWQ4_0 || args.partials || args.out_format != kOutF32) return false;
     const char *e = std::getenv("PFNG_B200_GEMM");
     const bool want = e ? std::strcmp(e, "tc") == 0 : kTcDefault;
     return want && gemm_tc_supported(args.wtype, args.m, args.n, args.k, args.w);
@@ -600,6 +671,9 @@ cudaError_t launch_gemm(const GemmArgs &args, cudaStream_t s) {
     p.step_bytes = static_cast<uint32_t>(row_bytes_of(args.wtype, BK));
     p.w_total = p.row_bytes * args.n;
     p.w_vec16 = (p.row_bytes % 16 == 0 && p.step_bytes % 16 == 0) ? 1 : 0;
+    p.out_format = args.out_format;
+    p.out = args.out;
+    p.ldo = args.ldo;
     const bool part = args.partials != nullptr;
     switch (args.wtype) {
     case kWQ4_0: return part ? launch_tile<kWQ4_0, true>(p, s) : launch_tile<kWQ4_0, false>(p, s);

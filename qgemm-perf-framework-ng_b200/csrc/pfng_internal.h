@@ -35,6 +35,12 @@ cudaError_t launch_quantize_q8_0_split(const float *x, int64_t ldx, const SplitA
                                        cudaStream_t s);
 cudaError_t launch_quantize_q8_K_split(const float *x, int64_t ldx, const SplitA &out, int64_t m, int64_t k,
                                        cudaStream_t s);
+// fp32 -> q8_0 blocks with an output row stride of ldy blocks
+cudaError_t launch_quantize_q8_0_strided(const float *x, int64_t ldx, void *y, int64_t ldy, int64_t m, int64_t k,
+                                         cudaStream_t s);
+// fp32 C [m][ldc] -> fp16 / bf16 out [m][ldo] (round to nearest even)
+cudaError_t launch_convert_out(const float *c, int64_t ldc, void *out, int64_t ldo, int format, int64_t m, int64_t n,
+                               cudaStream_t s);
 // raw blocks -> split operand
 cudaError_t launch_convert_q8_0_split(const void *a, const SplitA &out, int64_t m, int64_t k, cudaStream_t s);
 cudaError_t launch_convert_q8_K_split(const void *a, const SplitA &out, int64_t m, int64_t k, cudaStream_t s);
@@ -62,6 +68,9 @@ struct GemvArgs {
 bool gemv_supported(int wtype, int64_t m, int count, const int64_t *n, int64_t k, const void *const *w);
 cudaError_t launch_gemv(const GemvArgs &args, cudaStream_t s);
 
+// Output formats of the matmul result (the PFNG_B200_OUT_* codes).
+constexpr int kOutF32 = 0, kOutF16 = 1, kOutBF16 = 2, kOutQ8_0 = 3;
+
 // gemm.cu -- tensor-core GEMM on a split activation operand.
 struct GemmArgs {
     int wtype;
@@ -72,6 +81,11 @@ struct GemmArgs {
     int32_t *partials;
     int64_t m, n, k;
     int *err = nullptr;  // library error word for bounded waits (tensor-memory kernel)
+    // fused epilogue: kOutF32 writes c; other formats write out with row
+    // stride ldo (elements, or q8_0 blocks along n)
+    int out_format = kOutF32;
+    void *out = nullptr;
+    int64_t ldo = 0;
 };
 bool gemm_supported(int wtype, int64_t m, int64_t n, int64_t k, const void *w);
 cudaError_t launch_gemm(const GemmArgs &args, cudaStream_t s);

@@ -9,6 +9,8 @@
 // fp16 scale uses round-to-nearest-even.  Reductions (max, min, sums) are
 // order-independent except for ties, which are broken toward the lowest
 // index exactly as the reference's sequential loops do.
+#include <cuda_bf16.h>
+
 #include "pfng_common.cuh"
 #include "pfng_internal.h"
 #include "pfng_quant.cuh"
@@ -31,7 +33,7 @@ PFNG_DEV void load4(const float *p, float v[4]) {
 
 template <bool kVec, bool kSplit>
 __global__ void __launch_bounds__(kThreads) quantize_q8_0_kernel(const float *__restrict__ x, int64_t ldx,
-                                                                  uint8_t *__restrict__ y, SplitA split,
+                                                                  uint8_t *__restrict__ y, int64_t ldy, SplitA split,
                                                                   int64_t m, int64_t k, int64_t rows) {
     const int64_t nb = k / 32;
     const int64_t total = rows * nb;
@@ -56,7 +58,7 @@ __global__ void __launch_bounds__(kThreads) quantize_q8_0_kernel(const float *__
                 split.aux[row * nb + col] = 0x4B400000 - 8 * r.qsum;
             }
         } else {
-            uint8_t *blk = y + bi * kQ8_0Bytes;
+            uint8_t *blk = y + (row * ldy + col) * kQ8_0Bytes;
             uint16_t *h = reinterpret_cast<uint16_t *>(blk + 2 + 4 * g);
             h[0] = static_cast<uint16_t>(r.q & 0xffffu);
             h[1] = static_cast<uint16_t>(r.q >> 16);
@@ -322,6 +324,23 @@ __global__ void __launch_bounds__(kThreads) quantize_q4_K_kernel(const float *__
     }
 }
 
+// fp32 C -> fp16 / bf16, round to nearest even (cuda_fp16 / cuda_bf16
+// conversions); one thread per element.
+template <bool kBf16>
+__global__ void __launch_bounds__(kThreads) convert_out_kernel(const float *__restrict__ c, int64_t ldc, void *out,
+                                                                int64_t ldo, int64_t m, int64_t n) {
+    const int64_t total = m * n;
+    for (int64_t e = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x; e < total;
+         e += static_cast<int64_t>(gridDim.x) * kThreads) {
+        const int64_t r = e / n, col = e % n;
+        const float v = c[r * ldc + col];
+        if constexpr (kBf16)
+            static_cast<__nv_bfloat16 *>(out)[r * ldo + col] = __float2bfloat16_rn(v);
+        else
+            static_cast<__half *>(out)[r * ldo + col] = __float2half_rn(v);
+    }
+}
+
 int grid_for(int64_t work_items, int items_per_block) {
     const int64_t blocks = (work_items + items_per_block - 1) / items_per_block;
     const int64_t cap = static_cast<int64_t>(device_sm_count()) * 8;
@@ -332,14 +351,30 @@ bool vec_ok(const float *x, int64_t ldx) { return (reinterpret_cast<uintptr_t>(x
 
 }  // namespace
 
-cudaError_t launch_quantize_q8_0(const float *x, int64_t ldx, void *y, int64_t m, int64_t k, cudaStream_t s) {
+cudaError_t launch_quantize_q8_0_strided(const float *x, int64_t ldx, void *y, int64_t ldy, int64_t m, int64_t k,
+                                         cudaStream_t s) {
     const int64_t blocks = m * (k / 32);
     const int grid = grid_for(blocks, kThreads / 8);
     SplitA none{};
+    uint8_t *out = static_cast<uint8_t *>(y);
     if (vec_ok(x, ldx))
-        quantize_q8_0_kernel<true, false><<<grid, kThreads, 0, s>>>(x, ldx, static_cast<uint8_t *>(y), none, m, k, m);
+        quantize_q8_0_kernel<true, false><<<grid, kThreads, 0, s>>>(x, ldx, out, ldy, none, m, k, m);
     else
-        quantize_q8_0_kernel<false, false><<<grid, kThreads, 0, s>>>(x, ldx, static_cast<uint8_t *>(y), none, m, k, m);
+        quantize_q8_0_kernel<false, false><<<grid, kThreads, 0, s>>>(x, ldx, out, ldy, none, m, k, m);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_q8_0(const float *x, int64_t ldx, void *y, int64_t m, int64_t k, cudaStream_t s) {
+    return launch_quantize_q8_0_strided(x, ldx, y, k / 32, m, k, s);
+}
+
+cudaError_t launch_convert_out(const float *c, int64_t ldc, void *out, int64_t ldo, int format, int64_t m, int64_t n,
+                               cudaStream_t s) {
+    const int grid = grid_for(m * n, kThreads);
+    if (format == kOutBF16)
+        convert_out_kernel<true><<<grid, kThreads, 0, s>>>(c, ldc, out, ldo, m, n);
+    else
+        convert_out_kernel<false><<<grid, kThreads, 0, s>>>(c, ldc, out, ldo, m, n);
     return cudaGetLastError();
 }
 
@@ -348,9 +383,9 @@ cudaError_t launch_quantize_q8_0_split(const float *x, int64_t ldx, const SplitA
     const int64_t blocks = out.rows_pad * (k / 32);
     const int grid = grid_for(blocks, kThreads / 8);
     if (vec_ok(x, ldx))
-        quantize_q8_0_kernel<true, true><<<grid, kThreads, 0, s>>>(x, ldx, nullptr, out, m, k, out.rows_pad);
+        quantize_q8_0_kernel<true, true><<<grid, kThreads, 0, s>>>(x, ldx, nullptr, 0, out, m, k, out.rows_pad);
     else
-        quantize_q8_0_kernel<false, true><<<grid, kThreads, 0, s>>>(x, ldx, nullptr, out, m, k, out.rows_pad);
+        quantize_q8_0_kernel<false, true><<<grid, kThreads, 0, s>>>(x, ldx, nullptr, 0, out, m, k, out.rows_pad);
     return cudaGetLastError();
 }
 

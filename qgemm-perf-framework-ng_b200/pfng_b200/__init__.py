@@ -37,6 +37,9 @@ LAYOUT = {
     Q4_0_PLANAR: (Q4_0_BYTES, 32, Q8_0_BYTES, 32),  # same bytes per row as q4_0, reordered
 }
 
+OUT_F32, OUT_F16, OUT_BF16, OUT_Q8_0 = 0, 1, 2, 3
+OUT_FORMATS = {"f32": OUT_F32, "f16": OUT_F16, "bf16": OUT_BF16, "q8_0": OUT_Q8_0}
+
 OK = 0
 ERR_KERNEL_TIMEOUT = -6
 OVERLAP_WEIGHTS = 1
@@ -90,6 +93,14 @@ def _declare(L: ctypes.CDLL) -> None:
         f = getattr(L, f"pfng_b200_compute_{t}")
         f.restype = I
         f.argtypes = [P, P, I64, P, I64, I64, I64, I64, P, S, I, P]
+    for name in ("mm_out_workspace_size", "compute_out_workspace_size"):
+        f = getattr(L, f"pfng_b200_{name}")
+        f.restype = S
+        f.argtypes = [I, I, I64, I64, I64, I]
+    L.pfng_b200_mm_out.restype = I
+    L.pfng_b200_mm_out.argtypes = [I, P, P, P, I, I64, I64, I64, I64, P, S, I, P]
+    L.pfng_b200_compute_out.restype = I
+    L.pfng_b200_compute_out.argtypes = [I, P, P, I64, P, I, I64, I64, I64, I64, P, S, I, P]
     for name in ("pack_q4_0_planar", "unpack_q4_0_planar"):
         f = getattr(L, f"pfng_b200_{name}")
         f.restype = I
@@ -239,6 +250,47 @@ def compute(wtype, w, x, n: int, out=None, path="auto", workspace=None, stream=N
     _check(getattr(lib(), f"pfng_b200_compute_{name}")(
         _ptr(w), _ptr(x), x.stride(0), _ptr(out), m, n, k, out.stride(0), _ptr(ws), nbytes, p,
         _stream(stream)), f"compute_{name}")
+    return out
+
+
+def _fmt(out_format) -> int:
+    return OUT_FORMATS[out_format] if isinstance(out_format, str) else int(out_format)
+
+
+def _out_tensor(fmt: int, m: int, n: int, device):
+    import torch
+    if fmt == OUT_Q8_0:
+        return torch.empty(m * (n // 32) * Q8_0_BYTES, dtype=torch.uint8, device=device)
+    dt = {OUT_F32: torch.float32, OUT_F16: torch.float16, OUT_BF16: torch.bfloat16}[fmt]
+    return torch.empty((m, n), dtype=dt, device=device)
+
+
+def _ldo(fmt: int, out, n: int) -> int:
+    return n // 32 if fmt == OUT_Q8_0 else out.stride(0)
+
+
+def mm_out(wtype, w, a, m: int, n: int, k: int, out_format, out=None, path="auto", workspace=None, stream=None):
+    """mm() with the result written as fp32 / fp16 / bf16 or q8_0 blocks along n (fused epilogue)."""
+    wt, p, fmt = _wt(wtype), _path(path), _fmt(out_format)
+    if out is None:
+        out = _out_tensor(fmt, m, n, w.device)
+    ws = _workspace(lib().pfng_b200_mm_out_workspace_size(wt, fmt, m, n, k, p), w.device, workspace)
+    nbytes = 0 if ws is None else ws.numel()
+    _check(lib().pfng_b200_mm_out(wt, _ptr(w), _ptr(a), _ptr(out), fmt, _ldo(fmt, out, n), m, n, k, _ptr(ws),
+                                  nbytes, p, _stream(stream)), "mm_out")
+    return out
+
+
+def compute_out(wtype, w, x, n: int, out_format, out=None, path="auto", workspace=None, stream=None):
+    """compute() with the result written as fp32 / fp16 / bf16 or q8_0 blocks along n (fused epilogue)."""
+    wt, p, fmt = _wt(wtype), _path(path), _fmt(out_format)
+    m, k = x.shape
+    if out is None:
+        out = _out_tensor(fmt, m, n, w.device)
+    ws = _workspace(lib().pfng_b200_compute_out_workspace_size(wt, fmt, m, n, k, p), w.device, workspace)
+    nbytes = 0 if ws is None else ws.numel()
+    _check(lib().pfng_b200_compute_out(wt, _ptr(w), _ptr(x), x.stride(0), _ptr(out), fmt, _ldo(fmt, out, n), m, n,
+                                       k, _ptr(ws), nbytes, p, _stream(stream)), "compute_out")
     return out
 
 

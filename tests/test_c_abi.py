@@ -137,3 +137,21 @@ def test_planar_argument_checks(L):
     ldc = (ctypes.c_int64 * 1)(4)
     assert grouped(4, 1, ptrs, n, ptrs, ldc, FAKE, 256, 1, 256, 0, None) == INVALID
     assert grouped(3, 1, ptrs, n, ptrs, ldc, FAKE, 256, 1, 96, 0, None) == SHAPE
+
+
+def test_output_format_argument_checks(L):
+    mm, comp = L.pfng_b200_mm_out, L.pfng_b200_compute_out
+    assert mm(0, FAKE, FAKE, FAKE, 4, 64, 4, 64, 256, None, 0, 0, None) == INVALID      # unknown format
+    assert mm(0, FAKE, FAKE, FAKE, 3, 2, 4, 48, 256, None, 0, 0, None) == SHAPE        # q8_0 needs n % 32 == 0
+    assert mm(0, FAKE, FAKE, FAKE, 3, 1, 4, 64, 256, None, 0, 0, None) == SHAPE        # ldo < n / 32 blocks
+    assert mm(0, FAKE, FAKE, FAKE, 1, 63, 4, 64, 256, None, 0, 0, None) == SHAPE       # ldo < n halves
+    assert mm(0, FAKE, FAKE, FAKE + 1, 1, 64, 4, 64, 256, None, 0, 0, None) == ALIGN   # 2-byte outputs
+    assert mm(0, FAKE + 1, FAKE, FAKE, 1, 64, 4, 64, 256, None, 0, 0, None) == ALIGN   # W still checked
+    assert mm(0, None, FAKE, FAKE, 2, 64, 4, 64, 256, None, 0, 0, None) == INVALID
+    assert mm(0, None, None, None, 3, 2, 0, 64, 256, None, 0, 0, None) == OK          # empty
+    assert comp(0, FAKE, FAKE, 128, FAKE, 1, 64, 4, 64, 256, None, 0, 0, None) == SHAPE  # ldx < k
+    # workspace: GEMV / SIMPLE keep an fp32 C scratch, the tensor-core GEMM converts in its epilogue
+    assert pb.lib().pfng_b200_compute_out_workspace_size(0, 1, 1, 4096, 4096, 1) >= 4096 * 4
+    assert pb.lib().pfng_b200_compute_out_workspace_size(0, 0, 1, 4096, 4096, 1) == 0
+    fused = pb.lib().pfng_b200_compute_out_workspace_size(0, 3, 480, 1536, 1536, 2)
+    assert fused == pb.compute_workspace_size("q4_0", 480, 1536, 1536, "mma")
