@@ -764,6 +764,160 @@ PFNG_DEV void rows_q4_0p_smem(const GemvParams &p, const Out &o, const uint8_t *
     }
 }
 
+// ---------------------------------------------------------------------------
+// q4_K, m = 1, k <= 4096: activations in registers.  Lane l of iteration i
+// takes the unit (block b = 8 i + l / 4, nibble pair pr = l & 3): the 32
+// nibble bytes at 16 + 32 pr of the block, whose low nibbles are sub-block
+// 2 pr and high nibbles sub-block 2 pr + 1.  A warp's units of one iteration
+// cover eight whole blocks (16-byte reads, 4 lanes per 16-byte bank slot).
+// Same integer sums as row_q4_K; the min term sum_j m_j * bsum_j of the two
+// sub-blocks is one dp2a over the packed mins and sub-block sums.
+// ---------------------------------------------------------------------------
+template <int NI>
+struct ActRegsK {
+    uint4 a0[NI][2];  // 32 activations of sub-block 2 pr
+    uint4 a1[NI][2];  // 32 activations of sub-block 2 pr + 1
+    float d[NI];      // the block's activation scale
+    int bs[NI];       // sums of the two sub-blocks' activations, two int16
+};
+
+// Weights of one row's units: the block header (d, dmin, 12 scale bytes) and
+// the unit's 32 nibble bytes.
+template <int NI, int R = 2>
+struct RowsWK {
+    uint4 hd[NI][R];    // [.][row]
+    uint4 q[NI][R][2];  // [.][row][half]
+};
+
+template <int NI>
+PFNG_DEV void load_act_q4_K(const GemvParams &p, const uint8_t *act, int lane, ActRegsK<NI> &ar) {
+    const int nbk = p.k / 256;
+    const int8_t *aqs = reinterpret_cast<const int8_t *>(act);
+    const float *ad = reinterpret_cast<const float *>(aqs + p.k);
+    const int16_t *abs16 = reinterpret_cast<const int16_t *>(ad + nbk);
+    const int pr = lane & 3;
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+        const int b = 8 * i + (lane >> 2);
+        if (b < nbk) {
+            const uint4 *a = reinterpret_cast<const uint4 *>(aqs + b * 256 + 64 * pr);
+            ar.a0[i][0] = a[0], ar.a0[i][1] = a[1], ar.a1[i][0] = a[2], ar.a1[i][1] = a[3];
+            ar.d[i] = ad[b];
+            const int16_t *bs = abs16 + b * 16 + 4 * pr;
+            const int s0 = bs[0] + bs[1], s1 = bs[2] + bs[3];
+            ar.bs[i] = static_cast<int>((static_cast<uint32_t>(s0) & 0xffffu) | (static_cast<uint32_t>(s1) << 16));
+        } else {
+            ar.a0[i][0] = ar.a0[i][1] = ar.a1[i][0] = ar.a1[i][1] = make_uint4(0, 0, 0, 0);
+            ar.d[i] = 0.0f;
+            ar.bs[i] = 0;
+        }
+    }
+}
+
+// R rows from row_off on; rows at or past nrows repeat the last valid row
+// (loaded, never stored).
+template <int NI, int R>
+PFNG_DEV void load_rows_q4_K(const GemvParams &p, const uint8_t *tile, uint32_t row_off, int nrows, int lane,
+                             RowsWK<NI, R> &rw) {
+    const int nbk = p.k / 256;
+    const int pr = lane & 3;
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+        const int b = 8 * i + (lane >> 2);
+        if (b < nbk) {
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int rr = r < nrows ? r : nrows - 1;
+                const uint8_t *blk = tile + row_off + static_cast<uint32_t>(rr * p.row_bytes) + 144u * b;
+                rw.hd[i][r] = *reinterpret_cast<const uint4 *>(blk);
+                rw.q[i][r][0] = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * pr);
+                rw.q[i][r][1] = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * pr);
+            }
+        }
+    }
+}
+
+// 6-bit scales and mins of sub-blocks 2 pr and 2 pr + 1 (llama_reference.cpp
+// :116-121), two bytes each: hd.y, hd.z, hd.w are scale bytes 0-3, 4-7, 8-11.
+// For pr < 2: sc = q[j] & 63, m = q[j + 4] & 63; otherwise
+// sc = (q[j + 4] & 15) | (q[j - 4] >> 6) << 4, m = q[j + 4] >> 4 | (q[j] >> 6) << 4.
+PFNG_DEV void q4_K_scales_pair(const uint4 &hd, int pr, uint32_t &scpk, uint32_t &mpk) {
+    const bool lo = pr < 2;
+    const uint32_t sh = (pr & 1) * 16;
+    const uint32_t xa_sc = ((lo ? hd.y : hd.w) >> sh) & 0xffffu;
+    const uint32_t xa_m = ((lo ? hd.z : hd.w) >> sh) & 0xffffu;
+    const uint32_t xb_sc = (hd.y >> sh) & 0xffffu, xb_m = (hd.z >> sh) & 0xffffu;
+    scpk = lo ? (xa_sc & 0x3f3fu) : ((xa_sc & 0x0f0fu) | ((xb_sc >> 2) & 0x3030u));
+    mpk = lo ? (xa_m & 0x3f3fu) : (((xa_m >> 4) & 0x0f0fu) | ((xb_m >> 2) & 0x3030u));
+}
+
+template <int NI, int R, bool kPartials>
+PFNG_DEV void rows_q4_K_reg(const GemvParams &p, const Out &o, const ActRegsK<NI> &ar, const RowsWK<NI, R> &rw,
+                            int row0, int nrows, int lane) {
+    const int nbk = p.k / 256;
+    const int pr = lane & 3;
+    float acc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+        const int b = 8 * i + (lane >> 2);
+        if (b < nbk) {
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const uint4 q0 = rw.q[i][r][0], q1 = rw.q[i][r][1];
+                const uint4 l0 = ar.a0[i][0], l1 = ar.a0[i][1], h0 = ar.a1[i][0], h1 = ar.a1[i][1];
+                int ql = dp4a_us(q0.x & 0x0f0f0f0fu, static_cast<int>(l0.x), 0);
+                int qh = dp4a_us(q0.x & 0xf0f0f0f0u, static_cast<int>(h0.x), 0);
+                ql = dp4a_us(q0.y & 0x0f0f0f0fu, static_cast<int>(l0.y), ql);
+                qh = dp4a_us(q0.y & 0xf0f0f0f0u, static_cast<int>(h0.y), qh);
+                ql = dp4a_us(q0.z & 0x0f0f0f0fu, static_cast<int>(l0.z), ql);
+                qh = dp4a_us(q0.z & 0xf0f0f0f0u, static_cast<int>(h0.z), qh);
+                ql = dp4a_us(q0.w & 0x0f0f0f0fu, static_cast<int>(l0.w), ql);
+                qh = dp4a_us(q0.w & 0xf0f0f0f0u, static_cast<int>(h0.w), qh);
+                ql = dp4a_us(q1.x & 0x0f0f0f0fu, static_cast<int>(l1.x), ql);
+                qh = dp4a_us(q1.x & 0xf0f0f0f0u, static_cast<int>(h1.x), qh);
+                ql = dp4a_us(q1.y & 0x0f0f0f0fu, static_cast<int>(l1.y), ql);
+                qh = dp4a_us(q1.y & 0xf0f0f0f0u, static_cast<int>(h1.y), qh);
+                ql = dp4a_us(q1.z & 0x0f0f0f0fu, static_cast<int>(l1.z), ql);
+                qh = dp4a_us(q1.z & 0xf0f0f0f0u, static_cast<int>(h1.z), qh);
+                ql = dp4a_us(q1.w & 0x0f0f0f0fu, static_cast<int>(l1.w), ql);
+                qh = dp4a_us(q1.w & 0xf0f0f0f0u, static_cast<int>(h1.w), qh);
+                qh >>= 4;  // 16 x the high-nibble sum, exactly
+                if constexpr (kPartials) {
+                    if (r < nrows) {
+                        int32_t *out = p.partials + static_cast<int64_t>(row0 + r) * (p.k / 32) + b * 8 + 2 * pr;
+                        out[0] = ql;
+                        out[1] = qh;
+                    }
+                } else {
+                    uint32_t scpk, mpk;
+                    q4_K_scales_pair(rw.hd[i][r], pr, scpk, mpk);
+                    const int i1 = static_cast<int>(scpk & 0xffu) * ql + static_cast<int>(scpk >> 8) * qh;
+                    const int i2 = __dp2a_lo(ar.bs[i], static_cast<int>(mpk), 0);
+                    const float d = f16_bits_to_f32(rw.hd[i][r].x & 0xffffu);
+                    const float dmin = f16_bits_to_f32(rw.hd[i][r].x >> 16);
+                    const float part =
+                        __fsub_rn(__fmul_rn(d, static_cast<float>(i1)), __fmul_rn(dmin, static_cast<float>(i2)));
+                    acc[r] = __fmaf_rn(ar.d[i], part, acc[r]);
+                }
+            }
+        }
+    }
+    if constexpr (!kPartials) {
+        if constexpr (R == 4) {
+            reduce_store4(o, acc[0], acc[1], acc[2], acc[3], row0, nrows, lane);
+        } else {
+            const bool upper = (lane & 16) != 0;
+            float v = (upper ? acc[1] : acc[0]) + __shfl_xor_sync(0xffffffffu, upper ? acc[0] : acc[1], 16);
+#pragma unroll
+            for (int sh = 8; sh > 0; sh >>= 1) v += __shfl_xor_sync(0xffffffffu, v, sh);
+            if (lane == 0) o.c[row0] = v;
+            if (lane == 16 && nrows > 1) o.c[row0 + 1] = v;
+        }
+    }
+}
+
 PFNG_DEV uint32_t scale_byte(uint32_t s0, uint32_t s1, uint32_t s2, int i) {
     return (i < 8 ? __byte_perm(s0, s1, static_cast<uint32_t>(i)) : __byte_perm(s2, 0u, static_cast<uint32_t>(i - 8))) &
            0xffu;
@@ -1043,6 +1197,8 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
 
     ActRegs<(RG > 0 ? RG : 1)> ar;
     ActRegsP<(RG > 0 ? RG : 1)> arp;
+    ActRegsK<(RG > 0 ? RG : 1)> ark;
+    if constexpr (WT == kWQ4_K && RG > 0) load_act_q4_K<RG>(p, act, lane, ark);
     if constexpr (WT == kWQ4_0P && RG > 0) {
         const int nbp = p.groups * 32;
         const float *ad = reinterpret_cast<const float *>(act + nbp * 32);
@@ -1113,7 +1269,16 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
         // the stage's window starts at the tile's first byte rounded down to 16
         const uint32_t mis = (static_cast<uint32_t>(tile_row) * static_cast<uint32_t>(p.row_bytes)) & 15u;
         const uint8_t *buf = smem + p.stage_offset + static_cast<uint32_t>(stage) * p.stage_bytes;
-        if constexpr (WT == kWQ4_0P && RG > 0 && !kPartials && kClaimRows == 4 && PFNG_GEMV_CLAIM4) {
+        if constexpr (WT == kWQ4_K && RG > 0 && !kPartials && kClaimRows == 4 && PFNG_GEMV_CLAIM4) {
+            const int first = kClaimRows * qr;
+            const int nrows = tile_rows - first < kClaimRows ? tile_rows - first : kClaimRows;
+            const uint32_t row_off = static_cast<uint32_t>(first) * static_cast<uint32_t>(p.row_bytes) + mis;
+            RowsWK<RG, 4> rw;
+            if (nrows > 0) load_rows_q4_K<RG, 4>(p, buf, row_off, nrows, lane, rw);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[stage]);
+            if (nrows > 0) rows_q4_K_reg<RG, 4, kPartials>(p, o, ark, rw, tile_row + first, nrows, lane);
+        } else if constexpr (WT == kWQ4_0P && RG > 0 && !kPartials && kClaimRows == 4 && PFNG_GEMV_CLAIM4) {
             const int first = kClaimRows * qr;
             const int nrows = tile_rows - first < kClaimRows ? tile_rows - first : kClaimRows;
             const uint32_t row_off = static_cast<uint32_t>(first) * static_cast<uint32_t>(p.row_bytes) + mis;
@@ -1163,6 +1328,14 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
                     if (lane == 0) mbar_arrive(&empty[stage]);
                 }
                 if (nrows > 0) rows_q4_0p_reg<RG, kPartials>(p, o, arp, rw, row0, nrows, lane);
+            } else if constexpr (WT == kWQ4_K && RG > 0) {
+                RowsWK<RG, 2> rw;
+                if (nrows > 0) load_rows_q4_K<RG, 2>(p, buf, row_off, nrows, lane, rw);
+                if (last) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[stage]);
+                }
+                if (nrows > 0) rows_q4_K_reg<RG, 2, kPartials>(p, o, ark, rw, row0, nrows, lane);
             } else if constexpr (WT == kWQ4_0 && RG > 0) {
                 // copy the pair's weights to registers; after the claim's last
                 // pair is copied, release the stage, then compute
@@ -1302,6 +1475,11 @@ cudaError_t dispatch_flags(const GemvParams &p, uint32_t smem, bool partials, bo
 
 template <int WT>
 cudaError_t dispatch_mt(const GemvParams &p, uint32_t smem, bool partials, bool f32, cudaStream_t s) {
+    if constexpr (WT == kWQ4_K) {
+        // units of 64 values, 32 per iteration: k <= 4096 in two iterations
+        if (p.m == 1 && p.k <= 2048) return dispatch_flags<WT, 1, 1>(p, smem, partials, f32, s);
+        if (p.m == 1 && p.k <= 4096) return dispatch_flags<WT, 1, 2>(p, smem, partials, f32, s);
+    }
     if constexpr (WT == kWQ4_0P) {
         if (p.m == 1) {
             if (p.groups <= 1) return dispatch_flags<WT, 1, 1>(p, smem, partials, f32, s);

@@ -335,3 +335,21 @@ def test_q4_0_tcgen05_kernel(oracle, monkeypatch, m, n, k):
     c_mma = host(pb.compute("q4_0", wd, xd, n, path="mma"))
     check_close(c_tc, ref, bound, f"tcgen05 q4_0 {m}x{n}x{k}")
     np.testing.assert_array_equal(c_tc.view(np.uint32), c_mma.view(np.uint32))
+
+
+@pytest.mark.parametrize("wtype", ["q4_K", "iq2_xxs"])
+@pytest.mark.parametrize("n,k", [(4096, 4096), (1000, 2048), (520, 1536)])
+def test_k_types_decode(oracle, wtype, n, k):
+    # m = 1 decode shapes of the K-block types (register paths for k <= 4096):
+    # integer partials bit-exact, fp32 within tolerance, grouped == single
+    rng = np.random.default_rng(n + k)
+    w = make_weights(oracle, wtype, n, k, rng)
+    x = rng.standard_normal((1, k)).astype(np.float32)
+    a = oracle.quantize("q8_K", x)
+    wd, xd = dev_bytes(w), dev(x)
+    c = host(pb.compute(wtype, wd, xd, n, path="gemv"))
+    check_close(c, oracle.mm(wtype, w, a, 1, n, k), oracle.bound(wtype, w, a, 1, n, k), f"{wtype} decode {n}x{k}")
+    got = host(pb.partials(wtype, wd, dev_bytes(a), 1, n, k, path="gemv"))
+    np.testing.assert_array_equal(got, oracle.partials(wtype, w, a, 1, n, k))
+    g = host(pb.compute_grouped(wtype, [wd], xd, [n])[0])
+    np.testing.assert_array_equal(g.view(np.uint32), c.view(np.uint32))
