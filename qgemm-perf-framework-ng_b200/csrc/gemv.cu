@@ -97,7 +97,12 @@ constexpr int kTileRowsLong = PFNG_GEMV_TILE_ROWS;  // rows per tile when a row 
 static_assert(kTileRowsLong >= kClaimRows && (kTileRowsLong & (kTileRowsLong - 1)) == 0, "tile rows");
 constexpr int kMaxGroup = kGemvMaxGroup;
 constexpr uint32_t kBarrierBytes = 2 * kMaxStages * 8;
-constexpr uint32_t kGridTableBytes = 256 * 8;
+// iq2_xxs grid points (256 x 8 bytes), then the byte sign masks of the 128
+// sign indices (128 x 8 bytes).  Measured alternatives (decode step): 16
+// bank-striped copies of the grid with the masks computed in registers was
+// 5 % slower (16.5 vs 15.7 us) -- the lookups' bank conflicts are not the
+// limit, the instruction count is.
+constexpr uint32_t kGridTableBytes = 256 * 8 + 128 * 8;
 constexpr uint32_t kStageSlack = 32;  // bytes read past a window by aligned loads; never used
 constexpr int kRegGroupsMax = 2;      // m = 1 keeps up to 2 x 64 blocks (k <= 4096) in registers
 
@@ -1052,6 +1057,124 @@ PFNG_DEV void row_iq2_xxs(const GemvParams &p, const Out &o, const uint8_t *act,
     if constexpr (!kPartials) warp_reduce_store<MT>(p, o, acc, row, lane);
 }
 
+// ---------------------------------------------------------------------------
+// iq2_xxs, m = 1, k <= 4096: activations in registers.  Lane l of iteration i
+// takes the 32-value group sb = l & 7 of block b = 4 i + l / 8 (8 qs bytes at
+// 2 + 8 sb).  Signs come from the table of byte masks m (0xff = negative)
+// after the grid: with signed dp4a, (g ^ m) is g or -g - 1, so
+//   sum s g a = dp4a(g ^ m, a) + dp4a(m & 0x01010101, a)
+// per 4 values -- the same integer as applying the signs first.
+// ---------------------------------------------------------------------------
+template <int NI>
+struct ActRegsI {
+    uint4 a[NI][2];  // the lane's 32 activations of iteration i
+    float d[NI];     // their block's scale
+};
+
+template <int NI, int R>
+struct RowsWI {
+    uint32_t idx[NI][R];  // four grid indices
+    uint32_t ss[NI][R];   // four 7-bit sign indices and the 4-bit scale
+    uint32_t d[NI][R];    // fp16 block scale (bits)
+};
+
+template <int NI>
+PFNG_DEV void load_act_iq2(const GemvParams &p, const uint8_t *act, int lane, ActRegsI<NI> &ar) {
+    const int nbk = p.k / 256;
+    const int8_t *aqs = reinterpret_cast<const int8_t *>(act);
+    const float *ad = reinterpret_cast<const float *>(aqs + p.k);
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+        const int b = 4 * i + (lane >> 3), sb = lane & 7;
+        if (b < nbk) {
+            const uint4 *a = reinterpret_cast<const uint4 *>(aqs + b * 256 + 32 * sb);
+            ar.a[i][0] = a[0], ar.a[i][1] = a[1];
+            ar.d[i] = ad[b];
+        } else {
+            ar.a[i][0] = ar.a[i][1] = make_uint4(0, 0, 0, 0);
+            ar.d[i] = 0.0f;
+        }
+    }
+}
+
+template <int NI, int R>
+PFNG_DEV void load_rows_iq2(const GemvParams &p, const uint8_t *tile, uint32_t row_off, int nrows, int lane,
+                            RowsWI<NI, R> &rw) {
+    const int nbk = p.k / 256;
+    const int sb = lane & 7;
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+        const int b = 4 * i + (lane >> 3);
+        if (b < nbk) {
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int rr = r < nrows ? r : nrows - 1;
+                const uint32_t boff = row_off + static_cast<uint32_t>(rr * p.row_bytes) + 66u * b;
+                const uint32_t off = boff + 2 + 8 * sb;
+                const uint32_t *w = reinterpret_cast<const uint32_t *>(tile + (off & ~3u));
+                const uint32_t sh = (off & 2u) ? 16u : 0u;
+                const uint32_t w0 = w[0], w1 = w[1], w2 = w[2];
+                rw.idx[i][r] = __funnelshift_r(w0, w1, sh);
+                rw.ss[i][r] = __funnelshift_r(w1, w2, sh);
+                rw.d[i][r] = *reinterpret_cast<const uint16_t *>(tile + boff);
+            }
+        }
+    }
+}
+
+template <int NI, int R, bool kPartials>
+PFNG_DEV void rows_iq2_reg(const GemvParams &p, const Out &o, const ActRegsI<NI> &ar, const RowsWI<NI, R> &rw,
+                           int row0, int nrows, int lane, const uint2 *grid) {
+    const int nbk = p.k / 256;
+    const int sb = lane & 7;
+    float acc[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+        const int b = 4 * i + (lane >> 3);
+        if (b < nbk) {
+            const uint32_t av[8] = {ar.a[i][0].x, ar.a[i][0].y, ar.a[i][0].z, ar.a[i][0].w,
+                                    ar.a[i][1].x, ar.a[i][1].y, ar.a[i][1].z, ar.a[i][1].w};
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const uint32_t idx = rw.idx[i][r], ss = rw.ss[i][r];
+                int dot = 0, corr = 0;
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {
+                    const uint2 gv = grid[(idx >> (8 * g)) & 0xffu];
+                    const uint2 mk = grid[256 + ((ss >> (7 * g)) & 0x7fu)];
+                    dot = dp4a(static_cast<int>(gv.x ^ mk.x), static_cast<int>(av[2 * g]), dot);
+                    corr = dp4a(static_cast<int>(mk.x & 0x01010101u), static_cast<int>(av[2 * g]), corr);
+                    dot = dp4a(static_cast<int>(gv.y ^ mk.y), static_cast<int>(av[2 * g + 1]), dot);
+                    corr = dp4a(static_cast<int>(mk.y & 0x01010101u), static_cast<int>(av[2 * g + 1]), corr);
+                }
+                dot += corr;
+                if constexpr (kPartials) {
+                    if (r < nrows) p.partials[static_cast<int64_t>(row0 + r) * (p.k / 32) + b * 8 + sb] = dot;
+                } else {
+                    // llama_reference.cpp:160: 0.125 * d * a.d, times the scaled integer sum
+                    const int scale = 2 * static_cast<int>(ss >> 28) + 1;
+                    const float s = __fmul_rn(__fmul_rn(0.125f, f16_bits_to_f32(rw.d[i][r])), ar.d[i]);
+                    acc[r] = __fmaf_rn(s, static_cast<float>(scale * dot), acc[r]);
+                }
+            }
+        }
+    }
+    if constexpr (!kPartials) {
+        if constexpr (R == 4) {
+            reduce_store4(o, acc[0], acc[1], acc[2], acc[3], row0, nrows, lane);
+        } else {
+            const bool upper = (lane & 16) != 0;
+            float v = (upper ? acc[1] : acc[0]) + __shfl_xor_sync(0xffffffffu, upper ? acc[0] : acc[1], 16);
+#pragma unroll
+            for (int sh = 8; sh > 0; sh >>= 1) v += __shfl_xor_sync(0xffffffffu, v, sh);
+            if (lane == 0) o.c[row0] = v;
+            if (lane == 16 && nrows > 1) o.c[row0 + 1] = v;
+        }
+    }
+}
+
 // Waits until the producer has issued local tile i: 1 once it has, 0 if the
 // producer finished with fewer tiles, -1 (error recorded) if it never does.
 PFNG_DEV int wait_issued(const int *issued_count, const int *final_count, int i, int *err) {
@@ -1180,6 +1303,11 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
             }
             grid[i] = make_uint2(lo, hi);
         }
+        // byte masks (0xff = negative) of the 128 sign indices
+        for (int i = tid; i < 128; i += kConsumerThreads) {
+            const uint32_t sgn = iq2_sign_mask(static_cast<uint32_t>(i));
+            grid[256 + i] = make_uint2(expand_bits4(sgn), expand_bits4(sgn >> 4));
+        }
     }
     const uint8_t *act = smem + p.act_offset;
     if (p.overlap) asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -1199,6 +1327,8 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
     ActRegsP<(RG > 0 ? RG : 1)> arp;
     ActRegsK<(RG > 0 ? RG : 1)> ark;
     if constexpr (WT == kWQ4_K && RG > 0) load_act_q4_K<RG>(p, act, lane, ark);
+    ActRegsI<(RG > 0 ? RG : 1)> ari;
+    if constexpr (WT == kWIQ2 && RG > 0) load_act_iq2<RG>(p, act, lane, ari);
     if constexpr (WT == kWQ4_0P && RG > 0) {
         const int nbp = p.groups * 32;
         const float *ad = reinterpret_cast<const float *>(act + nbp * 32);
@@ -1269,7 +1399,16 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
         // the stage's window starts at the tile's first byte rounded down to 16
         const uint32_t mis = (static_cast<uint32_t>(tile_row) * static_cast<uint32_t>(p.row_bytes)) & 15u;
         const uint8_t *buf = smem + p.stage_offset + static_cast<uint32_t>(stage) * p.stage_bytes;
-        if constexpr (WT == kWQ4_K && RG > 0 && !kPartials && kClaimRows == 4 && PFNG_GEMV_CLAIM4) {
+        if constexpr (WT == kWIQ2 && RG > 0 && !kPartials && kClaimRows == 4 && PFNG_GEMV_CLAIM4) {
+            const int first = kClaimRows * qr;
+            const int nrows = tile_rows - first < kClaimRows ? tile_rows - first : kClaimRows;
+            const uint32_t row_off = static_cast<uint32_t>(first) * static_cast<uint32_t>(p.row_bytes) + mis;
+            RowsWI<RG, 4> rw;
+            if (nrows > 0) load_rows_iq2<RG, 4>(p, buf, row_off, nrows, lane, rw);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[stage]);
+            if (nrows > 0) rows_iq2_reg<RG, 4, kPartials>(p, o, ari, rw, tile_row + first, nrows, lane, grid);
+        } else if constexpr (WT == kWQ4_K && RG > 0 && !kPartials && kClaimRows == 4 && PFNG_GEMV_CLAIM4) {
             const int first = kClaimRows * qr;
             const int nrows = tile_rows - first < kClaimRows ? tile_rows - first : kClaimRows;
             const uint32_t row_off = static_cast<uint32_t>(first) * static_cast<uint32_t>(p.row_bytes) + mis;
@@ -1328,6 +1467,14 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
                     if (lane == 0) mbar_arrive(&empty[stage]);
                 }
                 if (nrows > 0) rows_q4_0p_reg<RG, kPartials>(p, o, arp, rw, row0, nrows, lane);
+            } else if constexpr (WT == kWIQ2 && RG > 0) {
+                RowsWI<RG, 2> rw;
+                if (nrows > 0) load_rows_iq2<RG, 2>(p, buf, row_off, nrows, lane, rw);
+                if (last) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[stage]);
+                }
+                if (nrows > 0) rows_iq2_reg<RG, 2, kPartials>(p, o, ari, rw, row0, nrows, lane, grid);
             } else if constexpr (WT == kWQ4_K && RG > 0) {
                 RowsWK<RG, 2> rw;
                 if (nrows > 0) load_rows_q4_K<RG, 2>(p, buf, row_off, nrows, lane, rw);
@@ -1475,6 +1622,12 @@ cudaError_t dispatch_flags(const GemvParams &p, uint32_t smem, bool partials, bo
 
 template <int WT>
 cudaError_t dispatch_mt(const GemvParams &p, uint32_t smem, bool partials, bool f32, cudaStream_t s) {
+    if constexpr (WT == kWIQ2) {
+        // units of 32 values, 32 per iteration: k <= 4096 in four iterations
+        if (p.m == 1 && p.k <= 1024) return dispatch_flags<WT, 1, 1>(p, smem, partials, f32, s);
+        if (p.m == 1 && p.k <= 2048) return dispatch_flags<WT, 1, 2>(p, smem, partials, f32, s);
+        if (p.m == 1 && p.k <= 4096) return dispatch_flags<WT, 1, 4>(p, smem, partials, f32, s);
+    }
     if constexpr (WT == kWQ4_K) {
         // units of 64 values, 32 per iteration: k <= 4096 in two iterations
         if (p.m == 1 && p.k <= 2048) return dispatch_flags<WT, 1, 1>(p, smem, partials, f32, s);
