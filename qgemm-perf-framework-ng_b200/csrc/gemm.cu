@@ -220,13 +220,22 @@ PFNG_DEV void store_pair(int8_t *bt, int row, int ca, uint4 va, int cb, uint4 vb
     *reinterpret_cast<uint4 *>(bt + swz(row, c1)) = v1;
 }
 
+// Fold constants of sub-block u, column `col`: s and -(2^23 + 2^22) s, stored
+// per column pair as {s_c, s_c+1, cm_c, cm_c+1} so that a thread's two
+// adjacent columns read both packed-fma operands with one 16-byte load.
+PFNG_DEV void store_fold(float *fold, int bn, int u, int col, float sv) {
+    float *q = fold + (u * bn + (col & ~1)) * 2 + (col & 1);
+    q[0] = sv;
+    q[2] = -kMagic * sv;
+}
+
 // Unpack the raw W tile of stage `s` into the int8 B tile and the
 // per-(sub-block, column) fold data.  Runs once per CTA per k-step.
 template <int WT, class C>
 PFNG_DEV void decode_w(const GemmParams &p, const Smem<C> &sm, int s, int64_t ks, int64_t n0, int tid) {
     const uint8_t *wr = sm.w_raw(s);
     int8_t *bt = sm.b_tile();
-    float2 *fold = sm.fold();
+    float *fold = reinterpret_cast<float *>(sm.fold());
     for (int task = tid; task < C::BN * 8; task += kThreads) {
         const int row = task >> 3, u = task & 7;
         const uint32_t mis = p.w_vec16 ? 0u : static_cast<uint32_t>((n0 + row) * p.row_bytes + ks * p.step_bytes) & 3u;
@@ -241,18 +250,20 @@ PFNG_DEV void decode_w(const GemmParams &p, const Smem<C> &sm, int s, int64_t ks
                 q[0] = v.x, q[1] = v.y, q[2] = v.z, q[3] = v.w;
                 dbits = *reinterpret_cast<const uint16_t *>(wr + base + 128u + 2u * u);
             }
+            // nibble - 8 per byte: for b in 0..15, b + 0x78 stays below 0x100
+            // (no carry into the next byte) and flipping bit 7 gives b - 8
             uint4 lo, hi;
-            lo.x = __vsub4(q[0] & 0x0f0f0f0fu, 0x08080808u);
-            lo.y = __vsub4(q[1] & 0x0f0f0f0fu, 0x08080808u);
-            lo.z = __vsub4(q[2] & 0x0f0f0f0fu, 0x08080808u);
-            lo.w = __vsub4(q[3] & 0x0f0f0f0fu, 0x08080808u);
-            hi.x = __vsub4((q[0] >> 4) & 0x0f0f0f0fu, 0x08080808u);
-            hi.y = __vsub4((q[1] >> 4) & 0x0f0f0f0fu, 0x08080808u);
-            hi.z = __vsub4((q[2] >> 4) & 0x0f0f0f0fu, 0x08080808u);
-            hi.w = __vsub4((q[3] >> 4) & 0x0f0f0f0fu, 0x08080808u);
+            lo.x = ((q[0] & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+            lo.y = ((q[1] & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+            lo.z = ((q[2] & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+            lo.w = ((q[3] & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+            hi.x = (((q[0] >> 4) & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+            hi.y = (((q[1] >> 4) & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+            hi.z = (((q[2] >> 4) & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+            hi.w = (((q[3] >> 4) & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
             store_pair(bt, row, 2 * u, lo, 2 * u + 1, hi, u >= 4);
             const float dw = f16_bits_to_f32(dbits);
-            fold[u * C::BN + row] = make_float2(dw, -kMagic * dw);
+            store_fold(fold, C::BN, u, row, dw);
         } else if constexpr (WT == kWQ4_K) {
             // u = (nibble pair pr, half h): 16 payload bytes -> 16 values of sub-blocks 2pr and 2pr+1
             const uint8_t *blk = wr + base;
@@ -275,7 +286,7 @@ PFNG_DEV void decode_w(const GemmParams &p, const Smem<C> &sm, int s, int64_t ks
             else
                 scv = (scale_byte(s0, s1, s2, u + 4) & 15u) | ((scale_byte(s0, s1, s2, u - 4) >> 6) << 4);
             const float sv = __fmul_rn(f16_bits_to_f32(dd & 0xffffu), static_cast<float>(scv));
-            fold[u * C::BN + row] = make_float2(sv, -kMagic * sv);
+            store_fold(fold, C::BN, u, row, sv);
             if (u == 0) {
                 uint32_t mpk0 = 0, mpk1 = 0;
 #pragma unroll
@@ -288,7 +299,7 @@ PFNG_DEV void decode_w(const GemmParams &p, const Smem<C> &sm, int s, int64_t ks
                         mpk1 |= mnv << (8 * (j - 4));
                 }
                 const float dmin = f16_bits_to_f32(dd >> 16);
-                sm.mins_d()[row] = make_float2(dmin, -kMagic * dmin);
+                store_fold(reinterpret_cast<float *>(sm.mins_d()), 0, 0, row, dmin);
                 sm.mins_pk()[row] = make_uint2(mpk0, mpk1);
             }
         } else {
@@ -311,7 +322,7 @@ PFNG_DEV void decode_w(const GemmParams &p, const Smem<C> &sm, int s, int64_t ks
                        u >= 4);
             const float d = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(wr + base));
             const float sv = __fmul_rn(__fmul_rn(0.125f, d), static_cast<float>(2 * (ss >> 28) + 1));
-            fold[u * C::BN + row] = make_float2(sv, -kMagic * sv);
+            store_fold(fold, C::BN, u, row, sv);
         }
     }
     if constexpr (WT == kWQ4_K) {
@@ -466,7 +477,7 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     const float4 f = *reinterpret_cast<const float4 *>(fold + wn * C::WN + nt * 8 + 2 * t4);
-                    const float2 sv = make_float2(f.x, f.z), cm = make_float2(f.y, f.w);
+                    const float2 sv = make_float2(f.x, f.y), cm = make_float2(f.z, f.w);
 #pragma unroll
                     for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
@@ -508,7 +519,7 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
                         const float4 md = *reinterpret_cast<const float4 *>(sm.mins_d() + col);
                         const float2 y = make_float2(__int_as_float(static_cast<int>(kMagicBits) + i2[0]),
                                                      __int_as_float(static_cast<int>(kMagicBits) + i2[1]));
-                        const float2 t = ffma2(y, make_float2(md.x, md.z), make_float2(md.y, md.w));
+                        const float2 t = ffma2(y, make_float2(md.x, md.y), make_float2(md.z, md.w));
                         acc[mt][nt][h] = ffma2(t, make_float2(nad, nad), acc[mt][nt][h]);
                     }
                 }
