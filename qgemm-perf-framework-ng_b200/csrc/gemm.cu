@@ -44,7 +44,10 @@ namespace {
 constexpr int BK = 256;
 constexpr int kThreads = 256;
 constexpr bool kTcDefault = false;
-constexpr int kStages = 3;
+#ifndef PFNG_GEMM_STAGES
+#define PFNG_GEMM_STAGES 3
+#endif
+constexpr int kStages = PFNG_GEMM_STAGES;  // cp.async ring depth
 constexpr uint32_t kMagicBits = 0x4B400000u;  // float 12582912 = 2^23 + 2^22
 constexpr float kMagic = 12582912.0f;
 // true when the activations are q8_0 (one fp32 scale per 32 values)
@@ -148,28 +151,35 @@ struct Smem {
     }
 };
 
-// Issue the cp.async copies of k-step `ks` into stage `s`.
+// cp.async copies of k-step `ks` of the activation tile: int8 rows, the
+// per-sub-block scales (q8_0) or sums (q8_K), and the q8_K block scales.
 template <int WT, class C>
-PFNG_DEV void load_stage(const GemmParams &p, const Smem<C> &sm, int s, int64_t ks, int64_t m0, int64_t n0, int tid) {
+PFNG_DEV void load_a(const GemmParams &p, int8_t *a_qs, float *a_scale, float *a_d8k, int64_t ks, int64_t m0,
+                     int tid) {
     const int64_t K = p.k;
     // A int8 rows: BM x 256 B
 #pragma unroll
     for (int i = 0; i < C::BM * 16 / kThreads; ++i) {
         const int q = tid + i * kThreads;
         const int row = q >> 4, ch = q & 15;
-        cp_async16(sm.a_qs(s) + swz(row, ch), p.a.qs + (m0 + row) * K + ks * BK + ch * 16, 16);
+        cp_async16(a_qs + swz(row, ch), p.a.qs + (m0 + row) * K + ks * BK + ch * 16, 16);
     }
     if (tid < C::BM * 2) {
         const int row = tid >> 1, half = tid & 1;
         const void *src = kQ8_0Act<WT> ? static_cast<const void *>(p.a.d + (m0 + row) * (K / 32) + ks * 8 + half * 4)
                                   : static_cast<const void *>(p.a.aux + (m0 + row) * (K / 32) + ks * 8 + half * 4);
-        cp_async16(sm.a_scale(s) + row * kAScaleStride + half * 4, src, 16);
+        cp_async16(a_scale + row * kAScaleStride + half * 4, src, 16);
     }
     if constexpr (!kQ8_0Act<WT>) {
-        if (tid < C::BM) cp_async4(sm.a_d8k(s) + tid, p.a.d + (m0 + tid) * (K / 256) + ks, 4);
+        if (tid < C::BM) cp_async4(a_d8k + tid, p.a.d + (m0 + tid) * (K / 256) + ks, 4);
     }
-    // raw W: BN rows x step_bytes, each row into a kWRowSlot-byte slot
-    uint8_t *wr = sm.w_raw(s);
+}
+
+// cp.async copies of k-step `ks` of the raw W tile: BN rows x step_bytes,
+// each row into a kWRowSlot-byte slot of `wr`.
+template <int WT, class C>
+PFNG_DEV void load_w(const GemmParams &p, uint8_t *wr, int64_t ks, int64_t n0, int tid) {
+    const int64_t K = p.k;
     if constexpr (WT == kWQ4_0P) {
         // planar rows: the k-step's 8 nibble fields (128 B) into slot bytes
         // 0..127, their 8 fp16 scales (16 B) into bytes 128..143
@@ -205,6 +215,13 @@ PFNG_DEV void load_stage(const GemmParams &p, const Smem<C> &sm, int s, int64_t 
     }
 }
 
+// Issue the cp.async copies of k-step `ks` into stage `s`.
+template <int WT, class C>
+PFNG_DEV void load_stage(const GemmParams &p, const Smem<C> &sm, int s, int64_t ks, int64_t m0, int64_t n0, int tid) {
+    load_a<WT, C>(p, sm.a_qs(s), sm.a_scale(s), sm.a_d8k(s), ks, m0, tid);
+    load_w<WT, C>(p, sm.w_raw(s), ks, n0, tid);
+}
+
 PFNG_DEV uint32_t scale_byte(uint32_t s0, uint32_t s1, uint32_t s2, int i) {
     const uint32_t w = i < 4 ? s0 : (i < 8 ? s1 : s2);
     return (w >> (8 * (i & 3))) & 0xffu;
@@ -229,6 +246,61 @@ PFNG_DEV void store_fold(float *fold, int bn, int u, int col, float sv) {
     q[2] = -kMagic * sv;
 }
 
+// One decode task (row = task / 8, 32-value unit u = task % 8) of the raw W
+// tile `wr` into the int8 B tile and the fold constants, for the types whose
+// decode reads nothing but W (q4_0 in either layout, iq2_xxs).
+template <int WT, int BN>
+PFNG_DEV void decode_task(const GemmParams &p, const uint8_t *wr, int8_t *bt, float *fold, const uint2 *grid,
+                          int64_t ks, int64_t n0, int task) {
+    static_assert(WT == kWQ4_0 || WT == kWQ4_0P || WT == kWIQ2, "decode_task types");
+    const int row = task >> 3, u = task & 7;
+    const uint32_t mis = p.w_vec16 ? 0u : static_cast<uint32_t>((n0 + row) * p.row_bytes + ks * p.step_bytes) & 3u;
+    const uint32_t base = row * kWRowSlot + mis;
+    if constexpr (WT == kWQ4_0 || WT == kWQ4_0P) {
+        uint32_t q[4], dbits;
+        if constexpr (WT == kWQ4_0) {
+            load_q4_0_block_smem(wr, base + 18u * u, q, dbits);
+        } else {
+            const uint4 v = *reinterpret_cast<const uint4 *>(wr + base + 16u * u);
+            q[0] = v.x, q[1] = v.y, q[2] = v.z, q[3] = v.w;
+            dbits = *reinterpret_cast<const uint16_t *>(wr + base + 128u + 2u * u);
+        }
+        // nibble - 8 per byte: for b in 0..15, b + 0x78 stays below 0x100
+        // (no carry into the next byte) and flipping bit 7 gives b - 8
+        uint4 lo, hi;
+        lo.x = ((q[0] & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+        lo.y = ((q[1] & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+        lo.z = ((q[2] & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+        lo.w = ((q[3] & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+        hi.x = (((q[0] >> 4) & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+        hi.y = (((q[1] >> 4) & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+        hi.z = (((q[2] >> 4) & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+        hi.w = (((q[3] >> 4) & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+        store_pair(bt, row, 2 * u, lo, 2 * u + 1, hi, u >= 4);
+        store_fold(fold, BN, u, row, f16_bits_to_f32(dbits));
+    } else {
+        // iq2_xxs: 32-value group u of the 66-byte block
+        const uint32_t off = base + 2 + 8 * u;
+        const uint32_t *w = reinterpret_cast<const uint32_t *>(wr + (off & ~3u));
+        const uint32_t sh = (off & 2u) ? 16u : 0u;
+        const uint32_t idx = __funnelshift_r(w[0], w[1], sh);
+        const uint32_t ss = __funnelshift_r(w[1], w[2], sh);
+        uint32_t v[8];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            const uint2 gv = grid[(idx >> (8 * g)) & 0xffu];
+            const uint32_t sgn = iq2_sign_mask((ss >> (7 * g)) & 0x7fu);
+            v[2 * g] = apply_sign_bytes(gv.x, expand_bits4(sgn));
+            v[2 * g + 1] = apply_sign_bytes(gv.y, expand_bits4(sgn >> 4));
+        }
+        store_pair(bt, row, 2 * u, make_uint4(v[0], v[1], v[2], v[3]), 2 * u + 1, make_uint4(v[4], v[5], v[6], v[7]),
+                   u >= 4);
+        const float d = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(wr + base));
+        const float sv = __fmul_rn(__fmul_rn(0.125f, d), static_cast<float>(2 * (ss >> 28) + 1));
+        store_fold(fold, BN, u, row, sv);
+    }
+}
+
 // Unpack the raw W tile of stage `s` into the int8 B tile and the
 // per-(sub-block, column) fold data.  Runs once per CTA per k-step.
 template <int WT, class C>
@@ -236,35 +308,15 @@ PFNG_DEV void decode_w(const GemmParams &p, const Smem<C> &sm, int s, int64_t ks
     const uint8_t *wr = sm.w_raw(s);
     int8_t *bt = sm.b_tile();
     float *fold = reinterpret_cast<float *>(sm.fold());
-    for (int task = tid; task < C::BN * 8; task += kThreads) {
-        const int row = task >> 3, u = task & 7;
-        const uint32_t mis = p.w_vec16 ? 0u : static_cast<uint32_t>((n0 + row) * p.row_bytes + ks * p.step_bytes) & 3u;
-        const uint32_t base = row * kWRowSlot + mis;
-        if constexpr (WT == kWQ4_0 || WT == kWQ4_0P) {
-            // block u of the row
-            uint32_t q[4], dbits;
-            if constexpr (WT == kWQ4_0) {
-                load_q4_0_block_smem(wr, base + 18u * u, q, dbits);
-            } else {
-                const uint4 v = *reinterpret_cast<const uint4 *>(wr + base + 16u * u);
-                q[0] = v.x, q[1] = v.y, q[2] = v.z, q[3] = v.w;
-                dbits = *reinterpret_cast<const uint16_t *>(wr + base + 128u + 2u * u);
-            }
-            // nibble - 8 per byte: for b in 0..15, b + 0x78 stays below 0x100
-            // (no carry into the next byte) and flipping bit 7 gives b - 8
-            uint4 lo, hi;
-            lo.x = ((q[0] & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
-            lo.y = ((q[1] & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
-            lo.z = ((q[2] & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
-            lo.w = ((q[3] & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
-            hi.x = (((q[0] >> 4) & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
-            hi.y = (((q[1] >> 4) & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
-            hi.z = (((q[2] >> 4) & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
-            hi.w = (((q[3] >> 4) & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
-            store_pair(bt, row, 2 * u, lo, 2 * u + 1, hi, u >= 4);
-            const float dw = f16_bits_to_f32(dbits);
-            store_fold(fold, C::BN, u, row, dw);
-        } else if constexpr (WT == kWQ4_K) {
+    if constexpr (WT != kWQ4_K) {
+        for (int task = tid; task < C::BN * 8; task += kThreads)
+            decode_task<WT, C::BN>(p, wr, bt, fold, sm.grid(), ks, n0, task);
+    } else {
+        for (int task = tid; task < C::BN * 8; task += kThreads) {
+            const int row = task >> 3, u = task & 7;
+            const uint32_t mis =
+                p.w_vec16 ? 0u : static_cast<uint32_t>((n0 + row) * p.row_bytes + ks * p.step_bytes) & 3u;
+            const uint32_t base = row * kWRowSlot + mis;
             // u = (nibble pair pr, half h): 16 payload bytes -> 16 values of sub-blocks 2pr and 2pr+1
             const uint8_t *blk = wr + base;
             const int pr = u >> 1, h = u & 1;
@@ -302,27 +354,6 @@ PFNG_DEV void decode_w(const GemmParams &p, const Smem<C> &sm, int s, int64_t ks
                 store_fold(reinterpret_cast<float *>(sm.mins_d()), 0, 0, row, dmin);
                 sm.mins_pk()[row] = make_uint2(mpk0, mpk1);
             }
-        } else {
-            // iq2_xxs: 32-value group u of the 66-byte block
-            const uint2 *grid = sm.grid();
-            const uint32_t off = base + 2 + 8 * u;
-            const uint32_t *w = reinterpret_cast<const uint32_t *>(wr + (off & ~3u));
-            const uint32_t sh = (off & 2u) ? 16u : 0u;
-            const uint32_t idx = __funnelshift_r(w[0], w[1], sh);
-            const uint32_t ss = __funnelshift_r(w[1], w[2], sh);
-            uint32_t v[8];
-#pragma unroll
-            for (int g = 0; g < 4; ++g) {
-                const uint2 gv = grid[(idx >> (8 * g)) & 0xffu];
-                const uint32_t sgn = iq2_sign_mask((ss >> (7 * g)) & 0x7fu);
-                v[2 * g] = apply_sign_bytes(gv.x, expand_bits4(sgn));
-                v[2 * g + 1] = apply_sign_bytes(gv.y, expand_bits4(sgn >> 4));
-            }
-            store_pair(bt, row, 2 * u, make_uint4(v[0], v[1], v[2], v[3]), 2 * u + 1, make_uint4(v[4], v[5], v[6], v[7]),
-                       u >= 4);
-            const float d = f16_bits_to_f32(*reinterpret_cast<const uint16_t *>(wr + base));
-            const float sv = __fmul_rn(__fmul_rn(0.125f, d), static_cast<float>(2 * (ss >> 28) + 1));
-            store_fold(fold, C::BN, u, row, sv);
         }
     }
     if constexpr (WT == kWQ4_K) {
@@ -545,6 +576,176 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// Overlapped variant for the types whose W decode reads nothing but W (q4_0
+// in either layout, iq2_xxs): the W tile of k-step ks + 1 is decoded while
+// k-step ks is multiplied.  Activation tiles and raw W tiles have separate
+// two-deep cp.async rings -- during iteration ks they hold A[ks] (in use),
+// A[ks + 1] (landing), raw W[ks + 1] (being decoded) and W[ks + 2]
+// (landing) -- and the decoded B tile and its fold constants are
+// double-buffered.  Each thread decodes its share of W[ks + 1] in pieces
+// between the sub-blocks of ks, so the decode's integer work interleaves with
+// every warp's MMAs and packed fmas, and one barrier per k-step publishes the
+// decoded tile and retires the buffers.  Results are bit-identical to
+// gemm_kernel (same integer partials, same fold order).
+// ---------------------------------------------------------------------------
+template <class C>
+struct SmemOv {
+    // one activation buffer: int8 rows, per-sub-block scales (q8_0) or sums
+    // (q8_K), q8_K block scales
+    static constexpr uint32_t kA = C::kAQs + C::kAScale + C::kAD8K;
+    static constexpr uint32_t kTotal = 2 * kA + 2 * C::kWRaw + 2 * C::kBTile + 2 * C::kFold + C::kGrid;
+    uint8_t *base;
+    PFNG_DEV int8_t *a_qs(int b) const { return reinterpret_cast<int8_t *>(base + b * kA); }
+    PFNG_DEV float *a_scale(int b) const { return reinterpret_cast<float *>(base + b * kA + C::kAQs); }
+    PFNG_DEV float *a_d8k(int b) const { return reinterpret_cast<float *>(base + b * kA + C::kAQs + C::kAScale); }
+    PFNG_DEV uint8_t *w_raw(int b) const { return base + 2 * kA + b * C::kWRaw; }
+    PFNG_DEV int8_t *b_tile(int b) const {
+        return reinterpret_cast<int8_t *>(base + 2 * kA + 2 * C::kWRaw + b * C::kBTile);
+    }
+    PFNG_DEV float2 *fold(int b) const {
+        return reinterpret_cast<float2 *>(base + 2 * kA + 2 * C::kWRaw + 2 * C::kBTile + b * C::kFold);
+    }
+    PFNG_DEV uint2 *grid() const {
+        return reinterpret_cast<uint2 *>(base + 2 * kA + 2 * C::kWRaw + 2 * C::kBTile + 2 * C::kFold);
+    }
+};
+
+template <int WT, class C>
+__global__ void __launch_bounds__(kThreads) gemm_kernel_ov(const GemmParams p) {
+    static_assert(WT != kWQ4_K, "the q4_K decode reads its k-step's activation sums");
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    const SmemOv<C> sm{smem_raw};
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int wm = warp >> 2, wn = warp & 3;
+    const int g = lane >> 2, t4 = lane & 3;
+    const int64_t n0 = static_cast<int64_t>(blockIdx.x) * C::BN;
+    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * C::BM;
+    const int64_t KT = p.k / BK;
+    constexpr int MT = C::MT, NT = C::NT;
+    constexpr int kTasks = C::BN * 8 / kThreads;  // decode tasks per thread and k-step
+    static_assert(kTasks >= 1 && 8 % kTasks == 0, "decode pieces");
+
+    if constexpr (WT == kWIQ2) {
+        uint2 *grid = sm.grid();
+        for (int i = tid; i < 256; i += kThreads) {
+            const uint32_t code = pfng_iq2xxs_grid_codes[i];
+            uint32_t lo = 0, hi = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t c = (code >> (2 * j)) & 3u;
+                const uint32_t byte = 8u + 17u * c + (c >> 1);
+                if (j < 4)
+                    lo |= byte << (8 * j);
+                else
+                    hi |= byte << (8 * (j - 4));
+            }
+            grid[i] = make_uint2(lo, hi);
+        }
+    }
+
+    float2 acc[MT][NT][2];
+#pragma unroll
+    for (int a = 0; a < MT; ++a)
+#pragma unroll
+        for (int b = 0; b < NT; ++b) acc[a][b][0] = acc[a][b][1] = make_float2(0.0f, 0.0f);
+    const int cin = static_cast<int>(kMagicBits);
+
+    // prologue: A[0], W[0], W[1]; decode W[0]
+    load_a<WT, C>(p, sm.a_qs(0), sm.a_scale(0), sm.a_d8k(0), 0, m0, tid);
+    load_w<WT, C>(p, sm.w_raw(0), 0, n0, tid);
+    if (KT > 1) load_w<WT, C>(p, sm.w_raw(1), 1, n0, tid);
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < kTasks; ++t)
+        decode_task<WT, C::BN>(p, sm.w_raw(0), sm.b_tile(0), reinterpret_cast<float *>(sm.fold(0)), sm.grid(), 0, n0,
+                               tid + t * kThreads);
+    __syncthreads();
+
+    for (int64_t ks = 0; ks < KT; ++ks) {
+        const int cur = static_cast<int>(ks & 1), nxt = cur ^ 1;
+        if (ks + 1 < KT) load_a<WT, C>(p, sm.a_qs(nxt), sm.a_scale(nxt), sm.a_d8k(nxt), ks + 1, m0, tid);
+        if (ks + 2 < KT) load_w<WT, C>(p, sm.w_raw(cur), ks + 2, n0, tid);  // W[ks] was decoded last iteration
+        cp_async_commit();
+        const bool dec = ks + 1 < KT;
+        const uint8_t *wr_next = sm.w_raw(nxt);
+        int8_t *bt_next = sm.b_tile(nxt);
+        float *fold_next = reinterpret_cast<float *>(sm.fold(nxt));
+
+        const int8_t *at = sm.a_qs(cur);
+        const int8_t *bt = sm.b_tile(cur);
+        const float *ascale = sm.a_scale(cur);
+        // activation block scales of this thread's rows (q8_K: one per 256 block)
+        float da8k[MT][2];
+        if constexpr (!kQ8_0Act<WT>) {
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) da8k[mt][h] = sm.a_d8k(cur)[wm * C::WM + mt * 16 + g + 8 * h];
+        }
+        uint32_t af[2][MT][4], bf[2][NT][2];
+        int res[MT][NT][4];
+        load_frags<C>(at, bt, 0, wm, wn, lane, af[0], bf[0]);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) mma_s8(res[mt][nt], af[0][mt], bf[0][nt][0], bf[0][nt][1], cin);
+        load_frags<C>(at, bt, 1, wm, wn, lane, af[1], bf[1]);
+#pragma unroll
+        for (int kb = 0; kb < 8; ++kb) {
+            const int nx = (kb + 1) & 1;
+            float da[MT][2];
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+                    da[mt][h] = kQ8_0Act<WT> ? ascale[(wm * C::WM + mt * 16 + g + 8 * h) * kAScaleStride + kb]
+                                             : da8k[mt][h];
+            const float2 *fold = sm.fold(cur) + kb * C::BN;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const float4 f = *reinterpret_cast<const float4 *>(fold + wn * C::WN + nt * 8 + 2 * t4);
+                const float2 sv = make_float2(f.x, f.y), cm = make_float2(f.z, f.w);
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt) {
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const float2 y = make_float2(__int_as_float(res[mt][nt][2 * h]),
+                                                     __int_as_float(res[mt][nt][2 * h + 1]));
+                        const float2 t = ffma2(y, sv, cm);
+                        acc[mt][nt][h] = ffma2(t, make_float2(da[mt][h], da[mt][h]), acc[mt][nt][h]);
+                    }
+                    if (kb + 1 < 8) mma_s8(res[mt][nt], af[nx][mt], bf[nx][nt][0], bf[nx][nt][1], cin);
+                }
+            }
+            if (kb + 2 < 8) load_frags<C>(at, bt, kb + 2, wm, wn, lane, af[kb & 1], bf[kb & 1]);
+            // a piece of the next k-step's decode after every (8 / kTasks)-th sub-block
+            if ((kb + 1) % (8 / kTasks) == 0 && dec)
+                decode_task<WT, C::BN>(p, wr_next, bt_next, fold_next, sm.grid(), ks + 1, n0,
+                                       tid + ((kb + 1) / (8 / kTasks) - 1) * kThreads);
+        }
+        cp_async_wait<0>();
+        __syncthreads();
+    }
+
+    if (p.out_format == kOutQ8_0) {
+        epilogue_q8_0<C>(p, smem_raw, acc, m0, n0, tid);
+        return;
+    }
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int64_t r = m0 + wm * C::WM + mt * 16 + g + 8 * h;
+                const int64_t c = n0 + wn * C::WN + nt * 8 + 2 * t4;
+                if (r < p.m) store_out2(p, r, c, acc[mt][nt][h]);
+            }
+}
+
 // C tile of the CTA quantized to q8_0 along n: the tile is staged in shared
 // memory (the main loop's buffers are free by then), then each warp
 // quantizes four 32-column blocks at a time with the standalone quantizer's
@@ -628,22 +829,60 @@ cudaError_t launch_t(const GemmParams &p, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+template <int WT, class C>
+cudaError_t launch_t_ov(const GemmParams &p, cudaStream_t s) {
+    auto kernel = gemm_kernel_ov<WT, C>;
+    constexpr uint32_t smem = SmemOv<C>::kTotal;
+    static_assert(C::BM * (C::BN + 4) * 4 <= smem, "staged C tile of the q8_0 epilogue");
+    static thread_local bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !configured[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < 64) configured[dev] = true;
+    }
+    const dim3 grid(static_cast<unsigned>((p.n + C::BN - 1) / C::BN), static_cast<unsigned>((p.m + C::BM - 1) / C::BM));
+    kernel<<<grid, kThreads, smem, s>>>(p);
+    return cudaGetLastError();
+}
+
+// The overlapped kernel serves q4_0 (both layouts) and iq2_xxs products on
+// 128 x 128 tiles; PFNG_B200_GEMM_OV=0 selects the two-phase kernel instead
+// (comparisons).  Measured on B200: 2048x11008x4096 656 vs 698 us, 512x4096x4096
+// 69 vs 73 us; with the 64 x 128 tiles of 480x1536x1536 it is 3 % slower, so
+// the smaller tiles keep the two-phase kernel.
+template <int WT, bool kPartials>
+constexpr bool kOvType = !kPartials && WT != kWQ4_K;
+inline bool ov_enabled() {
+    const char *e = std::getenv("PFNG_B200_GEMM_OV");
+    return !(e && std::strcmp(e, "0") == 0);
+}
+
+template <int WT, class C, bool kPartials>
+cudaError_t launch_pick(const GemmParams &p, cudaStream_t s) {
+    if constexpr (kOvType<WT, kPartials> && C::BM == 128 && C::BN == 128) {
+        if (ov_enabled()) return launch_t_ov<WT, C>(p, s);
+    }
+    return launch_t<WT, C, kPartials>(p, s);
+}
+
 template <int WT, bool kPartials>
 cudaError_t launch_tile(const GemmParams &p, cudaStream_t s) {
     // tile choice by CTA count (PFNG_B200_GEMM_TILE = "128x128" / "64x128" / "64x64" forces one, for comparisons)
     if (const char *t = std::getenv("PFNG_B200_GEMM_TILE")) {
-        if (std::strcmp(t, "128x128") == 0) return launch_t<WT, Cfg<128, 128>, kPartials>(p, s);
-        if (std::strcmp(t, "64x128") == 0) return launch_t<WT, Cfg<64, 128>, kPartials>(p, s);
-        if (std::strcmp(t, "64x64") == 0) return launch_t<WT, Cfg<64, 64>, kPartials>(p, s);
+        if (std::strcmp(t, "128x128") == 0) return launch_pick<WT, Cfg<128, 128>, kPartials>(p, s);
+        if (std::strcmp(t, "64x128") == 0) return launch_pick<WT, Cfg<64, 128>, kPartials>(p, s);
+        if (std::strcmp(t, "64x64") == 0) return launch_pick<WT, Cfg<64, 64>, kPartials>(p, s);
     }
     const int64_t sms = device_sm_count();
     auto ctas = [&](int bm, int bn) { return ((p.n + bn - 1) / bn) * ((p.m + bm - 1) / bm); };
     // measured on B200: 128x128 wins once it fills ~80% of the SMs (512x4096x4096:
     // 86 us vs 111 us with 64x128); below that the smaller tiles' extra CTAs win
     // (480x1536x1536: 64x128 25 us, 128x128 36 us)
-    if (ctas(128, 128) * 5 >= 4 * sms) return launch_t<WT, Cfg<128, 128>, kPartials>(p, s);
-    if (ctas(64, 128) * 2 >= sms) return launch_t<WT, Cfg<64, 128>, kPartials>(p, s);
-    return launch_t<WT, Cfg<64, 64>, kPartials>(p, s);
+    if (ctas(128, 128) * 5 >= 4 * sms) return launch_pick<WT, Cfg<128, 128>, kPartials>(p, s);
+    if (ctas(64, 128) * 2 >= sms) return launch_pick<WT, Cfg<64, 128>, kPartials>(p, s);
+    return launch_pick<WT, Cfg<64, 64>, kPartials>(p, s);
 }
 
 }  // namespace

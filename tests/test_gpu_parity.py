@@ -60,7 +60,7 @@ def make_weights(oracle, wtype, n, k, rng, full_range=True):
 def check_close(c, ref, bound, what):
     err = np.abs(c.astype(np.float64) - ref.astype(np.float64))
     limit = TOL * bound + 1e-30
-    bad = err > limit
+    bad = ~(err <= limit)  # NaN fails too
     assert not bad.any(), f"{what}: {bad.sum()} elements out of tolerance, worst {np.max(err / limit):.3g}x"
 
 
