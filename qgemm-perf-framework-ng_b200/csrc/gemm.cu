@@ -192,7 +192,8 @@ PFNG_DEV void load_w(const GemmParams &p, uint8_t *wr, int64_t ks, int64_t n0, i
             cp_async16(wr + row * kWRowSlot + ch * 16, src, ok ? 16u : 0u);
         }
     } else if (p.w_vec16) {
-        const int chunks = static_cast<int>(p.step_bytes / 16);
+        // 16-byte chunks per row and k-step: the raw bytes of 256 values
+        constexpr int chunks = (WT == kWIQ2 ? 256 / 256 * kIQ2Bytes : 256 / 32 * kQ4_0Bytes) / 16;
         for (int q = tid; q < C::BN * chunks; q += kThreads) {
             const int row = q / chunks, ch = q % chunks;
             const int64_t n = n0 + row;
@@ -202,7 +203,8 @@ PFNG_DEV void load_w(const GemmParams &p, uint8_t *wr, int64_t ks, int64_t n0, i
         }
     } else {
         // word-granular window [start & ~3, start + step_bytes + 3) per row
-        const int words = static_cast<int>((p.step_bytes + 3) / 4) + 1;
+        constexpr int kStep = WT == kWIQ2 ? kIQ2Bytes : (WT == kWQ4_K ? kQ4_KBytes : 256 / 32 * kQ4_0Bytes);
+        constexpr int words = (kStep + 3) / 4 + 1;
         for (int q = tid; q < C::BN * words; q += kThreads) {
             const int row = q / words, wd = q % words;
             const int64_t n = n0 + row;
@@ -376,6 +378,47 @@ PFNG_DEV void decode_w(const GemmParams &p, const Smem<C> &sm, int s, int64_t ks
 }
 
 // A and B fragments of sub-block kb for this warp's MT x NT m16n8k32 tiles.
+PFNG_DEV void ldmatrix_x4_s(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3, uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(addr));
+}
+
+// This thread's ldmatrix row offsets in a swizzled [rows][256 B] tile.
+// swz(row, 2 kb + h) = row * 256 + ((2 kb + h) ^ (row & 7)) * 16 and the
+// fragment rows have row & 7 = lane & 7, so the offset of sub-block kb is
+// off ^ (32 kb) with off = row * 256 + ((h ^ (lane & 7)) << 4): one xor per
+// load instead of the swizzle arithmetic.
+template <class C>
+struct FragOff {
+    uint32_t a[C::MT];
+    uint32_t b[C::NT / 2];
+    PFNG_DEV FragOff(int wm, int wn, int lane) {
+#pragma unroll
+        for (int mt = 0; mt < C::MT; ++mt) {
+            const int row = wm * C::WM + mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+            a[mt] = static_cast<uint32_t>(row * 256 + ((((lane >> 4) & 1) ^ (lane & 7)) << 4));
+        }
+#pragma unroll
+        for (int np = 0; np < C::NT / 2; ++np) {
+            const int row = wn * C::WN + np * 16 + (lane & 7) + ((lane >> 4) & 1) * 8;
+            b[np] = static_cast<uint32_t>(row * 256 + ((((lane >> 3) & 1) ^ (lane & 7)) << 4));
+        }
+    }
+};
+
+// load_frags from shared-space base addresses and precomputed offsets.
+template <class C>
+PFNG_DEV void load_frags_o(uint32_t at_s, uint32_t bt_s, int kb, const FragOff<C> &fo, uint32_t (&af)[C::MT][4],
+                           uint32_t (&bf)[C::NT][2]) {
+    const uint32_t x = static_cast<uint32_t>(kb) * 32u;
+#pragma unroll
+    for (int mt = 0; mt < C::MT; ++mt) ldmatrix_x4_s(af[mt][0], af[mt][1], af[mt][2], af[mt][3], at_s + (fo.a[mt] ^ x));
+#pragma unroll
+    for (int np = 0; np < C::NT / 2; ++np)
+        ldmatrix_x4_s(bf[2 * np][0], bf[2 * np][1], bf[2 * np + 1][0], bf[2 * np + 1][1], bt_s + (fo.b[np] ^ x));
+}
+
 template <class C>
 PFNG_DEV void load_frags(const int8_t *at, const int8_t *bt, int kb, int wm, int wn, int lane,
                          uint32_t (&af)[C::MT][4], uint32_t (&bf)[C::NT][2]) {
@@ -408,6 +451,7 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
     const int64_t m0 = static_cast<int64_t>(blockIdx.y) * C::BM;
     const int64_t KT = p.k / BK;
     constexpr int MT = C::MT, NT = C::NT;
+    const FragOff<C> fo(wm, wn, lane);
 
     if constexpr (WT == kWIQ2) {
         uint2 *grid = sm.grid();
@@ -488,12 +532,13 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
             // FMA and shared-memory pipes overlap inside one warp.
             uint32_t af[2][MT][4], bf[2][NT][2];
             int res[MT][NT][4];
-            load_frags<C>(at, bt, 0, wm, wn, lane, af[0], bf[0]);
+            const uint32_t at_s = smem_u32(at), bt_s = smem_u32(bt);
+            load_frags_o<C>(at_s, bt_s, 0, fo, af[0], bf[0]);
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) mma_s8(res[mt][nt], af[0][mt], bf[0][nt][0], bf[0][nt][1], cin);
-            load_frags<C>(at, bt, 1, wm, wn, lane, af[1], bf[1]);
+            load_frags_o<C>(at_s, bt_s, 1, fo, af[1], bf[1]);
 #pragma unroll
             for (int kb = 0; kb < 8; ++kb) {
                 const int nx = (kb + 1) & 1;
@@ -521,7 +566,7 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
                         if (kb + 1 < 8) mma_s8(res[mt][nt], af[nx][mt], bf[nx][nt][0], bf[nx][nt][1], cin);
                     }
                 }
-                if (kb + 2 < 8) load_frags<C>(at, bt, kb + 2, wm, wn, lane, af[kb & 1], bf[kb & 1]);
+                if (kb + 2 < 8) load_frags_o<C>(at_s, bt_s, kb + 2, fo, af[kb & 1], bf[kb & 1]);
             }
         }
 
@@ -624,6 +669,7 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel_ov(const GemmParams p) {
     const int64_t KT = p.k / BK;
     constexpr int MT = C::MT, NT = C::NT;
     constexpr int kTasks = C::BN * 8 / kThreads;  // decode tasks per thread and k-step
+    const FragOff<C> fo(wm, wn, lane);
     static_assert(kTasks >= 1 && 8 % kTasks == 0, "decode pieces");
 
     if constexpr (WT == kWIQ2) {
@@ -687,12 +733,13 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel_ov(const GemmParams p) {
         }
         uint32_t af[2][MT][4], bf[2][NT][2];
         int res[MT][NT][4];
-        load_frags<C>(at, bt, 0, wm, wn, lane, af[0], bf[0]);
+        const uint32_t at_s = smem_u32(at), bt_s = smem_u32(bt);
+        load_frags_o<C>(at_s, bt_s, 0, fo, af[0], bf[0]);
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) mma_s8(res[mt][nt], af[0][mt], bf[0][nt][0], bf[0][nt][1], cin);
-        load_frags<C>(at, bt, 1, wm, wn, lane, af[1], bf[1]);
+        load_frags_o<C>(at_s, bt_s, 1, fo, af[1], bf[1]);
 #pragma unroll
         for (int kb = 0; kb < 8; ++kb) {
             const int nx = (kb + 1) & 1;
@@ -720,7 +767,7 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel_ov(const GemmParams p) {
                     if (kb + 1 < 8) mma_s8(res[mt][nt], af[nx][mt], bf[nx][nt][0], bf[nx][nt][1], cin);
                 }
             }
-            if (kb + 2 < 8) load_frags<C>(at, bt, kb + 2, wm, wn, lane, af[kb & 1], bf[kb & 1]);
+            if (kb + 2 < 8) load_frags_o<C>(at_s, bt_s, kb + 2, fo, af[kb & 1], bf[kb & 1]);
             // a piece of the next k-step's decode after every (8 / kTasks)-th sub-block
             if ((kb + 1) % (8 / kTasks) == 0 && dec)
                 decode_task<WT, C::BN>(p, wr_next, bt_next, fold_next, sm.grid(), ks + 1, n0,
