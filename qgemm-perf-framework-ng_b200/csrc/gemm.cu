@@ -478,9 +478,17 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
         for (int b = 0; b < NT; ++b) acc[a][b][0] = acc[a][b][1] = make_float2(0.0f, 0.0f);
     const int cin = kPartials ? 0 : static_cast<int>(kMagicBits);
 
+    // The kernel is a programmatic dependent of the activation quantizer: the
+    // weights of the first stages are fetched before waiting for it, the
+    // activations after.  Group s holds A[s] (group 0 also every W prologue
+    // stage), so the wait_group accounting of the loop is unchanged.
+#pragma unroll
+    for (int s = 0; s < kStages - 1; ++s)
+        if (s < KT) load_w<WT, C>(p, sm.w_raw(s), s, n0, tid);
+    pdl_wait();
 #pragma unroll
     for (int s = 0; s < kStages - 1; ++s) {
-        if (s < KT) load_stage<WT, C>(p, sm, s, s, m0, n0, tid);
+        if (s < KT) load_a<WT, C>(p, sm.a_qs(s), sm.a_scale(s), sm.a_d8k(s), s, m0, tid);
         cp_async_commit();
     }
 
@@ -697,17 +705,22 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel_ov(const GemmParams p) {
         for (int b = 0; b < NT; ++b) acc[a][b][0] = acc[a][b][1] = make_float2(0.0f, 0.0f);
     const int cin = static_cast<int>(kMagicBits);
 
-    // prologue: A[0], W[0], W[1]; decode W[0]
-    load_a<WT, C>(p, sm.a_qs(0), sm.a_scale(0), sm.a_d8k(0), 0, m0, tid);
+    // prologue: W[0], W[1], then (the kernel is a programmatic dependent of
+    // the activation quantizer) wait for the activations and fetch A[0]
+    // while W[0] is decoded
     load_w<WT, C>(p, sm.w_raw(0), 0, n0, tid);
     if (KT > 1) load_w<WT, C>(p, sm.w_raw(1), 1, n0, tid);
     cp_async_commit();
-    cp_async_wait<0>();
+    pdl_wait();
+    load_a<WT, C>(p, sm.a_qs(0), sm.a_scale(0), sm.a_d8k(0), 0, m0, tid);
+    cp_async_commit();
+    cp_async_wait<1>();
     __syncthreads();
 #pragma unroll
     for (int t = 0; t < kTasks; ++t)
         decode_task<WT, C::BN>(p, sm.w_raw(0), sm.b_tile(0), reinterpret_cast<float *>(sm.fold(0)), sm.grid(), 0, n0,
                                tid + t * kThreads);
+    cp_async_wait<0>();
     __syncthreads();
 
     for (int64_t ks = 0; ks < KT; ++ks) {
@@ -860,6 +873,24 @@ int64_t row_bytes_of(int wtype, int64_t k) {
     }
 }
 
+// Launch as a programmatic dependent of the preceding kernel on the stream
+// (the activation quantizer): the kernels fetch weights before pdl_wait()
+// and read activations after it.
+template <class C, class K>
+cudaError_t launch_pdl(K kernel, const GemmParams &p, uint32_t smem, cudaStream_t s) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>((p.n + C::BN - 1) / C::BN), static_cast<unsigned>((p.m + C::BM - 1) / C::BM));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
 template <int WT, class C, bool kPartials>
 cudaError_t launch_t(const GemmParams &p, cudaStream_t s) {
     auto kernel = gemm_kernel<WT, C, kPartials>;
@@ -871,9 +902,7 @@ cudaError_t launch_t(const GemmParams &p, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) configured[dev] = true;
     }
-    const dim3 grid(static_cast<unsigned>((p.n + C::BN - 1) / C::BN), static_cast<unsigned>((p.m + C::BM - 1) / C::BM));
-    kernel<<<grid, kThreads, C::kSmem, s>>>(p);
-    return cudaGetLastError();
+    return launch_pdl<C>(kernel, p, C::kSmem, s);
 }
 
 template <int WT, class C>
@@ -889,9 +918,7 @@ cudaError_t launch_t_ov(const GemmParams &p, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) configured[dev] = true;
     }
-    const dim3 grid(static_cast<unsigned>((p.n + C::BN - 1) / C::BN), static_cast<unsigned>((p.m + C::BM - 1) / C::BM));
-    kernel<<<grid, kThreads, smem, s>>>(p);
-    return cudaGetLastError();
+    return launch_pdl<C>(kernel, p, smem, s);
 }
 
 // The overlapped kernel serves q4_0 (both layouts) and iq2_xxs products on

@@ -124,6 +124,14 @@ PFNG_DEV uint64_t l2_policy_evict_first() {
     return policy;
 }
 
+// ---- programmatic dependent launch --------------------------------------------
+// pdl_trigger: kernels launched after this one with programmatic stream
+// serialization may start once every CTA of this grid has executed it (or
+// exited).  pdl_wait: block until the preceding grid has completed and its
+// memory is visible; a no-op in a kernel launched without the attribute.
+PFNG_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+PFNG_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // ---- small integer helpers ---------------------------------------------------
 // Read the 16 payload bytes and the fp16 scale of an 18-byte q4_0 block that
 // starts at byte offset `off` (even) of shared memory `base`, using aligned

@@ -35,6 +35,9 @@ template <bool kVec, bool kSplit>
 __global__ void __launch_bounds__(kThreads) quantize_q8_0_kernel(const float *__restrict__ x, int64_t ldx,
                                                                   uint8_t *__restrict__ y, int64_t ldy, SplitA split,
                                                                   int64_t m, int64_t k, int64_t rows) {
+    // the GEMM that reads this operand may start now and fetch its weights;
+    // it waits for this grid's completion before reading the operand
+    if (threadIdx.x == 0) pdl_trigger();
     const int64_t nb = k / 32;
     const int64_t total = rows * nb;
     const int g = threadIdx.x & 7;
@@ -75,6 +78,9 @@ template <bool kVec, bool kSplit>
 __global__ void __launch_bounds__(kThreads) quantize_q8_K_kernel(const float *__restrict__ x, int64_t ldx,
                                                                   uint8_t *__restrict__ y, SplitA split,
                                                                   int64_t m, int64_t k, int64_t rows) {
+    // the GEMM that reads this operand may start now and fetch its weights;
+    // it waits for this grid's completion before reading the operand
+    if (threadIdx.x == 0) pdl_trigger();
     const int64_t nb = k / 256;
     const int64_t total = rows * nb;
     const int lane = threadIdx.x & 31;
@@ -115,6 +121,9 @@ __global__ void __launch_bounds__(kThreads) quantize_q8_K_kernel(const float *__
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads) convert_q8_0_split_kernel(const uint8_t *__restrict__ a, SplitA split,
                                                                        int64_t m, int64_t k, int64_t rows) {
+    // the GEMM that reads this operand may start now and fetch its weights;
+    // it waits for this grid's completion before reading the operand
+    if (threadIdx.x == 0) pdl_trigger();
     const int64_t nb = k / 32;
     const int64_t total = rows * nb;
     const int g = threadIdx.x & 7;
@@ -146,6 +155,9 @@ __global__ void __launch_bounds__(kThreads) convert_q8_0_split_kernel(const uint
 
 __global__ void __launch_bounds__(kThreads) convert_q8_K_split_kernel(const uint8_t *__restrict__ a, SplitA split,
                                                                        int64_t m, int64_t k, int64_t rows) {
+    // the GEMM that reads this operand may start now and fetch its weights;
+    // it waits for this grid's completion before reading the operand
+    if (threadIdx.x == 0) pdl_trigger();
     const int64_t nb = k / 256;
     const int64_t total = rows * nb;
     const int lane = threadIdx.x & 31;
