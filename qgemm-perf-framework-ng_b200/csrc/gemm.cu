@@ -921,11 +921,11 @@ cudaError_t launch_t_ov(const GemmParams &p, cudaStream_t s) {
     return launch_pdl<C>(kernel, p, smem, s);
 }
 
-// The overlapped kernel serves q4_0 (both layouts) and iq2_xxs products on
-// 128 x 128 tiles; PFNG_B200_GEMM_OV=0 selects the two-phase kernel instead
-// (comparisons).  Measured on B200: 2048x11008x4096 656 vs 698 us, 512x4096x4096
-// 69 vs 73 us; with the 64 x 128 tiles of 480x1536x1536 it is 3 % slower, so
-// the smaller tiles keep the two-phase kernel.
+// The overlapped kernel serves q4_0 (both layouts) and iq2_xxs products;
+// PFNG_B200_GEMM_OV=0 selects the two-phase kernel instead (comparisons).
+// Measured on B200 (us per quantize + GEMM step, overlapped vs two-phase):
+// 2048x11008x4096 627 vs 698, 512x4096x4096 66 vs 73, 480x1536x1536 on 64 x 64
+// tiles 20.2 vs 21.3 (q4_0) and 24.6 vs 25.3 (iq2_xxs).
 template <int WT, bool kPartials>
 constexpr bool kOvType = !kPartials && WT != kWQ4_K;
 inline bool ov_enabled() {
@@ -935,7 +935,7 @@ inline bool ov_enabled() {
 
 template <int WT, class C, bool kPartials>
 cudaError_t launch_pick(const GemmParams &p, cudaStream_t s) {
-    if constexpr (kOvType<WT, kPartials> && C::BM == 128 && C::BN == 128) {
+    if constexpr (kOvType<WT, kPartials>) {
         if (ov_enabled()) return launch_t_ov<WT, C>(p, s);
     }
     return launch_t<WT, C, kPartials>(p, s);
@@ -952,11 +952,12 @@ cudaError_t launch_tile(const GemmParams &p, cudaStream_t s) {
     const int64_t sms = device_sm_count();
     auto ctas = [&](int bm, int bn) { return ((p.n + bn - 1) / bn) * ((p.m + bm - 1) / bm); };
     // measured on B200: 128x128 wins once it fills ~80% of the SMs (512x4096x4096:
-    // 86 us vs 111 us with 64x128); below that the smaller tiles' extra CTAs win
-    // (480x1536x1536: 64x128 25 us, 128x128 36 us)
+    // 66 us vs 95 us with 64x64); below that 64x64, whose CTAs fit two per SM
+    // (about 100-115 KB of shared memory each), as long as they fit in one wave
+    // (480x1536x1536: 192 CTAs, 20.2 us vs 20.8 with 64x128 and 30 with 128x128)
     if (ctas(128, 128) * 5 >= 4 * sms) return launch_pick<WT, Cfg<128, 128>, kPartials>(p, s);
-    if (ctas(64, 128) * 2 >= sms) return launch_pick<WT, Cfg<64, 128>, kPartials>(p, s);
-    return launch_pick<WT, Cfg<64, 64>, kPartials>(p, s);
+    if (ctas(64, 64) <= 2 * sms) return launch_pick<WT, Cfg<64, 64>, kPartials>(p, s);
+    return launch_pick<WT, Cfg<64, 128>, kPartials>(p, s);
 }
 
 }  // namespace
