@@ -127,9 +127,14 @@ size_t raw_a_bytes(int wtype, int64_t m, int64_t k) {
 }
 
 // Workspace needed by a resolved path (f32: activations arrive as fp32).
-size_t workspace_for(int wtype, int64_t m, int64_t k, int resolved, bool f32) {
+size_t workspace_for(int wtype, int64_t m, int64_t n, int64_t k, int resolved, bool f32) {
     if (m == 0 || k == 0) return 0;
-    if (resolved == PFNG_B200_PATH_MMA) return split_a_bytes(m, k, block_k(wtype) == 32 ? 32 : 256);
+    if (resolved == PFNG_B200_PATH_MMA) {
+        // the split activation operand, then the split-K partial tiles if the
+        // shape is split (gemm_partial_bytes)
+        const size_t part = gemm_partial_bytes(m, n, k);
+        return split_a_bytes(m, k, block_k(wtype) == 32 ? 32 : 256) + (part > 0 ? part + 256 : 0);
+    }
     if (resolved == PFNG_B200_PATH_SIMPLE && f32) return raw_a_bytes(wtype, m, k) + 256;
     return 0;
 }
@@ -141,6 +146,14 @@ cudaError_t zero_c(float *c, int64_t m, int64_t n, int64_t ldc, cudaStream_t s) 
 
 void *align_ptr(void *p, uintptr_t a) {
     return reinterpret_cast<void *>((reinterpret_cast<uintptr_t>(p) + a - 1) & ~(a - 1));
+}
+
+// Split-K partial tiles behind the split activation operand in the workspace.
+void carve_partial(GemmArgs &g, void *workspace, size_t workspace_need, int wtype, int64_t m, int64_t k) {
+    const size_t a_bytes = split_a_bytes(m, k, block_k(wtype));
+    if (workspace_need <= a_bytes) return;
+    g.partial = static_cast<float *>(align_ptr(static_cast<uint8_t *>(workspace) + a_bytes, 256));
+    g.partial_bytes = workspace_need - a_bytes - 256;
 }
 
 // The shared body of mm / compute / partials.
@@ -156,7 +169,7 @@ int run_matmul(int wtype, const void *w, const void *a, const float *x, int64_t 
     if (k == 0) return partials ? PFNG_B200_OK : status_of(zero_c(c, m, n, ldc, s));
     const int resolved = resolve_path(wtype, m, n, k, w, path);
     if (resolved < 0) return PFNG_B200_ERR_UNSUPPORTED;
-    const size_t need = workspace_for(wtype, m, k, resolved, f32);
+    const size_t need = workspace_for(wtype, m, n, k, resolved, f32);
     if (need > 0 && (!workspace || workspace_bytes < need)) return PFNG_B200_ERR_WORKSPACE;
 
     cudaError_t e = cudaSuccess;
@@ -185,6 +198,7 @@ int run_matmul(int wtype, const void *w, const void *a, const float *x, int64_t 
             e = f32 ? launch_quantize_q8_K_split(x, ldx, sa, m, k, s) : launch_convert_q8_K_split(a, sa, m, k, s);
         if (e == cudaSuccess) {
             GemmArgs g{wtype, w, sa, c, ldc, partials, m, n, k, info->error_word};
+            carve_partial(g, workspace, need, wtype, m, k);
             e = launch_gemm(g, s);
         }
     } else {
@@ -213,7 +227,7 @@ size_t c_scratch_bytes(int64_t m, int64_t n) { return static_cast<size_t>(m) * s
 // Workspace of a resolved path writing output format `fmt`: the MMA GEMM
 // converts in its epilogue; GEMV and SIMPLE write fp32 C to scratch first.
 size_t out_workspace_for(int wtype, int fmt, int64_t m, int64_t n, int64_t k, int resolved, bool f32) {
-    const size_t base = workspace_for(wtype, m, k, resolved, f32);
+    const size_t base = workspace_for(wtype, m, n, k, resolved, f32);
     if (fmt == kOutF32 || resolved == PFNG_B200_PATH_MMA || m == 0 || n == 0) return base;
     return round_up(static_cast<int64_t>(base), 256) + c_scratch_bytes(m, n);
 }
@@ -258,12 +272,13 @@ int run_matmul_out(int wtype, const void *w, const void *a, const float *x, int6
             g.out_format = fmt;
             g.out = out;
             g.ldo = ldo;
+            carve_partial(g, workspace, need, wtype, m, k);
             e = launch_gemm(g, s);
         }
         return status_of(e);
     }
     // fp32 C into scratch behind the path's own workspace, then convert
-    const size_t base = workspace_for(wtype, m, k, resolved, f32);
+    const size_t base = workspace_for(wtype, m, n, k, resolved, f32);
     uint8_t *ws = static_cast<uint8_t *>(workspace);
     float *cs = static_cast<float *>(align_ptr(ws + round_up(static_cast<int64_t>(base), 256), 256));
     st = run_matmul(wtype, w, a, x, ldx, cs, n, nullptr, m, n, k, workspace, base, resolved, s);
@@ -293,11 +308,11 @@ size_t query_workspace(int wtype, int64_t m, int64_t n, int64_t k, int path, boo
     if (path == PFNG_B200_PATH_AUTO) {
         // AUTO may take the tensor-core or the simple path depending on the
         // pointers' alignment, so ask for what either needs.
-        const size_t mma = m > 8 ? workspace_for(wtype, m, k, PFNG_B200_PATH_MMA, f32) : 0;
-        const size_t simple = workspace_for(wtype, m, k, PFNG_B200_PATH_SIMPLE, f32);
+        const size_t mma = m > 8 ? workspace_for(wtype, m, n, k, PFNG_B200_PATH_MMA, f32) : 0;
+        const size_t simple = workspace_for(wtype, m, n, k, PFNG_B200_PATH_SIMPLE, f32);
         return mma > simple ? mma : simple;
     }
-    return workspace_for(wtype, m, k, path, f32);
+    return workspace_for(wtype, m, n, k, path, f32);
 }
 
 }  // namespace

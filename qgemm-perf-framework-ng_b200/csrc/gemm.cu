@@ -56,9 +56,10 @@ constexpr bool kQ8_0Act = WT == kWQ4_0 || WT == kWQ4_0P;
 constexpr uint32_t kWRowSlot = 160;          // >= 144 raw bytes + 8 window slack, multiple of 16
 constexpr int kAScaleStride = 12;
 
-template <int BM_, int BN_>
+template <int BM_, int BN_, int ST_ = kStages>
 struct Cfg {
     static constexpr int BM = BM_, BN = BN_;
+    static constexpr int ST = ST_;  // cp.async ring depth of the two-phase kernel
     static constexpr int WM = BM / 2, WN = BN / 4;  // warp tile
     static constexpr int MT = WM / 16, NT = WN / 8;  // m16n8 fragments per warp
     static_assert(MT >= 1 && NT >= 2 && NT % 2 == 0, "tile shape");
@@ -75,7 +76,7 @@ struct Cfg {
     static constexpr uint32_t kMin = BN * 16;        // q4_K: (dmin, -M dmin) and packed mins per column
     static constexpr uint32_t kAPack = BM * 16;      // q4_K: packed bsum bytes per row
     static constexpr uint32_t kGrid = 2048;          // iq2_xxs lattice table
-    static constexpr uint32_t kSmem = kStages * kStage + kBTile + kFold + kMin + kAPack + kGrid;
+    static constexpr uint32_t kSmem = ST * kStage + kBTile + kFold + kMin + kAPack + kGrid;
 };
 
 struct GemmParams {
@@ -92,6 +93,12 @@ struct GemmParams {
     int out_format;       // kOutF32 (C in c) or another output format (in out)
     void *out;
     int64_t ldo;          // elements (fp16 / bf16) or blocks (q8_0)
+    // split-K: blockIdx.z takes k-steps [z ks_per_split, (z + 1) ks_per_split);
+    // with splits > 1 every split writes its fp32 tile to partial [splits][m][n]
+    // and a reduction sums them in split order
+    int splits;
+    int ks_per_split;
+    float *partial;
 };
 
 PFNG_DEV void cp_async16(void *dst, const void *src, uint32_t src_bytes) {
@@ -137,17 +144,17 @@ struct Smem {
     PFNG_DEV float *a_scale(int s) const { return reinterpret_cast<float *>(stage(s) + C::kAQs); }
     PFNG_DEV float *a_d8k(int s) const { return reinterpret_cast<float *>(stage(s) + C::kAQs + C::kAScale); }
     PFNG_DEV uint8_t *w_raw(int s) const { return stage(s) + C::kAQs + C::kAScale + C::kAD8K; }
-    PFNG_DEV int8_t *b_tile() const { return reinterpret_cast<int8_t *>(base + kStages * C::kStage); }
-    PFNG_DEV float2 *fold() const { return reinterpret_cast<float2 *>(base + kStages * C::kStage + C::kBTile); }
+    PFNG_DEV int8_t *b_tile() const { return reinterpret_cast<int8_t *>(base + C::ST * C::kStage); }
+    PFNG_DEV float2 *fold() const { return reinterpret_cast<float2 *>(base + C::ST * C::kStage + C::kBTile); }
     PFNG_DEV float2 *mins_d() const {
-        return reinterpret_cast<float2 *>(base + kStages * C::kStage + C::kBTile + C::kFold);
+        return reinterpret_cast<float2 *>(base + C::ST * C::kStage + C::kBTile + C::kFold);
     }
     PFNG_DEV uint2 *mins_pk() const { return reinterpret_cast<uint2 *>(mins_d() + C::BN); }
     PFNG_DEV uint4 *a_pack() const {
-        return reinterpret_cast<uint4 *>(base + kStages * C::kStage + C::kBTile + C::kFold + C::kMin);
+        return reinterpret_cast<uint4 *>(base + C::ST * C::kStage + C::kBTile + C::kFold + C::kMin);
     }
     PFNG_DEV uint2 *grid() const {
-        return reinterpret_cast<uint2 *>(base + kStages * C::kStage + C::kBTile + C::kFold + C::kMin + C::kAPack);
+        return reinterpret_cast<uint2 *>(base + C::ST * C::kStage + C::kBTile + C::kFold + C::kMin + C::kAPack);
     }
 };
 
@@ -478,27 +485,32 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
         for (int b = 0; b < NT; ++b) acc[a][b][0] = acc[a][b][1] = make_float2(0.0f, 0.0f);
     const int cin = kPartials ? 0 : static_cast<int>(kMagicBits);
 
+    // this CTA's k-steps [k0, k1) (the whole range without split-K)
+    const int64_t k0 = static_cast<int64_t>(blockIdx.z) * p.ks_per_split;
+    const int64_t k1 = k0 + p.ks_per_split < KT ? k0 + p.ks_per_split : KT;
+    constexpr int ST = C::ST;
+
     // The kernel is a programmatic dependent of the activation quantizer: the
     // weights of the first stages are fetched before waiting for it, the
     // activations after.  Group s holds A[s] (group 0 also every W prologue
     // stage), so the wait_group accounting of the loop is unchanged.
 #pragma unroll
-    for (int s = 0; s < kStages - 1; ++s)
-        if (s < KT) load_w<WT, C>(p, sm.w_raw(s), s, n0, tid);
+    for (int s = 0; s < ST - 1; ++s)
+        if (k0 + s < k1) load_w<WT, C>(p, sm.w_raw(s), k0 + s, n0, tid);
     pdl_wait();
 #pragma unroll
-    for (int s = 0; s < kStages - 1; ++s) {
-        if (s < KT) load_a<WT, C>(p, sm.a_qs(s), sm.a_scale(s), sm.a_d8k(s), s, m0, tid);
+    for (int s = 0; s < ST - 1; ++s) {
+        if (k0 + s < k1) load_a<WT, C>(p, sm.a_qs(s), sm.a_scale(s), sm.a_d8k(s), k0 + s, m0, tid);
         cp_async_commit();
     }
 
-    for (int64_t ks = 0; ks < KT; ++ks) {
-        const int s = static_cast<int>(ks % kStages);
-        cp_async_wait<kStages - 2>();
+    for (int64_t ks = k0; ks < k1; ++ks) {
+        const int s = static_cast<int>((ks - k0) % ST);
+        cp_async_wait<ST - 2>();
         __syncthreads();
         decode_w<WT, C>(p, sm, s, ks, n0, tid);
-        if (ks + kStages - 1 < KT)
-            load_stage<WT, C>(p, sm, static_cast<int>((ks + kStages - 1) % kStages), ks + kStages - 1, m0, n0, tid);
+        if (ks + ST - 1 < k1)
+            load_stage<WT, C>(p, sm, static_cast<int>((ks - k0 + ST - 1) % ST), ks + ST - 1, m0, n0, tid);
         cp_async_commit();
         __syncthreads();
 
@@ -612,6 +624,23 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
     cp_async_wait<0>();
 
     if constexpr (!kPartials) {
+        if (p.splits > 1) {
+            // this split's fp32 tile; reduce_splits_kernel adds the splits
+            float *part = p.partial + static_cast<int64_t>(blockIdx.z) * p.m * p.n;
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int64_t r = m0 + wm * C::WM + mt * 16 + g + 8 * h;
+                        const int64_t c = n0 + wn * C::WN + nt * 8 + 2 * t4;
+                        if (r >= p.m) continue;
+                        if (c < p.n) part[r * p.n + c] = acc[mt][nt][h].x;
+                        if (c + 1 < p.n) part[r * p.n + c + 1] = acc[mt][nt][h].y;
+                    }
+            return;
+        }
         if (p.out_format == kOutQ8_0) {
             epilogue_q8_0<C>(p, smem_raw, acc, m0, n0, tid);
             return;
@@ -873,13 +902,49 @@ int64_t row_bytes_of(int wtype, int64_t k) {
     }
 }
 
+// Split-K reduction: C = sum of the splits' fp32 tiles in split order,
+// written in the output format.  One warp per 128 columns of a row, four
+// columns per lane; for q8_0 (n % 32 == 0) each 8-lane group holds one
+// 32-column block and quantizes it with the standalone quantizer's core, so
+// the bytes are those of pfng_b200_quantize_q8_0 on the reduced C.
+__global__ void __launch_bounds__(kThreads) reduce_splits_kernel(const GemmParams p) {
+    const int lane = threadIdx.x & 31;
+    const int64_t wid = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+    const int64_t per_row = (p.n + 127) / 128;
+    if (wid >= p.m * per_row) return;  // whole warps
+    const int64_t r = wid / per_row;
+    const int64_t c0 = (wid % per_row) * 128 + 4 * lane;
+    float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int z = 0; z < p.splits; ++z) {
+        const float *src = p.partial + (static_cast<int64_t>(z) * p.m + r) * p.n;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            if (c0 + i < p.n) v[i] = __fadd_rn(v[i], src[c0 + i]);
+    }
+    if (p.out_format == kOutQ8_0) {
+        const Q8_0Lane q = q8_0_quantize_lane(v);
+        if (c0 < p.n) {
+            uint8_t *b = static_cast<uint8_t *>(p.out) + (r * p.ldo + c0 / 32) * kQ8_0Bytes;
+            const int gl = lane & 7;
+            uint16_t *hq = reinterpret_cast<uint16_t *>(b + 2 + 4 * gl);
+            hq[0] = static_cast<uint16_t>(q.q & 0xffffu);
+            hq[1] = static_cast<uint16_t>(q.q >> 16);
+            if (gl == 0) *reinterpret_cast<uint16_t *>(b) = q.dbits;
+        }
+        return;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i += 2) store_out2(p, r, c0 + i, make_float2(v[i], v[i + 1]));
+}
+
 // Launch as a programmatic dependent of the preceding kernel on the stream
 // (the activation quantizer): the kernels fetch weights before pdl_wait()
 // and read activations after it.
 template <class C, class K>
 cudaError_t launch_pdl(K kernel, const GemmParams &p, uint32_t smem, cudaStream_t s) {
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(static_cast<unsigned>((p.n + C::BN - 1) / C::BN), static_cast<unsigned>((p.m + C::BM - 1) / C::BM));
+    cfg.gridDim = dim3(static_cast<unsigned>((p.n + C::BN - 1) / C::BN), static_cast<unsigned>((p.m + C::BM - 1) / C::BM),
+                       static_cast<unsigned>(p.splits));
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
@@ -936,31 +1001,100 @@ inline bool ov_enabled() {
 template <int WT, class C, bool kPartials>
 cudaError_t launch_pick(const GemmParams &p, cudaStream_t s) {
     if constexpr (kOvType<WT, kPartials>) {
-        if (ov_enabled()) return launch_t_ov<WT, C>(p, s);
+        if (p.splits == 1 && ov_enabled()) return launch_t_ov<WT, C>(p, s);
     }
     return launch_t<WT, C, kPartials>(p, s);
 }
 
-template <int WT, bool kPartials>
-cudaError_t launch_tile(const GemmParams &p, cudaStream_t s) {
-    // tile choice by CTA count (PFNG_B200_GEMM_TILE = "128x128" / "64x128" / "64x64" forces one, for comparisons)
-    if (const char *t = std::getenv("PFNG_B200_GEMM_TILE")) {
-        if (std::strcmp(t, "128x128") == 0) return launch_pick<WT, Cfg<128, 128>, kPartials>(p, s);
-        if (std::strcmp(t, "64x128") == 0) return launch_pick<WT, Cfg<64, 128>, kPartials>(p, s);
-        if (std::strcmp(t, "64x64") == 0) return launch_pick<WT, Cfg<64, 64>, kPartials>(p, s);
+// Tile shapes: 128 x 128 and 64 x 128 (one CTA per SM), 64 x 64 and, for
+// m <= 32, 32 x 128 with a two-deep ring (two CTAs per SM).
+enum TileKind { kT128x128, kT64x128, kT64x64, kT32x128 };
+constexpr uint32_t kSmemPerSm2 = 113 * 1024;  // a CTA at most this size fits twice per SM
+
+uint32_t tile_smem(TileKind t) {
+    switch (t) {
+    case kT128x128: return Cfg<128, 128>::kSmem;
+    case kT64x128: return Cfg<64, 128>::kSmem;
+    case kT64x64: return Cfg<64, 64>::kSmem;
+    default: return Cfg<32, 128, 2>::kSmem;
     }
+}
+int tile_bm(TileKind t) { return t == kT128x128 ? 128 : t == kT32x128 ? 32 : 64; }
+int tile_bn(TileKind t) { return t == kT64x64 ? 64 : 128; }
+
+// measured on B200: 128x128 wins once it fills ~80% of the SMs (512x4096x4096:
+// 66 us vs 95 us with 64x64); below that 64x64, whose CTAs fit two per SM,
+// as long as they fit in one wave (480x1536x1536: 192 CTAs, 20.2 us vs 20.8
+// with 64x128 and 30 with 128x128); m <= 32 takes 32-row tiles.
+// PFNG_B200_GEMM_TILE = "128x128" / "64x128" / "64x64" / "32x128" forces one.
+TileKind tile_choice(int64_t m, int64_t n, int64_t sms) {
+    if (const char *t = std::getenv("PFNG_B200_GEMM_TILE")) {
+        if (std::strcmp(t, "128x128") == 0) return kT128x128;
+        if (std::strcmp(t, "64x128") == 0) return kT64x128;
+        if (std::strcmp(t, "64x64") == 0) return kT64x64;
+        if (std::strcmp(t, "32x128") == 0) return kT32x128;
+    }
+    auto ctas = [&](int bm, int bn) { return ((n + bn - 1) / bn) * ((m + bm - 1) / bm); };
+    if (m <= 32) return kT32x128;
+    if (ctas(128, 128) * 5 >= 4 * sms) return kT128x128;
+    if (ctas(64, 64) <= 2 * sms) return kT64x64;
+    return kT64x128;
+}
+
+// Split-K factor: when the tiles fill at most half of the resident CTA slots
+// and k has at least 4 k-steps, each tile's k range is split so the splits
+// fill the slots (at most 8, at least two k-steps each; PFNG_B200_GEMM_SPLITS
+// lowers the cap, 1 disables splitting).  A split product adds the splits'
+// fp32 tiles in split order: deterministic, but a different summation order
+// than the unsplit kernel.
+int splits_for(TileKind t, int64_t m, int64_t n, int64_t k, int64_t sms) {
+    int64_t cap = 8;
+    if (const char *e = std::getenv("PFNG_B200_GEMM_SPLITS")) cap = std::atoi(e) > 0 ? std::atoi(e) : 1;
+    const int64_t tiles = ((n + tile_bn(t) - 1) / tile_bn(t)) * ((m + tile_bm(t) - 1) / tile_bm(t));
+    const int64_t slots = sms * (tile_smem(t) <= kSmemPerSm2 ? 2 : 1);
+    const int64_t kt = k / BK;
+    if (tiles * 2 > slots || kt < 4 || cap < 2) return 1;
+    int64_t sp = slots / tiles;
+    if (sp > kt / 2) sp = kt / 2;
+    if (sp > cap) sp = cap;
+    // splits that are all non-empty
+    const int64_t per = (kt + sp - 1) / sp;
+    return static_cast<int>((kt + per - 1) / per);
+}
+
+template <int WT, bool kPartials>
+cudaError_t launch_tile(GemmParams &p, cudaStream_t s) {
     const int64_t sms = device_sm_count();
-    auto ctas = [&](int bm, int bn) { return ((p.n + bn - 1) / bn) * ((p.m + bm - 1) / bm); };
-    // measured on B200: 128x128 wins once it fills ~80% of the SMs (512x4096x4096:
-    // 66 us vs 95 us with 64x64); below that 64x64, whose CTAs fit two per SM
-    // (about 100-115 KB of shared memory each), as long as they fit in one wave
-    // (480x1536x1536: 192 CTAs, 20.2 us vs 20.8 with 64x128 and 30 with 128x128)
-    if (ctas(128, 128) * 5 >= 4 * sms) return launch_pick<WT, Cfg<128, 128>, kPartials>(p, s);
-    if (ctas(64, 64) <= 2 * sms) return launch_pick<WT, Cfg<64, 64>, kPartials>(p, s);
-    return launch_pick<WT, Cfg<64, 128>, kPartials>(p, s);
+    const TileKind t = tile_choice(p.m, p.n, sms);
+    const int64_t kt = p.k / BK;
+    p.splits = 1;
+    if constexpr (!kPartials) {
+        const int sp = splits_for(t, p.m, p.n, p.k, sms);
+        if (sp > 1 && p.partial) p.splits = sp;
+    }
+    p.ks_per_split = static_cast<int>((kt + p.splits - 1) / p.splits);
+    cudaError_t e;
+    switch (t) {
+    case kT128x128: e = launch_pick<WT, Cfg<128, 128>, kPartials>(p, s); break;
+    case kT64x128: e = launch_pick<WT, Cfg<64, 128>, kPartials>(p, s); break;
+    case kT64x64: e = launch_pick<WT, Cfg<64, 64>, kPartials>(p, s); break;
+    default: e = launch_pick<WT, Cfg<32, 128, 2>, kPartials>(p, s); break;
+    }
+    if (e != cudaSuccess || p.splits == 1) return e;
+    const int64_t warps = p.m * ((p.n + 127) / 128);
+    const int64_t blocks = (warps * 32 + kThreads - 1) / kThreads;
+    if (blocks > 0x7fffffff) return cudaErrorInvalidValue;
+    reduce_splits_kernel<<<static_cast<unsigned>(blocks), kThreads, 0, s>>>(p);
+    return cudaGetLastError();
 }
 
 }  // namespace
+
+size_t gemm_partial_bytes(int64_t m, int64_t n, int64_t k) {
+    const int64_t sms = device_sm_count();
+    const int sp = splits_for(tile_choice(m, n, sms), m, n, k, sms);
+    return sp > 1 ? static_cast<size_t>(sp) * static_cast<size_t>(m) * static_cast<size_t>(n) * sizeof(float) : 0;
+}
 
 bool gemm_supported(int wtype, int64_t m, int64_t n, int64_t k, const void *w) {
     (void)wtype;
@@ -999,6 +1133,9 @@ cudaError_t launch_gemm(const GemmArgs &args, cudaStream_t s) {
     p.out_format = args.out_format;
     p.out = args.out;
     p.ldo = args.ldo;
+    // split-K partials, when the caller's workspace holds them
+    const size_t need = gemm_partial_bytes(args.m, args.n, args.k);
+    p.partial = (need > 0 && args.partial && args.partial_bytes >= need) ? args.partial : nullptr;
     const bool part = args.partials != nullptr;
     switch (args.wtype) {
     case kWQ4_0: return part ? launch_tile<kWQ4_0, true>(p, s) : launch_tile<kWQ4_0, false>(p, s);

@@ -86,8 +86,14 @@ struct GemmArgs {
     int out_format = kOutF32;
     void *out = nullptr;
     int64_t ldo = 0;
+    // split-K partial tiles ([splits][m][n] fp32, gemm_partial_bytes); without
+    // them the product runs unsplit
+    float *partial = nullptr;
+    size_t partial_bytes = 0;
 };
 bool gemm_supported(int wtype, int64_t m, int64_t n, int64_t k, const void *w);
+// workspace bytes of the split-K partial tiles for this shape (0: no split)
+size_t gemm_partial_bytes(int64_t m, int64_t n, int64_t k);
 cudaError_t launch_gemm(const GemmArgs &args, cudaStream_t s);
 
 // gemm_tc.cu -- q4_0 on tcgen05 / TMEM (k % 256 == 0, 16-byte aligned W)

@@ -332,6 +332,7 @@ def test_q4_0_tcgen05_kernel(oracle, monkeypatch, m, n, k):
     c_tc = host(pb.compute("q4_0", wd, xd, n, path="mma"))
     pb.check_kernel_error()
     monkeypatch.setenv("PFNG_B200_GEMM", "mma")
+    monkeypatch.setenv("PFNG_B200_GEMM_SPLITS", "1")  # same summation order as the tcgen05 kernel
     c_mma = host(pb.compute("q4_0", wd, xd, n, path="mma"))
     check_close(c_tc, ref, bound, f"tcgen05 q4_0 {m}x{n}x{k}")
     np.testing.assert_array_equal(c_tc.view(np.uint32), c_mma.view(np.uint32))
@@ -353,3 +354,25 @@ def test_k_types_decode(oracle, wtype, n, k):
     np.testing.assert_array_equal(got, oracle.partials(wtype, w, a, 1, n, k))
     g = host(pb.compute_grouped(wtype, [wd], xd, [n])[0])
     np.testing.assert_array_equal(g.view(np.uint32), c.view(np.uint32))
+
+
+@pytest.mark.parametrize("m,n,k", [(32, 4096, 4096), (17, 1000, 2048), (32, 4096, 11008), (64, 640, 4096)])
+def test_split_k_small_m(oracle, monkeypatch, m, n, k):
+    # small-m GEMM shapes whose tiles leave SMs idle run split-K: the splits'
+    # fp32 tiles are added in split order -- within tolerance of the oracle,
+    # deterministic, and every output format converts the same reduced C
+    rng = np.random.default_rng(m + n + k)
+    w = oracle.quantize("q4_0", rng.standard_normal((n, k)).astype(np.float32))
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    a = oracle.quantize("q8_0", x)
+    wd, xd = dev_bytes(w), dev(x)
+    c = host(pb.compute("q4_0", wd, xd, n, path="mma"))
+    check_close(c, oracle.mm("q4_0", w, a, m, n, k), oracle.bound("q4_0", w, a, m, n, k), f"split-K {m}x{n}x{k}")
+    c2 = host(pb.compute("q4_0", wd, xd, n, path="mma"))
+    np.testing.assert_array_equal(c2.view(np.uint32), c.view(np.uint32))
+    if n % 32 == 0:
+        q = host(pb.compute_out("q4_0", wd, xd, n, "q8_0", path="mma"))
+        assert q.tobytes() == oracle.quantize("q8_0", c).tobytes()
+    monkeypatch.setenv("PFNG_B200_GEMM_SPLITS", "1")
+    c1 = host(pb.compute("q4_0", wd, xd, n, path="mma"))
+    check_close(c1, oracle.mm("q4_0", w, a, m, n, k), oracle.bound("q4_0", w, a, m, n, k), f"unsplit {m}x{n}x{k}")
