@@ -51,8 +51,8 @@ def step_ops() -> float:
     return float(sum(2 * 1 * n * K_DIM for n in N_DIMS))
 
 
-def step_weight_bytes() -> int:
-    return sum(n * Q4_0_ROW_BYTES for n in N_DIMS)
+def step_weight_bytes(wtype: str = "q4_0") -> int:
+    return sum(weight_bytes(wtype, n, K_DIM) for n in N_DIMS)
 
 
 def dist_env():
@@ -208,11 +208,17 @@ def reference_arm(args) -> int:
     return 0
 
 
-def workload_config(layout: str = "ggml"):
+def workload_config(layout: str = "ggml", wtype: str = "q4_0"):
+    if wtype == "q4_0":
+        workload = ("configs[1]: q4_0 x q8_0 decode GEMV, M=1, (N,K) = (4096,4096) + (11008,4096), "
+                    "activation quantized on device (fused)")
+    else:
+        workload = (f"decode GEMV with {wtype} x q8_K weights on the shapes of configs[1] (M=1, (N,K) = (4096,4096) "
+                    "+ (11008,4096), activation quantized on device, fused); not a BASELINE configuration")
     return {
-        "workload": "configs[1]: q4_0 x q8_0 decode GEMV, M=1, (N,K) = (4096,4096) + (11008,4096), "
-                    "activation quantized on device (fused)",
-        "m": 1, "n": list(N_DIMS), "k": K_DIM, "weight_type": "q4_0", "activation_type": "q8_0",
+        "workload": workload,
+        "m": 1, "n": list(N_DIMS), "k": K_DIM, "weight_type": wtype,
+        "activation_type": "q8_0" if wtype == "q4_0" else "q8_K",
         "weight_layout": "ggml block_q4_0 rows" if layout == "ggml" else
                          "q4_0 planar rows (same bytes, repacked once on the device before timing)",
         "l2": "inputs larger than L2: weights rotate over copies totalling > 4x the 126 MB L2",
@@ -234,17 +240,18 @@ def ours(args) -> int:
 
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)  # graph capture needs a non-default stream
-    copies = max(2, -(-4 * L2_BYTES // step_weight_bytes()))
+    wtype = args.wtype
+    copies = max(2, -(-4 * L2_BYTES // step_weight_bytes(wtype)))
     gen = torch.Generator(device="cuda").manual_seed(1 + rank)
     planar = args.layout == "planar"
-    wt = pb.Q4_0_PLANAR if planar else pb.Q4_0
+    if planar and wtype != "q4_0":
+        raise SystemExit("--layout planar applies to q4_0 weights")
+    wt = pb.Q4_0_PLANAR if planar else pb.WTYPES[wtype]
     weights = []
     for _ in range(copies):
         per = []
         for n in N_DIMS:
-            wf = torch.randn((n, K_DIM), generator=gen, device="cuda", dtype=torch.float32)
-            q = pb.quantize_q4_0(wf)
-            del wf
+            q = make_weights_device(pb, torch, wtype, n, K_DIM, gen)
             # planar: the one-time repack a reference adapter does in prepare
             per.append(pb.pack_q4_0_planar(q, n, K_DIM) if planar else q)
             del q
@@ -302,7 +309,7 @@ def ours(args) -> int:
     # exactly K back-to-back launches of it on one stream (CUDA events on
     # that stream), so its average launch duration is elapsed / K.
     avg_launch = elapsed / args.steps
-    bytes_launch = step_weight_bytes() + K_DIM * 4 + sum(N_DIMS) * 4
+    bytes_launch = step_weight_bytes(wtype) + K_DIM * 4 + sum(N_DIMS) * 4
 
     # ---- end to end through the public API with host buffers.  Every step
     # copies its activation row from pinned host memory, runs the grouped
@@ -357,15 +364,19 @@ def ours(args) -> int:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": elapsed_max / args.steps * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8/int32 dot, fp32 fold (q4_0 x q8_0)",
-            "data": "synthetic: seeded N(0,1) fp32 weights (quantized to q4_0 on device) and activations",
-            "config": dict(workload_config(args.layout), parallelism=f"replicas x{world}" if world > 1 else "single GPU",
-                           weight_copies=copies, weight_bytes_resident=copies * step_weight_bytes()),
-            "weight_GBps": world * args.steps * step_weight_bytes() / elapsed_max / 1e9,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": f"int8/int32 dot, fp32 fold ({wtype} x {'q8_0' if wtype == 'q4_0' else 'q8_K'})",
+            "data": "synthetic: seeded N(0,1) fp32 weights (quantized on device) and activations"
+                    if wtype != "iq2_xxs" else "synthetic: seeded iq2_xxs blocks (uniform indices, signs, scales) "
+                    "and N(0,1) activations",
+            "config": dict(workload_config(args.layout, wtype),
+                           parallelism=f"replicas x{world}" if world > 1 else "single GPU",
+                           weight_copies=copies, weight_bytes_resident=copies * step_weight_bytes(wtype)),
+            "weight_GBps": world * args.steps * step_weight_bytes(wtype) / elapsed_max / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
-                         "traffic": profile_traffic("gemv_q4_0_planar_decode" if planar else "gemv_q4_0_decode"),
-                         "kernel": f"gemv_kernel<{'q4_0 planar' if planar else 'q4_0'}, m=1, fp32 activations>, "
+                         "traffic": profile_traffic("gemv_q4_0_planar_decode" if planar else f"gemv_{wtype}_decode"),
+                         "kernel": f"gemv_kernel<{'q4_0 planar' if planar else wtype}, m=1, fp32 activations>, "
                                    "both matrices in one launch",
                          "bytes_per_launch": bytes_launch, "avg_launch_us": avg_launch * 1e6,
                          "timing": "CUDA events around K back-to-back launches on the launching stream, / K",
@@ -378,7 +389,7 @@ def ours(args) -> int:
                    "host C out every step, the K steps captured in one CUDA graph"},
             "gpu_launches": args.steps,
         }
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and wtype == "q4_0":
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
     if dist is not None:

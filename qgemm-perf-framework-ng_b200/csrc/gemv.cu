@@ -97,12 +97,22 @@ constexpr int kTileRowsLong = PFNG_GEMV_TILE_ROWS;  // rows per tile when a row 
 static_assert(kTileRowsLong >= kClaimRows && (kTileRowsLong & (kTileRowsLong - 1)) == 0, "tile rows");
 constexpr int kMaxGroup = kGemvMaxGroup;
 constexpr uint32_t kBarrierBytes = 2 * kMaxStages * 8;
-// iq2_xxs grid points (256 x 8 bytes), then the byte sign masks of the 128
-// sign indices (128 x 8 bytes).  Measured alternatives (decode step): 16
-// bank-striped copies of the grid with the masks computed in registers was
-// 5 % slower (16.5 vs 15.7 us) -- the lookups' bank conflicts are not the
-// limit, the instruction count is.
-constexpr uint32_t kGridTableBytes = 256 * 8 + 128 * 8;
+// iq2_xxs tables: the 256 grid points, then the byte sign masks of the 128
+// sign indices, 8 bytes each, in kGridCopies bank-striped copies: entry e,
+// copy c at uint2 index kGridCopies e + c, i.e. in banks 2c, 2c + 1 whatever
+// e is.  Lane l reads copy l % kGridCopies, so a warp's 32 random lookups use
+// every bank at most twice (the minimum for 32 x 8 bytes) instead of piling
+// onto the banks of popular entries.
+#ifndef PFNG_GEMV_GRID_COPIES
+#define PFNG_GEMV_GRID_COPIES 16
+#endif
+constexpr int kGridCopies = PFNG_GEMV_GRID_COPIES;
+constexpr int kSignTable = 256 * kGridCopies;  // uint2 index of the sign masks
+constexpr uint32_t kGridTableBytes = (256 + 128) * kGridCopies * 8;
+
+PFNG_DEV int grid_slot(uint32_t entry, int lane) {
+    return static_cast<int>(entry) * kGridCopies + (lane & (kGridCopies - 1));
+}
 constexpr uint32_t kStageSlack = 32;  // bytes read past a window by aligned loads; never used
 constexpr int kRegGroupsMax = 2;      // m = 1 keeps up to 2 x 64 blocks (k <= 4096) in registers
 
@@ -1026,7 +1036,7 @@ PFNG_DEV void row_iq2_xxs(const GemvParams &p, const Out &o, const uint8_t *act,
             uint32_t v[8];
 #pragma unroll
             for (int g = 0; g < 4; ++g) {
-                const uint2 gv = grid[(idx >> (8 * g)) & 0xffu];
+                const uint2 gv = grid[grid_slot((idx >> (8 * g)) & 0xffu, lane)];
                 const uint32_t sgn = iq2_sign_mask((ss >> (7 * g)) & 0x7fu);
                 v[2 * g] = apply_sign_bytes(gv.x, expand_bits4(sgn));
                 v[2 * g + 1] = apply_sign_bytes(gv.y, expand_bits4(sgn >> 4));
@@ -1061,7 +1071,8 @@ PFNG_DEV void row_iq2_xxs(const GemvParams &p, const Out &o, const uint8_t *act,
 // iq2_xxs, m = 1, k <= 4096: activations in registers.  Lane l of iteration i
 // takes the 32-value group sb = l & 7 of block b = 4 i + l / 8 (8 qs bytes at
 // 2 + 8 sb).  Signs come from the table of byte masks m (0xff = negative)
-// after the grid: with signed dp4a, (g ^ m) is g or -g - 1, so
+// after the grid (both bank-striped, grid_slot): with signed dp4a, (g ^ m) is
+// g or -g - 1, so
 //   sum s g a = dp4a(g ^ m, a) + dp4a(m & 0x01010101, a)
 // per 4 values -- the same integer as applying the signs first.
 // ---------------------------------------------------------------------------
@@ -1142,8 +1153,8 @@ PFNG_DEV void rows_iq2_reg(const GemvParams &p, const Out &o, const ActRegsI<NI>
                 int dot = 0, corr = 0;
 #pragma unroll
                 for (int g = 0; g < 4; ++g) {
-                    const uint2 gv = grid[(idx >> (8 * g)) & 0xffu];
-                    const uint2 mk = grid[256 + ((ss >> (7 * g)) & 0x7fu)];
+                    const uint2 gv = grid[grid_slot((idx >> (8 * g)) & 0xffu, lane)];
+                    const uint2 mk = grid[kSignTable + grid_slot((ss >> (7 * g)) & 0x7fu, lane)];
                     dot = dp4a(static_cast<int>(gv.x ^ mk.x), static_cast<int>(av[2 * g]), dot);
                     corr = dp4a(static_cast<int>(mk.x & 0x01010101u), static_cast<int>(av[2 * g]), corr);
                     dot = dp4a(static_cast<int>(gv.y ^ mk.y), static_cast<int>(av[2 * g + 1]), dot);
@@ -1289,8 +1300,8 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
     // ---------------- consumers ----------------
     uint2 *grid = reinterpret_cast<uint2 *>(smem + p.grid_offset);
     if constexpr (WT == kWIQ2) {
-        for (int i = tid; i < 256; i += kConsumerThreads) {
-            const uint32_t code = pfng_iq2xxs_grid_codes[i];
+        for (int i = tid; i < 256 * kGridCopies; i += kConsumerThreads) {
+            const uint32_t code = pfng_iq2xxs_grid_codes[i / kGridCopies];
             uint32_t lo = 0, hi = 0;
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
@@ -1304,9 +1315,9 @@ __global__ void __launch_bounds__(kGemvThreads, kCtasPerSm) gemv_kernel(const Ge
             grid[i] = make_uint2(lo, hi);
         }
         // byte masks (0xff = negative) of the 128 sign indices
-        for (int i = tid; i < 128; i += kConsumerThreads) {
-            const uint32_t sgn = iq2_sign_mask(static_cast<uint32_t>(i));
-            grid[256 + i] = make_uint2(expand_bits4(sgn), expand_bits4(sgn >> 4));
+        for (int i = tid; i < 128 * kGridCopies; i += kConsumerThreads) {
+            const uint32_t sgn = iq2_sign_mask(static_cast<uint32_t>(i / kGridCopies));
+            grid[kSignTable + i] = make_uint2(expand_bits4(sgn), expand_bits4(sgn >> 4));
         }
     }
     const uint8_t *act = smem + p.act_offset;
