@@ -70,13 +70,15 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def profile_traffic(kernel_tag: str):
-    """DRAM bytes per launch from a committed ncu summary, if one exists."""
+def profile_traffic(kernel_tag: str, variant: str | None = None):
+    """DRAM bytes per launch from a committed ncu summary, if one exists (the
+    line `traffic_bytes_per_launch:` or `traffic_bytes_per_launch (variant):`)."""
     path = ROOT / "profiles" / f"{kernel_tag}.md"
     if not path.exists():
         return None
+    key = "traffic_bytes_per_launch" + (f" ({variant})" if variant else "") + ":"
     for line in path.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
+        if line.startswith(key):
             return float(line.split(":", 1)[1])
     return None
 
@@ -375,7 +377,9 @@ def ours(args) -> int:
             "weight_GBps": world * args.steps * step_weight_bytes(wtype) / elapsed_max / 1e9,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,
-                         "traffic": profile_traffic("gemv_q4_0_planar_decode" if planar else f"gemv_{wtype}_decode"),
+                         "traffic": profile_traffic("gemv_q4_0_planar_decode") if planar
+                         else profile_traffic("gemv_q4_0_decode") if wtype == "q4_0"
+                         else profile_traffic("gemv_k_types_decode", wtype),
                          "kernel": f"gemv_kernel<{'q4_0 planar' if planar else wtype}, m=1, fp32 activations>, "
                                    "both matrices in one launch",
                          "bytes_per_launch": bytes_launch, "avg_launch_us": avg_launch * 1e6,
