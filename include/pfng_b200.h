@@ -93,7 +93,12 @@ int pfng_b200_quantize_q4_K(const float *x, int64_t ldx, void *y, int64_t n, int
  * KernelCallbacks::run of a reference adapter
  * (bench/framework/kernel_registry.h:97).
  * workspace: device scratch of at least pfng_b200_mm_workspace_size() bytes,
- * 256-byte aligned (may be NULL when that size is 0). */
+ * 256-byte aligned (may be NULL when that size is 0).  On the tensor-core
+ * path it holds the activations in the GEMM's operand layout and, for shapes
+ * whose tiles would leave SMs idle (small m), the fp32 tiles of a split-k
+ * product, added in a fixed order (deterministic).  Results are identical
+ * for identical arguments; a split product sums in a different order than
+ * the unsplit one, within the same error bound. */
 size_t pfng_b200_mm_workspace_size(int wtype, int64_t m, int64_t n, int64_t k, int path);
 int pfng_b200_mm_q4_0_q8_0(const void *w, const void *a, float *c, int64_t m, int64_t n, int64_t k, int64_t ldc,
                            void *workspace, size_t workspace_bytes, int path, void *stream);
