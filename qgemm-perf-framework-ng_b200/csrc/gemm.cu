@@ -256,12 +256,12 @@ PFNG_DEV void store_fold(float *fold, int bn, int u, int col, float sv) {
 }
 
 // One decode task (row = task / 8, 32-value unit u = task % 8) of the raw W
-// tile `wr` into the int8 B tile and the fold constants, for the types whose
-// decode reads nothing but W (q4_0 in either layout, iq2_xxs).
+// tile `wr` into the int8 B tile and the fold constants.  q4_K tasks with
+// u == 0 also write the row's (dmin, -M dmin) pair and packed 6-bit mins to
+// mins_d / mins_pk; no type's decode reads the activations.
 template <int WT, int BN>
 PFNG_DEV void decode_task(const GemmParams &p, const uint8_t *wr, int8_t *bt, float *fold, const uint2 *grid,
-                          int64_t ks, int64_t n0, int task) {
-    static_assert(WT == kWQ4_0 || WT == kWQ4_0P || WT == kWIQ2, "decode_task types");
+                          int64_t ks, int64_t n0, int task, float *mins_d = nullptr, uint2 *mins_pk = nullptr) {
     const int row = task >> 3, u = task & 7;
     const uint32_t mis = p.w_vec16 ? 0u : static_cast<uint32_t>((n0 + row) * p.row_bytes + ks * p.step_bytes) & 3u;
     const uint32_t base = row * kWRowSlot + mis;
@@ -287,6 +287,44 @@ PFNG_DEV void decode_task(const GemmParams &p, const uint8_t *wr, int8_t *bt, fl
         hi.w = (((q[3] >> 4) & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
         store_pair(bt, row, 2 * u, lo, 2 * u + 1, hi, u >= 4);
         store_fold(fold, BN, u, row, f16_bits_to_f32(dbits));
+    } else if constexpr (WT == kWQ4_K) {
+        // u = (nibble pair pr, half h): 16 payload bytes -> 16 values of sub-blocks 2pr and 2pr+1
+        const uint8_t *blk = wr + base;
+        const int pr = u >> 1, h = u & 1;
+        const uint4 v = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * pr + 16 * h);
+        uint4 lo, hi;
+        lo.x = v.x & 0x0f0f0f0fu, lo.y = v.y & 0x0f0f0f0fu, lo.z = v.z & 0x0f0f0f0fu, lo.w = v.w & 0x0f0f0f0fu;
+        hi.x = (v.x >> 4) & 0x0f0f0f0fu, hi.y = (v.y >> 4) & 0x0f0f0f0fu;
+        hi.z = (v.z >> 4) & 0x0f0f0f0fu, hi.w = (v.w >> 4) & 0x0f0f0f0fu;
+        // sub-block 2pr holds k = 64 pr + j, sub-block 2pr + 1 holds k = 64 pr + 32 + j
+        store_pair(bt, row, 4 * pr + h, lo, 4 * pr + 2 + h, hi, pr >= 2);
+        // scale / min of sub-block u (llama_reference.cpp:116-121)
+        const uint32_t dd = *reinterpret_cast<const uint32_t *>(blk);
+        const uint32_t s0 = *reinterpret_cast<const uint32_t *>(blk + 4);
+        const uint32_t s1 = *reinterpret_cast<const uint32_t *>(blk + 8);
+        const uint32_t s2 = *reinterpret_cast<const uint32_t *>(blk + 12);
+        uint32_t scv;
+        if (u < 4)
+            scv = scale_byte(s0, s1, s2, u) & 63u;
+        else
+            scv = (scale_byte(s0, s1, s2, u + 4) & 15u) | ((scale_byte(s0, s1, s2, u - 4) >> 6) << 4);
+        const float sv = __fmul_rn(f16_bits_to_f32(dd & 0xffffu), static_cast<float>(scv));
+        store_fold(fold, BN, u, row, sv);
+        if (u == 0) {
+            uint32_t mpk0 = 0, mpk1 = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t mnv = j < 4 ? scale_byte(s0, s1, s2, j + 4) & 63u
+                                           : (scale_byte(s0, s1, s2, j + 4) >> 4) | ((scale_byte(s0, s1, s2, j) >> 6) << 4);
+                if (j < 4)
+                    mpk0 |= mnv << (8 * j);
+                else
+                    mpk1 |= mnv << (8 * (j - 4));
+            }
+            const float dmin = f16_bits_to_f32(dd >> 16);
+            store_fold(mins_d, 0, 0, row, dmin);
+            mins_pk[row] = make_uint2(mpk0, mpk1);
+        }
     } else {
         // iq2_xxs: 32-value group u of the 66-byte block
         const uint32_t off = base + 2 + 8 * u;
@@ -310,6 +348,23 @@ PFNG_DEV void decode_task(const GemmParams &p, const uint8_t *wr, int8_t *bt, fl
     }
 }
 
+// q4_K min term, A side: the 8 sub-block sums of a row's q8_K activations
+// split into 6-bit low bytes and high bytes (sum = lo + 64 hi), packed for
+// dp4a against the packed 6-bit mins.
+PFNG_DEV uint4 pack_bsum(const int32_t *bsum) {
+    uint32_t l0 = 0, l1 = 0, h0 = 0, h1 = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int v = bsum[j];
+        const uint32_t lo = static_cast<uint32_t>(v & 63), hi = static_cast<uint32_t>(v >> 6) & 0xffu;
+        if (j < 4)
+            l0 |= lo << (8 * j), h0 |= hi << (8 * j);
+        else
+            l1 |= lo << (8 * (j - 4)), h1 |= hi << (8 * (j - 4));
+    }
+    return make_uint4(l0, l1, h0, h1);
+}
+
 // Unpack the raw W tile of stage `s` into the int8 B tile and the
 // per-(sub-block, column) fold data.  Runs once per CTA per k-step.
 template <int WT, class C>
@@ -317,70 +372,12 @@ PFNG_DEV void decode_w(const GemmParams &p, const Smem<C> &sm, int s, int64_t ks
     const uint8_t *wr = sm.w_raw(s);
     int8_t *bt = sm.b_tile();
     float *fold = reinterpret_cast<float *>(sm.fold());
-    if constexpr (WT != kWQ4_K) {
-        for (int task = tid; task < C::BN * 8; task += kThreads)
-            decode_task<WT, C::BN>(p, wr, bt, fold, sm.grid(), ks, n0, task);
-    } else {
-        for (int task = tid; task < C::BN * 8; task += kThreads) {
-            const int row = task >> 3, u = task & 7;
-            const uint32_t mis =
-                p.w_vec16 ? 0u : static_cast<uint32_t>((n0 + row) * p.row_bytes + ks * p.step_bytes) & 3u;
-            const uint32_t base = row * kWRowSlot + mis;
-            // u = (nibble pair pr, half h): 16 payload bytes -> 16 values of sub-blocks 2pr and 2pr+1
-            const uint8_t *blk = wr + base;
-            const int pr = u >> 1, h = u & 1;
-            const uint4 v = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * pr + 16 * h);
-            uint4 lo, hi;
-            lo.x = v.x & 0x0f0f0f0fu, lo.y = v.y & 0x0f0f0f0fu, lo.z = v.z & 0x0f0f0f0fu, lo.w = v.w & 0x0f0f0f0fu;
-            hi.x = (v.x >> 4) & 0x0f0f0f0fu, hi.y = (v.y >> 4) & 0x0f0f0f0fu;
-            hi.z = (v.z >> 4) & 0x0f0f0f0fu, hi.w = (v.w >> 4) & 0x0f0f0f0fu;
-            // sub-block 2pr holds k = 64 pr + j, sub-block 2pr + 1 holds k = 64 pr + 32 + j
-            store_pair(bt, row, 4 * pr + h, lo, 4 * pr + 2 + h, hi, pr >= 2);
-            // scale / min of sub-block u (llama_reference.cpp:116-121)
-            const uint32_t dd = *reinterpret_cast<const uint32_t *>(blk);
-            const uint32_t s0 = *reinterpret_cast<const uint32_t *>(blk + 4);
-            const uint32_t s1 = *reinterpret_cast<const uint32_t *>(blk + 8);
-            const uint32_t s2 = *reinterpret_cast<const uint32_t *>(blk + 12);
-            uint32_t scv;
-            if (u < 4)
-                scv = scale_byte(s0, s1, s2, u) & 63u;
-            else
-                scv = (scale_byte(s0, s1, s2, u + 4) & 15u) | ((scale_byte(s0, s1, s2, u - 4) >> 6) << 4);
-            const float sv = __fmul_rn(f16_bits_to_f32(dd & 0xffffu), static_cast<float>(scv));
-            store_fold(fold, C::BN, u, row, sv);
-            if (u == 0) {
-                uint32_t mpk0 = 0, mpk1 = 0;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const uint32_t mnv = j < 4 ? scale_byte(s0, s1, s2, j + 4) & 63u
-                                               : (scale_byte(s0, s1, s2, j + 4) >> 4) | ((scale_byte(s0, s1, s2, j) >> 6) << 4);
-                    if (j < 4)
-                        mpk0 |= mnv << (8 * j);
-                    else
-                        mpk1 |= mnv << (8 * (j - 4));
-                }
-                const float dmin = f16_bits_to_f32(dd >> 16);
-                store_fold(reinterpret_cast<float *>(sm.mins_d()), 0, 0, row, dmin);
-                sm.mins_pk()[row] = make_uint2(mpk0, mpk1);
-            }
-        }
-    }
+    for (int task = tid; task < C::BN * 8; task += kThreads)
+        decode_task<WT, C::BN>(p, wr, bt, fold, sm.grid(), ks, n0, task, reinterpret_cast<float *>(sm.mins_d()),
+                               sm.mins_pk());
     if constexpr (WT == kWQ4_K) {
-        // A side: bsum32 of each row split into 6-bit low bytes and high bytes
-        for (int r = tid; r < C::BM; r += kThreads) {
-            const int32_t *bsum = reinterpret_cast<const int32_t *>(sm.a_scale(s)) + r * kAScaleStride;
-            uint32_t l0 = 0, l1 = 0, h0 = 0, h1 = 0;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int v = bsum[j];
-                const uint32_t lo = static_cast<uint32_t>(v & 63), hi = static_cast<uint32_t>(v >> 6) & 0xffu;
-                if (j < 4)
-                    l0 |= lo << (8 * j), h0 |= hi << (8 * j);
-                else
-                    l1 |= lo << (8 * (j - 4)), h1 |= hi << (8 * (j - 4));
-            }
-            sm.a_pack()[r] = make_uint4(l0, l1, h0, h1);
-        }
+        for (int r = tid; r < C::BM; r += kThreads)
+            sm.a_pack()[r] = pack_bsum(reinterpret_cast<const int32_t *>(sm.a_scale(s)) + r * kAScaleStride);
     }
 }
 
@@ -695,7 +692,7 @@ struct SmemOv {
 
 template <int WT, class C>
 __global__ void __launch_bounds__(kThreads) gemm_kernel_ov(const GemmParams p) {
-    static_assert(WT != kWQ4_K, "the q4_K decode reads its k-step's activation sums");
+    static_assert(WT != kWQ4_K, "q4_K products run on the two-phase kernel");
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const SmemOv<C> sm{smem_raw};
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -986,11 +983,14 @@ cudaError_t launch_t_ov(const GemmParams &p, cudaStream_t s) {
     return launch_pdl<C>(kernel, p, smem, s);
 }
 
-// The overlapped kernel serves q4_0 (both layouts) and iq2_xxs products;
+// The overlapped kernel serves q4_0 (both layouts) and iq2_xxs products
+// without split-K (the partials mode keeps the two-phase kernel);
 // PFNG_B200_GEMM_OV=0 selects the two-phase kernel instead (comparisons).
 // Measured on B200 (us per quantize + GEMM step, overlapped vs two-phase):
 // 2048x11008x4096 627 vs 698, 512x4096x4096 66 vs 73, 480x1536x1536 on 64 x 64
-// tiles 20.2 vs 21.3 (q4_0) and 24.6 vs 25.3 (iq2_xxs).
+// tiles 20.2 vs 21.3 (q4_0) and 24.6 vs 25.3 (iq2_xxs).  q4_K, whose min term
+// the overlapped kernel adds once per 256-block from the resident A tile, was
+// slower there: 2048x4096x4096 353 vs 338, 512x4096x4096 90.0 vs 85.9.
 template <int WT, bool kPartials>
 constexpr bool kOvType = !kPartials && WT != kWQ4_K;
 inline bool ov_enabled() {
@@ -1000,7 +1000,9 @@ inline bool ov_enabled() {
 
 template <int WT, class C, bool kPartials>
 cudaError_t launch_pick(const GemmParams &p, cudaStream_t s) {
-    if constexpr (kOvType<WT, kPartials>) {
+    // 32-row tiles keep the two-phase kernel: its two-deep ring fits two CTAs
+    // per SM, the overlapped kernel's buffers one (32x32000x4096: 63 vs 74 us)
+    if constexpr (kOvType<WT, kPartials> && C::BM > 32) {
         if (p.splits == 1 && ov_enabled()) return launch_t_ov<WT, C>(p, s);
     }
     return launch_t<WT, C, kPartials>(p, s);

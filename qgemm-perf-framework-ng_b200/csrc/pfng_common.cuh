@@ -157,7 +157,10 @@ PFNG_DEV uint32_t expand_bits4(uint32_t bits) {
     const uint32_t spread = ((bits & 0xfu) * 0x00204081u) & 0x01010101u;
     return spread * 0xffu;
 }
-// Apply byte masks: negate the bytes whose mask is 0xff.
-PFNG_DEV uint32_t apply_sign_bytes(uint32_t v, uint32_t mask) { return __vsub4(v ^ mask, mask); }
+// Apply byte masks: negate the bytes whose mask is 0xff.  For a byte b != 0,
+// (b ^ 0xff) + 1 = 256 - b stays within the byte, so one 32-bit add negates
+// every masked byte without a carry into its neighbour; the iq2_xxs grid
+// magnitudes (8, 25, 43) are never 0.
+PFNG_DEV uint32_t apply_sign_bytes(uint32_t v, uint32_t mask) { return (v ^ mask) + (mask & 0x01010101u); }
 
 }  // namespace pfng
