@@ -496,7 +496,8 @@ LLAMA_SHAPES = [(nn, kk) for nn, kk in ((4096, 4096), (11008, 4096), (4096, 1100
 
 def llama(args) -> int:
     """Llama-2-7B q4_0 prefill shapes, weight rows sharded over the ranks, x broadcast from
-    rank 0 and the output column slices all-gathered with NCCL.  One JSON line per shape."""
+    rank 0, each rank's output columns stored into every rank's C by its GEMM epilogue
+    (pfng_b200_compute_gather); the NCCL all-gather variant is timed beside it.  One JSON line per shape."""
     import torch
     import pfng_b200 as pb
     world, rank, local = dist_env()
@@ -541,6 +542,21 @@ def llama(args) -> int:
                 else:
                     full.copy_(slice_[:, :n])
 
+            # the all-gather fused into the GEMM: every rank's epilogue stores
+            # its columns into every rank's full C over NVLink (CUDA IPC);
+            # a one-element all-reduce after it orders the ranks
+            gc = pb.GatheredC(m, n) if dist is not None else None
+            dsts = gc.destinations(b) if gc is not None else [full]
+            flag = torch.zeros(1, device="cuda")
+
+            def fused_step(i):
+                if dist is not None:
+                    dist.broadcast(x, src=0)
+                if e > b:
+                    pb.compute_gather("q4_0", wsh[i % copies], x, e - b, dsts, n, workspace=wsp, stream=stream)
+                if dist is not None:
+                    dist.all_reduce(flag)
+
             def timed(fn):
                 for i in range(args.warmup):
                     fn(i)
@@ -561,8 +577,12 @@ def llama(args) -> int:
                 return t
 
             t_compute = timed(local_gemm)
-            t_e2e = timed(full_step)
+            t_nccl = timed(full_step)
+            t_e2e = timed(fused_step)
             pb.check_kernel_error()
+            if gc is not None:
+                torch.cuda.synchronize()
+                gc.close()
             if rank == 0:
                 ops = 2.0 * m * n * k
                 peak, peak_src = int8_peak_tops()
@@ -571,10 +591,13 @@ def llama(args) -> int:
                     "n_gpus": world, "scaling": "strong", "value": args.steps * ops / t_e2e / 1e9, "unit": UNIT,
                     "compute_only": args.steps * ops / t_compute / 1e9, "us_per_step_e2e": t_e2e / args.steps * 1e6,
                     "us_per_step_compute": t_compute / args.steps * 1e6,
+                    "us_per_step_e2e_nccl_all_gather": t_nccl / args.steps * 1e6,
                     "compute_frac_of_int8_peak": ops / (t_compute / args.steps) / 1e12 / peak,
                     "peak_source": peak_src, "rows_per_rank": e - b,
-                    "exchange": "NCCL broadcast of x, all-gather of C column slices, device unshard"
-                    if world > 1 else "none",
+                    "exchange": "NCCL broadcast of x; C gathered by the GEMM epilogue's stores into every rank's C "
+                    "(CUDA IPC over NVLink), one-element NCCL all-reduce as the completion barrier; "
+                    "us_per_step_e2e_nccl_all_gather: the same step with an NCCL all-gather of C slices and a "
+                    "device unshard instead" if world > 1 else "none",
                 }), flush=True)
             del wsh, gathered, full, slice_
             torch.cuda.empty_cache()

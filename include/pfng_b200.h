@@ -225,6 +225,41 @@ int pfng_b200_shard_rows(int64_t n, int world, int rank, int64_t granule, int64_
 int pfng_b200_unshard_columns(const float *slices, float *c, int64_t m, int64_t n, int64_t ldc, int world,
                               int64_t granule, int64_t slice_width, void *stream);
 
+/* ---- fused output all-gather over peer memory -----------------------------
+ * pfng_b200_compute_* (fp32 activations, fp32 C) writing the same C [m][n]
+ * to `ndst` destinations at once, each with row stride `ldd` floats.  With
+ * weight rows sharded over the GPUs of a node, rank r passes the column
+ * offset begin_r (pfng_b200_shard_rows) into every rank's full C -- its own
+ * and the others', mapped with pfng_b200_ipc_open -- so that the GEMM's
+ * epilogue stores each finished tile over NVLink while the other tiles are
+ * still computing: the all-gather of C fused into the matmul, with no
+ * collective and no reassembly pass.
+ *   - On the MMA path every tile goes to all destinations from registers,
+ *     followed by a system-scope fence; the GEMV and SIMPLE paths compute
+ *     into dst[0] and copy it to the others on the stream.
+ *   - The call does not wait for the other ranks.  Before a rank reads its C
+ *     (or a next call writes into the others'), every rank's call must have
+ *     completed: order the ranks with a barrier or collective on the stream
+ *     (e.g. a one-element NCCL all-reduce) after the call.
+ *   - workspace: pfng_b200_compute_workspace_size for (wtype, m, n, k, path).
+ * No counterpart in the reference (a single-device library); C equals
+ * pfng_b200_compute_* of the same arguments bit for bit. */
+#define PFNG_B200_MAX_DESTINATIONS 8
+int pfng_b200_compute_gather(int wtype, const void *w, const float *x, int64_t ldx, float *const *dst, int ndst,
+                             int64_t ldd, int64_t m, int64_t n, int64_t k, void *workspace, size_t workspace_bytes,
+                             int path, void *stream);
+
+/* Device buffers shared between the processes of a node (CUDA IPC): alloc
+ * returns a cudaMalloc'd buffer of the current device and its 64-byte
+ * handle; another process opens the handle to a device pointer to the same
+ * memory (peer access over NVLink), closes it when done, and the owner frees
+ * the buffer after every opener has closed it. */
+#define PFNG_B200_IPC_HANDLE_BYTES 64
+int pfng_b200_ipc_alloc(size_t bytes, void **ptr, void *handle);
+int pfng_b200_ipc_free(void *ptr);
+int pfng_b200_ipc_open(const void *handle, void **ptr);
+int pfng_b200_ipc_close(void *ptr);
+
 /* ---- matmul without any allocation ----------------------------------------
  * pfng_b200_compute_q4_0 on the tensor-core path (fp32 activations x [m][ldx]
  * quantized to q8_0, then C = A . W^T), for callers that must not allocate

@@ -157,16 +157,24 @@ void carve_partial(GemmArgs &g, void *workspace, size_t workspace_need, int wtyp
 }
 
 // The shared body of mm / compute / partials.
+// `copies` (fp32 C only): ncopies more destinations that receive C with
+// C's layout -- the MMA GEMM stores each tile to all of them in its
+// epilogue, the other paths copy C after computing it.
 int run_matmul(int wtype, const void *w, const void *a, const float *x, int64_t ldx, float *c, int64_t ldc,
                int32_t *partials, int64_t m, int64_t n, int64_t k, void *workspace, size_t workspace_bytes,
-               int path, cudaStream_t s) {
+               int path, cudaStream_t s, float *const *copies = nullptr, int ncopies = 0) {
     const bool f32 = x != nullptr;
     int st = check_mm(wtype, w, f32 ? static_cast<const void *>(x) : a, partials ? static_cast<void *>(partials) : c,
                       m, n, k, ldc, ldx, f32, partials != nullptr, path);
     if (st != PFNG_B200_OK || m == 0 || n == 0) return st;
     DeviceInfo *info = nullptr;
     if ((st = device_info(&info)) != PFNG_B200_OK) return st;
-    if (k == 0) return partials ? PFNG_B200_OK : status_of(zero_c(c, m, n, ldc, s));
+    if (k == 0) {
+        if (partials) return PFNG_B200_OK;
+        cudaError_t e = zero_c(c, m, n, ldc, s);
+        for (int d = 0; d < ncopies && e == cudaSuccess; ++d) e = zero_c(copies[d], m, n, ldc, s);
+        return status_of(e);
+    }
     const int resolved = resolve_path(wtype, m, n, k, w, path);
     if (resolved < 0) return PFNG_B200_ERR_UNSUPPORTED;
     const size_t need = workspace_for(wtype, m, n, k, resolved, f32);
@@ -199,8 +207,11 @@ int run_matmul(int wtype, const void *w, const void *a, const float *x, int64_t 
         if (e == cudaSuccess) {
             GemmArgs g{wtype, w, sa, c, ldc, partials, m, n, k, info->error_word};
             carve_partial(g, workspace, need, wtype, m, k);
+            g.copies = copies;
+            g.ncopies = ncopies;
             e = launch_gemm(g, s);
         }
+        return status_of(e);
     } else {
         const void *araw = a;
         if (f32) {
@@ -214,6 +225,11 @@ int run_matmul(int wtype, const void *w, const void *a, const float *x, int64_t 
             e = launch_simple(g, s);
         }
     }
+    // GEMV and SIMPLE: C to the other destinations by device copies
+    const size_t pitch = static_cast<size_t>(ldc) * sizeof(float);
+    for (int d = 0; d < ncopies && e == cudaSuccess; ++d)
+        e = cudaMemcpy2DAsync(copies[d], pitch, c, pitch, static_cast<size_t>(n) * sizeof(float),
+                              static_cast<size_t>(m), cudaMemcpyDefault, s);
     return status_of(e);
 }
 
@@ -629,5 +645,53 @@ int pfng_b200_unshard_columns(const float *slices, float *c, int64_t m, int64_t 
     return status_of(launch_unshard_columns(slices, c, m, n, ldc, world, granule, slice_width,
                                             static_cast<cudaStream_t>(stream)));
 }
+
+int pfng_b200_compute_gather(int wtype, const void *w, const float *x, int64_t ldx, float *const *dst, int ndst,
+                             int64_t ldd, int64_t m, int64_t n, int64_t k, void *workspace, size_t workspace_bytes,
+                             int path, void *stream) {
+    if (ndst < 1 || ndst > PFNG_B200_MAX_DESTINATIONS || !dst) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    if (m > 0 && n > 0) {
+        for (int d = 0; d < ndst; ++d) {
+            if (!dst[d]) return PFNG_B200_ERR_INVALID_ARGUMENT;
+            if (!aligned(dst[d], 4)) return PFNG_B200_ERR_ALIGNMENT;
+        }
+        if (!x && k > 0) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    }
+    static_assert(PFNG_B200_MAX_DESTINATIONS == kMaxCopies + 1, "destination count");
+    return run_matmul(wtype, w, nullptr, x, ldx, dst[0], ldd, nullptr, m, n, k, workspace, workspace_bytes, path,
+                      static_cast<cudaStream_t>(stream), dst + 1, ndst - 1);
+}
+
+// Device buffers other processes can map: cudaMalloc'd (the unit CUDA IPC
+// exports), so the handle maps the buffer from its first byte.
+int pfng_b200_ipc_alloc(size_t bytes, void **ptr, void *handle) {
+    if (!ptr || !handle || bytes == 0) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    static_assert(sizeof(cudaIpcMemHandle_t) == PFNG_B200_IPC_HANDLE_BYTES, "IPC handle size");
+    *ptr = nullptr;
+    void *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) return status_of(e);
+    cudaIpcMemHandle_t h;
+    e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return status_of(e);
+    }
+    std::memcpy(handle, &h, sizeof h);
+    *ptr = p;
+    return PFNG_B200_OK;
+}
+
+int pfng_b200_ipc_free(void *ptr) { return ptr ? status_of(cudaFree(ptr)) : PFNG_B200_OK; }
+
+int pfng_b200_ipc_open(const void *handle, void **ptr) {
+    if (!ptr || !handle) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    *ptr = nullptr;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof h);
+    return status_of(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int pfng_b200_ipc_close(void *ptr) { return ptr ? status_of(cudaIpcCloseMemHandle(ptr)) : PFNG_B200_OK; }
 
 }  // extern "C"

@@ -99,6 +99,11 @@ struct GemmParams {
     int splits;
     int ks_per_split;
     float *partial;
+    // fp32 C stored also to copies[0 .. ncopies) (same row stride ldc); c_vec4:
+    // c, every copy and ldc allow 16-byte accesses of column quads
+    float *copies[kMaxCopies];
+    int ncopies;
+    int c_vec4;
 };
 
 PFNG_DEV void cp_async16(void *dst, const void *src, uint32_t src_bytes) {
@@ -443,8 +448,54 @@ template <class C>
 PFNG_DEV void epilogue_q8_0(const GemmParams &p, uint8_t *smem, const float2 (&acc)[C::MT][C::NT][2], int64_t m0,
                             int64_t n0, int tid);
 PFNG_DEV void store_out2(const GemmParams &p, int64_t r, int64_t c, float2 v);
+// fp32 C to the copies as well (kernels instantiated with kCopies): after
+// the epilogue the CTA reads its finished tile back from C (in L2) and
+// stores it to every copy in 16-byte pieces along rows, all of a thread's
+// loads issued before its stores; a system-scope fence then makes the stores
+// performed before the kernel ends, so that a collective the caller orders
+// after this kernel publishes them.  Only the kCopies kernels carry this
+// code: inlined into the kernels without copies, a copies loop cost the
+// 2048 x 11008 x 4096 GEMM 35 % (626 -> 845 us).
+template <class C>
+PFNG_DEV void copy_tile_to_copies(const GemmParams &p) {
+    if (p.ncopies == 0) return;
+    // the tile origin from the special registers: nothing of it stays live
+    // across the main loop
+    const int64_t n0 = static_cast<int64_t>(blockIdx.x) * C::BN;
+    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * C::BM;
+    const int tid = threadIdx.x;
+    const int rows = static_cast<int>(p.m - m0 < C::BM ? p.m - m0 : C::BM);
+    const int cols = static_cast<int>(p.n - n0 < C::BN ? p.n - n0 : C::BN);
+    constexpr int kQuads = C::BN / 4;
+    constexpr int kPer = C::BM * kQuads / kThreads;
+    static_assert(C::BM * kQuads % kThreads == 0, "whole tile rounds");
+    __syncthreads();  // the whole tile is in C
+    if (p.c_vec4 && cols == C::BN) {
+        float4 v[kPer];
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+            const int i = tid + j * kThreads, r = i / kQuads;
+            if (r < rows) v[j] = *reinterpret_cast<const float4 *>(p.c + (m0 + r) * p.ldc + n0 + (i % kQuads) * 4);
+        }
+        for (int d = 0; d < p.ncopies; ++d) {
+#pragma unroll
+            for (int j = 0; j < kPer; ++j) {
+                const int i = tid + j * kThreads, r = i / kQuads;
+                if (r < rows) *reinterpret_cast<float4 *>(p.copies[d] + (m0 + r) * p.ldc + n0 + (i % kQuads) * 4) = v[j];
+            }
+        }
+    } else {
+        for (int i = tid; i < rows * C::BN; i += kThreads) {
+            const int r = i / C::BN, col = i % C::BN;
+            if (col >= cols) continue;
+            const float v = p.c[(m0 + r) * p.ldc + n0 + col];
+            for (int d = 0; d < p.ncopies; ++d) p.copies[d][(m0 + r) * p.ldc + n0 + col] = v;
+        }
+    }
+    __threadfence_system();
+}
 
-template <int WT, class C, bool kPartials>
+template <int WT, class C, bool kPartials, bool kCopies = false>
 __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Smem<C> sm{smem_raw};
@@ -652,6 +703,7 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
                     const int64_t c = n0 + wn * C::WN + nt * 8 + 2 * t4;
                     if (r < p.m) store_out2(p, r, c, acc[mt][nt][h]);
                 }
+        if constexpr (kCopies) copy_tile_to_copies<C>(p);
     }
 }
 
@@ -690,7 +742,7 @@ struct SmemOv {
     }
 };
 
-template <int WT, class C>
+template <int WT, class C, bool kCopies = false>
 __global__ void __launch_bounds__(kThreads) gemm_kernel_ov(const GemmParams p) {
     static_assert(WT != kWQ4_K, "q4_K products run on the two-phase kernel");
     extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -830,6 +882,7 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel_ov(const GemmParams p) {
                 const int64_t c = n0 + wn * C::WN + nt * 8 + 2 * t4;
                 if (r < p.m) store_out2(p, r, c, acc[mt][nt][h]);
             }
+    if constexpr (kCopies) copy_tile_to_copies<C>(p);
 }
 
 // C tile of the CTA quantized to q8_0 along n: the tile is staged in shared
@@ -932,6 +985,12 @@ __global__ void __launch_bounds__(kThreads) reduce_splits_kernel(const GemmParam
     }
 #pragma unroll
     for (int i = 0; i < 4; i += 2) store_out2(p, r, c0 + i, make_float2(v[i], v[i + 1]));
+    if (p.ncopies > 0) {
+        for (int d = 0; d < p.ncopies; ++d)
+            for (int i = 0; i < 4; ++i)
+                if (c0 + i < p.n) p.copies[d][r * p.ldc + c0 + i] = v[i];
+        __threadfence_system();
+    }
 }
 
 // Launch as a programmatic dependent of the preceding kernel on the stream
@@ -953,9 +1012,9 @@ cudaError_t launch_pdl(K kernel, const GemmParams &p, uint32_t smem, cudaStream_
     return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
-template <int WT, class C, bool kPartials>
+template <int WT, class C, bool kPartials, bool kCopies = false>
 cudaError_t launch_t(const GemmParams &p, cudaStream_t s) {
-    auto kernel = gemm_kernel<WT, C, kPartials>;
+    auto kernel = gemm_kernel<WT, C, kPartials, kCopies>;
     static thread_local bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -967,9 +1026,9 @@ cudaError_t launch_t(const GemmParams &p, cudaStream_t s) {
     return launch_pdl<C>(kernel, p, C::kSmem, s);
 }
 
-template <int WT, class C>
+template <int WT, class C, bool kCopies = false>
 cudaError_t launch_t_ov(const GemmParams &p, cudaStream_t s) {
-    auto kernel = gemm_kernel_ov<WT, C>;
+    auto kernel = gemm_kernel_ov<WT, C, kCopies>;
     constexpr uint32_t smem = SmemOv<C>::kTotal;
     static_assert(C::BM * (C::BN + 4) * 4 <= smem, "staged C tile of the q8_0 epilogue");
     static thread_local bool configured[64] = {false};
@@ -1002,8 +1061,15 @@ template <int WT, class C, bool kPartials>
 cudaError_t launch_pick(const GemmParams &p, cudaStream_t s) {
     // 32-row tiles keep the two-phase kernel: its two-deep ring fits two CTAs
     // per SM, the overlapped kernel's buffers one (32x32000x4096: 63 vs 74 us)
+    // copies (fp32 C to more destinations): the kernels built with the copy
+    // pass; with split-K the reduction stores the copies
+    const bool copies = p.ncopies > 0 && p.splits == 1;
     if constexpr (kOvType<WT, kPartials> && C::BM > 32) {
-        if (p.splits == 1 && ov_enabled()) return launch_t_ov<WT, C>(p, s);
+        if (p.splits == 1 && ov_enabled())
+            return copies ? launch_t_ov<WT, C, true>(p, s) : launch_t_ov<WT, C>(p, s);
+    }
+    if constexpr (!kPartials) {
+        if (copies) return launch_t<WT, C, false, true>(p, s);
     }
     return launch_t<WT, C, kPartials>(p, s);
 }
@@ -1064,8 +1130,50 @@ int splits_for(TileKind t, int64_t m, int64_t n, int64_t k, int64_t sms) {
     return static_cast<int>((kt + per - 1) / per);
 }
 
+// C [m][n] (row stride ldc) to every copy after the GEMM: one grid over all
+// SMs, 16-byte pieces along rows where c_vec4 allows, then a system-scope
+// fence (the stores are performed before the kernel ends).
+__global__ void __launch_bounds__(kThreads) push_copies_kernel(const GemmParams p) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+    if (p.c_vec4) {
+        const int64_t quads = p.n / 4, total = p.m * quads;
+        for (int64_t i = tid; i < total; i += stride) {
+            const int64_t o = (i / quads) * p.ldc + (i % quads) * 4;
+            const float4 v = *reinterpret_cast<const float4 *>(p.c + o);
+            for (int d = 0; d < p.ncopies; ++d) *reinterpret_cast<float4 *>(p.copies[d] + o) = v;
+        }
+        for (int64_t i = tid; i < p.m * (p.n % 4); i += stride) {  // ragged columns
+            const int64_t o = (i / (p.n % 4)) * p.ldc + quads * 4 + i % (p.n % 4);
+            for (int d = 0; d < p.ncopies; ++d) p.copies[d][o] = p.c[o];
+        }
+    } else {
+        for (int64_t i = tid; i < p.m * p.n; i += stride) {
+            const int64_t o = (i / p.n) * p.ldc + i % p.n;
+            for (int d = 0; d < p.ncopies; ++d) p.copies[d][o] = p.c[o];
+        }
+    }
+    __threadfence_system();
+}
+
+// How the copies are written: in the GEMM's epilogue (default) or by
+// push_copies_kernel after it (PFNG_B200_COPIES=push).
+inline bool push_copies() {
+    const char *e = std::getenv("PFNG_B200_COPIES");
+    return e && std::strcmp(e, "push") == 0;
+}
+
 template <int WT, bool kPartials>
 cudaError_t launch_tile(GemmParams &p, cudaStream_t s) {
+    if (p.ncopies > 0 && p.out_format == kOutF32 && push_copies()) {
+        GemmParams q = p;
+        q.ncopies = 0;
+        cudaError_t e = launch_tile<WT, kPartials>(q, s);
+        if (e != cudaSuccess) return e;
+        const int64_t sms = device_sm_count();
+        push_copies_kernel<<<static_cast<unsigned>(sms * 4), kThreads, 0, s>>>(p);
+        return cudaGetLastError();
+    }
     const int64_t sms = device_sm_count();
     const TileKind t = tile_choice(p.m, p.n, sms);
     const int64_t kt = p.k / BK;
@@ -1111,7 +1219,7 @@ bool gemm_supported(int wtype, int64_t m, int64_t n, int64_t k, const void *w) {
 // environment variable PFNG_B200_GEMM is "mma" (or the shape is unsupported);
 // "tc" / "mma" select either kernel explicitly, for comparisons.
 static bool use_tc(const GemmArgs &args) {
-    if (args.wtype != kWQ4_0 || args.partials || args.out_format != kOutF32) return false;
+    if (args.wtype != kWQ4_0 || args.partials || args.out_format != kOutF32 || args.ncopies > 0) return false;
     const char *e = std::getenv("PFNG_B200_GEMM");
     const bool want = e ? std::strcmp(e, "tc") == 0 : kTcDefault;
     return want && gemm_tc_supported(args.wtype, args.m, args.n, args.k, args.w);
@@ -1135,6 +1243,13 @@ cudaError_t launch_gemm(const GemmArgs &args, cudaStream_t s) {
     p.out_format = args.out_format;
     p.out = args.out;
     p.ldo = args.ldo;
+    p.ncopies = args.copies ? args.ncopies : 0;
+    bool vec4 = reinterpret_cast<uintptr_t>(args.c) % 16 == 0 && args.ldc % 4 == 0;
+    for (int d = 0; d < p.ncopies; ++d) {
+        p.copies[d] = args.copies[d];
+        vec4 = vec4 && reinterpret_cast<uintptr_t>(args.copies[d]) % 16 == 0;
+    }
+    p.c_vec4 = vec4 ? 1 : 0;
     // split-K partials, when the caller's workspace holds them
     const size_t need = gemm_partial_bytes(args.m, args.n, args.k);
     p.partial = (need > 0 && args.partial && args.partial_bytes >= need) ? args.partial : nullptr;

@@ -90,7 +90,12 @@ struct GemmArgs {
     // them the product runs unsplit
     float *partial = nullptr;
     size_t partial_bytes = 0;
+    // fp32 C also stored to `ncopies` more destinations with C's layout (row
+    // stride ldc), e.g. other GPUs' C mapped through CUDA IPC
+    float *const *copies = nullptr;
+    int ncopies = 0;
 };
+constexpr int kMaxCopies = 7;
 bool gemm_supported(int wtype, int64_t m, int64_t n, int64_t k, const void *w);
 // workspace bytes of the split-K partial tiles for this shape (0: no split)
 size_t gemm_partial_bytes(int64_t m, int64_t n, int64_t k);

@@ -112,6 +112,16 @@ def _declare(L: ctypes.CDLL) -> None:
     L.pfng_b200_shard_rows.argtypes = [I64, I, I, I64, ctypes.POINTER(I64), ctypes.POINTER(I64)]
     L.pfng_b200_unshard_columns.restype = I
     L.pfng_b200_unshard_columns.argtypes = [P, P, I64, I64, I64, I, I64, I64, P]
+    L.pfng_b200_compute_gather.restype = I
+    L.pfng_b200_compute_gather.argtypes = [I, P, P, I64, ctypes.POINTER(P), I, I64, I64, I64, I64, P, S, I, P]
+    L.pfng_b200_ipc_alloc.restype = I
+    L.pfng_b200_ipc_alloc.argtypes = [S, ctypes.POINTER(P), P]
+    L.pfng_b200_ipc_open.restype = I
+    L.pfng_b200_ipc_open.argtypes = [P, ctypes.POINTER(P)]
+    for name in ("ipc_free", "ipc_close"):
+        f = getattr(L, f"pfng_b200_{name}")
+        f.restype = I
+        f.argtypes = [P]
 
 
 def header_functions() -> list[str]:
@@ -361,6 +371,109 @@ def unshard_columns(slices, m: int, n: int, world: int, granule: int, out=None, 
     _check(lib().pfng_b200_unshard_columns(_ptr(slices), _ptr(out), m, n, out.stride(0), world, granule,
                                            width, _stream(stream)), "unshard_columns")
     return out
+
+
+# ------------------------------------------- fused all-gather of C over NVLink
+MAX_DESTINATIONS = 8
+IPC_HANDLE_BYTES = 64
+
+
+def compute_gather(wtype, w, x, n: int, destinations, ldd: int, path="auto", workspace=None, stream=None) -> None:
+    """compute() storing C [m][n] to every device pointer in `destinations` (row stride `ldd` floats):
+    the first is typically this GPU's C, the others other GPUs' C opened with ipc_open.  The call
+    does not wait for other ranks; order them (a barrier or collective on the stream) before C is read."""
+    wt, p = _wt(wtype), _path(path)
+    m, k = x.shape
+    ptrs = [d if isinstance(d, int) else d.data_ptr() for d in destinations]
+    arr = (ctypes.c_void_p * max(1, len(ptrs)))(*ptrs)
+    ws = _workspace(compute_workspace_size(wt, m, n, k, p), x.device, workspace)
+    nbytes = 0 if ws is None else ws.numel()
+    _check(lib().pfng_b200_compute_gather(wt, _ptr(w), _ptr(x), x.stride(0), arr, len(ptrs), ldd, m, n, k,
+                                          _ptr(ws), nbytes, p, _stream(stream)), "compute_gather")
+
+
+def ipc_alloc(nbytes: int) -> tuple[int, bytes]:
+    """A device buffer of the current GPU that other processes can open: (pointer, 64-byte handle)."""
+    ptr, handle = ctypes.c_void_p(), ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    _check(lib().pfng_b200_ipc_alloc(nbytes, ctypes.byref(ptr), handle), "ipc_alloc")
+    return ptr.value, handle.raw
+
+
+def ipc_free(ptr: int) -> None:
+    _check(lib().pfng_b200_ipc_free(ptr), "ipc_free")
+
+
+def ipc_open(handle: bytes) -> int:
+    """Device pointer (on the current GPU's address space) to another process's ipc_alloc buffer."""
+    ptr = ctypes.c_void_p()
+    buf = ctypes.create_string_buffer(bytes(handle), IPC_HANDLE_BYTES)
+    _check(lib().pfng_b200_ipc_open(buf, ctypes.byref(ptr)), "ipc_open")
+    return ptr.value
+
+
+def ipc_close(ptr: int) -> None:
+    _check(lib().pfng_b200_ipc_close(ptr), "ipc_close")
+
+
+class _DeviceArray:
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def device_tensor(ptr: int, shape, device=None):
+    """A float32 torch tensor viewing `shape` floats at device pointer `ptr` (no copy, not owning)."""
+    import torch
+    return torch.as_tensor(_DeviceArray(ptr, shape, "<f4"), device=device or torch.device("cuda"))
+
+
+class _Ipc:
+    alloc = staticmethod(ipc_alloc)
+    free = staticmethod(ipc_free)
+    open = staticmethod(ipc_open)
+    close = staticmethod(ipc_close)
+
+
+class GatheredC:
+    """Full fp32 C [m][n] on every rank of one node, writable by every rank.
+
+    Each rank allocates its C with ipc_alloc; the handles are all-gathered
+    over `group` (torch.distributed) and every rank opens the others'.  A rank
+    whose weight rows are [begin, end) (shard_rows) passes
+    destinations(begin) to compute_gather: its own C first, then the other
+    ranks' C in rank order, each offset by `begin` columns, with ldd = n.
+    `ipc` replaces the CUDA IPC calls (tests of the host logic)."""
+
+    def __init__(self, m: int, n: int, group=None, ipc=None):
+        import torch.distributed as dist
+        self.m, self.n, self.group = m, n, group
+        self._ipc = ipc or _Ipc
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.ptr, handle = self._ipc.alloc(max(1, m * n) * 4)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        self.bases = [self.ptr if r == self.rank else self._ipc.open(handles[r]) for r in range(self.world)]
+
+    def destinations(self, col: int) -> list[int]:
+        order = [self.rank] + [r for r in range(self.world) if r != self.rank]
+        return [self.bases[r] + 4 * col for r in order]
+
+    def tensor(self):
+        """This rank's C as a torch tensor (valid until close())."""
+        return device_tensor(self.ptr, (self.m, self.n))
+
+    def close(self) -> None:
+        """Unmap the other ranks' C, wait for every rank to do the same, free this rank's C."""
+        import torch.distributed as dist
+        if self.bases is None:
+            return
+        for r, b in enumerate(self.bases):
+            if r != self.rank:
+                self._ipc.close(b)
+        dist.barrier(group=self.group)
+        self._ipc.free(self.ptr)
+        self.bases = None
 
 
 def loaded_library_path() -> str:
