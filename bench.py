@@ -495,9 +495,9 @@ LLAMA_SHAPES = [(nn, kk) for nn, kk in ((4096, 4096), (11008, 4096), (4096, 1100
 
 
 def llama(args) -> int:
-    """Llama-2-7B q4_0 prefill shapes, weight rows sharded over the ranks, x broadcast from
-    rank 0, each rank's output columns stored into every rank's C by its GEMM epilogue
-    (pfng_b200_compute_gather); the NCCL all-gather variant is timed beside it.  One JSON line per shape."""
+    """Llama-2-7B q4_0 prefill shapes, weight rows sharded over the ranks, x quantized on
+    rank 0 and broadcast as q8_0, each rank's output columns stored into every rank's C by its matmul
+    (pfng_b200_mm_gather); the NCCL all-gather variant is timed beside it.  One JSON line per shape."""
     import torch
     import pfng_b200 as pb
     world, rank, local = dist_env()
@@ -545,15 +545,22 @@ def llama(args) -> int:
             # the all-gather fused into the GEMM: every rank's epilogue stores
             # its columns into every rank's full C over NVLink (CUDA IPC);
             # a one-element all-reduce after it orders the ranks
+            # rank 0 quantizes x and broadcasts the q8_0 bytes (1.06 bytes per
+            # value instead of 4); a one-element all-reduce after the matmul
+            # orders the ranks
             gc = pb.GatheredC(m, n) if dist is not None else None
             dsts = gc.destinations(b) if gc is not None else [full]
             flag = torch.zeros(1, device="cuda")
+            aq = torch.empty(m * (k // 32) * pb.Q8_0_BYTES, dtype=torch.uint8, device="cuda")
+            wsm = torch.empty(max(1, pb.mm_workspace_size("q4_0", m, width, k)), dtype=torch.uint8, device="cuda")
 
             def fused_step(i):
+                if rank == 0:
+                    pb.quantize_q8_0(x, out=aq, stream=stream)
                 if dist is not None:
-                    dist.broadcast(x, src=0)
+                    dist.broadcast(aq, src=0)
                 if e > b:
-                    pb.compute_gather("q4_0", wsh[i % copies], x, e - b, dsts, n, workspace=wsp, stream=stream)
+                    pb.mm_gather("q4_0", wsh[i % copies], aq, m, e - b, k, dsts, n, workspace=wsm, stream=stream)
                 if dist is not None:
                     dist.all_reduce(flag)
 
@@ -594,10 +601,10 @@ def llama(args) -> int:
                     "us_per_step_e2e_nccl_all_gather": t_nccl / args.steps * 1e6,
                     "compute_frac_of_int8_peak": ops / (t_compute / args.steps) / 1e12 / peak,
                     "peak_source": peak_src, "rows_per_rank": e - b,
-                    "exchange": "NCCL broadcast of x; C gathered by the GEMM epilogue's stores into every rank's C "
-                    "(CUDA IPC over NVLink), one-element NCCL all-reduce as the completion barrier; "
-                    "us_per_step_e2e_nccl_all_gather: the same step with an NCCL all-gather of C slices and a "
-                    "device unshard instead" if world > 1 else "none",
+                    "exchange": "x quantized to q8_0 on rank 0 and NCCL-broadcast; each rank's matmul stores its C "
+                    "columns into every rank's C (CUDA IPC over NVLink, pfng_b200_mm_gather); one-element NCCL "
+                    "all-reduce as the completion barrier; us_per_step_e2e_nccl_all_gather: fp32 x broadcast, "
+                    "NCCL all-gather of C slices and a device unshard instead" if world > 1 else "none",
                 }), flush=True)
             del wsh, gathered, full, slice_
             torch.cuda.empty_cache()

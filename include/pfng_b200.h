@@ -230,13 +230,15 @@ int pfng_b200_unshard_columns(const float *slices, float *c, int64_t m, int64_t 
  * to `ndst` destinations at once, each with row stride `ldd` floats.  With
  * weight rows sharded over the GPUs of a node, rank r passes the column
  * offset begin_r (pfng_b200_shard_rows) into every rank's full C -- its own
- * and the others', mapped with pfng_b200_ipc_open -- so that the GEMM's
- * epilogue stores each finished tile over NVLink while the other tiles are
- * still computing: the all-gather of C fused into the matmul, with no
- * collective and no reassembly pass.
- *   - On the MMA path every tile goes to all destinations from registers,
- *     followed by a system-scope fence; the GEMV and SIMPLE paths compute
- *     into dst[0] and copy it to the others on the stream.
+ * and the others', mapped with pfng_b200_ipc_open -- so that the matmul
+ * itself stores C into every rank's C over NVLink: the all-gather of C done
+ * by the call, with no collective and no reassembly pass.
+ *   - On the MMA path the GEMM writes dst[0] and a copy kernel after it
+ *     pushes C to the other destinations in 16-byte pieces over NVLink
+ *     (PFNG_B200_COPIES=epilogue: the GEMM's epilogue writes every
+ *     destination itself; measured slower), each followed by a system-scope
+ *     fence; the GEMV and SIMPLE paths compute into dst[0] and copy it to
+ *     the others on the stream.
  *   - The call does not wait for the other ranks.  Before a rank reads its C
  *     (or a next call writes into the others'), every rank's call must have
  *     completed: order the ranks with a barrier or collective on the stream
@@ -248,6 +250,11 @@ int pfng_b200_unshard_columns(const float *slices, float *c, int64_t m, int64_t 
 int pfng_b200_compute_gather(int wtype, const void *w, const float *x, int64_t ldx, float *const *dst, int ndst,
                              int64_t ldd, int64_t m, int64_t n, int64_t k, void *workspace, size_t workspace_bytes,
                              int path, void *stream);
+/* The same with activations already quantized (q8_0 / q8_K bytes, as
+ * pfng_b200_mm_*; workspace: pfng_b200_mm_workspace_size) -- e.g. broadcast
+ * to the ranks as q8_0, 1.06 bytes per value instead of fp32's 4. */
+int pfng_b200_mm_gather(int wtype, const void *w, const void *a, float *const *dst, int ndst, int64_t ldd, int64_t m,
+                        int64_t n, int64_t k, void *workspace, size_t workspace_bytes, int path, void *stream);
 
 /* Device buffers shared between the processes of a node (CUDA IPC): alloc
  * returns a cudaMalloc'd buffer of the current device and its 64-byte

@@ -646,19 +646,40 @@ int pfng_b200_unshard_columns(const float *slices, float *c, int64_t m, int64_t 
                                             static_cast<cudaStream_t>(stream)));
 }
 
+}  // extern "C"
+
+namespace {
+// The destination checks of the gather entry points.
+int check_destinations(float *const *dst, int ndst, int64_t m, int64_t n) {
+    static_assert(PFNG_B200_MAX_DESTINATIONS == kMaxCopies + 1, "destination count");
+    if (ndst < 1 || ndst > PFNG_B200_MAX_DESTINATIONS || !dst) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    if (m == 0 || n == 0) return PFNG_B200_OK;
+    for (int d = 0; d < ndst; ++d) {
+        if (!dst[d]) return PFNG_B200_ERR_INVALID_ARGUMENT;
+        if (!aligned(dst[d], 4)) return PFNG_B200_ERR_ALIGNMENT;
+    }
+    return PFNG_B200_OK;
+}
+}  // namespace
+
+extern "C" {
+
 int pfng_b200_compute_gather(int wtype, const void *w, const float *x, int64_t ldx, float *const *dst, int ndst,
                              int64_t ldd, int64_t m, int64_t n, int64_t k, void *workspace, size_t workspace_bytes,
                              int path, void *stream) {
-    if (ndst < 1 || ndst > PFNG_B200_MAX_DESTINATIONS || !dst) return PFNG_B200_ERR_INVALID_ARGUMENT;
-    if (m > 0 && n > 0) {
-        for (int d = 0; d < ndst; ++d) {
-            if (!dst[d]) return PFNG_B200_ERR_INVALID_ARGUMENT;
-            if (!aligned(dst[d], 4)) return PFNG_B200_ERR_ALIGNMENT;
-        }
-        if (!x && k > 0) return PFNG_B200_ERR_INVALID_ARGUMENT;
-    }
-    static_assert(PFNG_B200_MAX_DESTINATIONS == kMaxCopies + 1, "destination count");
+    const int st = check_destinations(dst, ndst, m, n);
+    if (st != PFNG_B200_OK) return st;
+    if (!x && m > 0 && n > 0 && k > 0) return PFNG_B200_ERR_INVALID_ARGUMENT;
     return run_matmul(wtype, w, nullptr, x, ldx, dst[0], ldd, nullptr, m, n, k, workspace, workspace_bytes, path,
+                      static_cast<cudaStream_t>(stream), dst + 1, ndst - 1);
+}
+
+int pfng_b200_mm_gather(int wtype, const void *w, const void *a, float *const *dst, int ndst, int64_t ldd, int64_t m,
+                        int64_t n, int64_t k, void *workspace, size_t workspace_bytes, int path, void *stream) {
+    const int st = check_destinations(dst, ndst, m, n);
+    if (st != PFNG_B200_OK) return st;
+    if (!a && m > 0 && n > 0 && k > 0) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    return run_matmul(wtype, w, a, nullptr, 0, dst[0], ldd, nullptr, m, n, k, workspace, workspace_bytes, path,
                       static_cast<cudaStream_t>(stream), dst + 1, ndst - 1);
 }
 

@@ -1156,11 +1156,15 @@ __global__ void __launch_bounds__(kThreads) push_copies_kernel(const GemmParams 
     __threadfence_system();
 }
 
-// How the copies are written: in the GEMM's epilogue (default) or by
-// push_copies_kernel after it (PFNG_B200_COPIES=push).
+// How the copies are written: by push_copies_kernel after the GEMM (default)
+// or in the GEMM's epilogue (PFNG_B200_COPIES=epilogue).  Measured on two
+// B200s (us per step of the row-sharded configs[4] shapes at m = 2048,
+// push vs epilogue): 271 vs 278, 496 vs 515, 587 vs 598, 1172 vs 1224.  The
+// 128 x 128 GEMM runs one CTA per SM, so nothing hides the epilogue's copy
+// of its tile, while the push kernel streams C at copy bandwidth.
 inline bool push_copies() {
     const char *e = std::getenv("PFNG_B200_COPIES");
-    return e && std::strcmp(e, "push") == 0;
+    return !(e && std::strcmp(e, "epilogue") == 0);
 }
 
 template <int WT, bool kPartials>

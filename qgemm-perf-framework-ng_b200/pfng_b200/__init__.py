@@ -114,6 +114,8 @@ def _declare(L: ctypes.CDLL) -> None:
     L.pfng_b200_unshard_columns.argtypes = [P, P, I64, I64, I64, I, I64, I64, P]
     L.pfng_b200_compute_gather.restype = I
     L.pfng_b200_compute_gather.argtypes = [I, P, P, I64, ctypes.POINTER(P), I, I64, I64, I64, I64, P, S, I, P]
+    L.pfng_b200_mm_gather.restype = I
+    L.pfng_b200_mm_gather.argtypes = [I, P, P, ctypes.POINTER(P), I, I64, I64, I64, I64, P, S, I, P]
     L.pfng_b200_ipc_alloc.restype = I
     L.pfng_b200_ipc_alloc.argtypes = [S, ctypes.POINTER(P), P]
     L.pfng_b200_ipc_open.restype = I
@@ -390,6 +392,18 @@ def compute_gather(wtype, w, x, n: int, destinations, ldd: int, path="auto", wor
     nbytes = 0 if ws is None else ws.numel()
     _check(lib().pfng_b200_compute_gather(wt, _ptr(w), _ptr(x), x.stride(0), arr, len(ptrs), ldd, m, n, k,
                                           _ptr(ws), nbytes, p, _stream(stream)), "compute_gather")
+
+
+def mm_gather(wtype, w, a, m: int, n: int, k: int, destinations, ldd: int, path="auto", workspace=None,
+              stream=None) -> None:
+    """compute_gather with pre-quantized activations `a` (q8_0 or q8_K bytes, as mm())."""
+    wt, p = _wt(wtype), _path(path)
+    ptrs = [d if isinstance(d, int) else d.data_ptr() for d in destinations]
+    arr = (ctypes.c_void_p * max(1, len(ptrs)))(*ptrs)
+    ws = _workspace(mm_workspace_size(wt, m, n, k, p), a.device, workspace)
+    nbytes = 0 if ws is None else ws.numel()
+    _check(lib().pfng_b200_mm_gather(wt, _ptr(w), _ptr(a), arr, len(ptrs), ldd, m, n, k, _ptr(ws), nbytes, p,
+                                     _stream(stream)), "mm_gather")
 
 
 def ipc_alloc(nbytes: int) -> tuple[int, bytes]:

@@ -2,8 +2,9 @@
 
 * One process: every destination must hold exactly what pfng_b200_compute_*
   writes for the same arguments (bit for bit, on every path, with split-K
-  and ragged shapes, copies written by the GEMM epilogue or by the push
-  kernel), and nothing outside the [m][n] window of its rows.
+  and ragged shapes, copies written by the push kernel or by the GEMM
+  epilogue), and nothing outside the [m][n] window of its rows; the
+  pre-quantized entry (mm_gather) likewise equals mm().
 * Two processes through CUDA IPC (GatheredC): each rank computes the columns
   of its weight rows into every rank's full C; after a host barrier every
   rank's C holds each rank's slice exactly as compute() gives it.  On a box
@@ -18,7 +19,7 @@ import pytest
 pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 import pfng_b200 as pb  # noqa: E402
-from test_gpu_parity import dev, dev_bytes, host, make_weights  # noqa: E402
+from test_gpu_parity import act_kind, dev, dev_bytes, host, make_weights  # noqa: E402
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -38,13 +39,14 @@ CASES = [
 ]
 
 
-@pytest.mark.parametrize("mode", ["epilogue", "push"])
+@pytest.mark.parametrize("mode", ["push", "epilogue"])
 @pytest.mark.parametrize("ndst", [1, 3, 8])
 @pytest.mark.parametrize("wtype,path,m,n,k", CASES)
 def test_every_destination_equals_compute(oracle, monkeypatch, wtype, path, m, n, k, ndst, mode):
-    # mode: copies written by the GEMM's epilogue or by the push kernel after it
-    if mode == "push":
-        monkeypatch.setenv("PFNG_B200_COPIES", "push")
+    # mode: copies written by the push kernel after the GEMM (default) or by
+    # the GEMM's epilogue
+    if mode == "epilogue":
+        monkeypatch.setenv("PFNG_B200_COPIES", "epilogue")
     rng = np.random.default_rng(m * 7 + n + k + ndst)
     base = "q4_0" if wtype == "q4_0_planar" else wtype
     wd = dev_bytes(make_weights(oracle, base, n, k, rng))
@@ -59,6 +61,21 @@ def test_every_destination_equals_compute(oracle, monkeypatch, wtype, path, m, n
         for d in range(ndst):
             assert got[d, :, :n].tobytes() == ref.tobytes(), f"{wtype}/{path}/{m}x{n}x{k} destination {d}"
             assert np.all(got[d, :, n:] == -7.0)
+
+
+@pytest.mark.parametrize("wtype,path,m,n,k", [c for c in CASES if c[1] != "simple"])
+def test_mm_gather_equals_mm(oracle, wtype, path, m, n, k):
+    rng = np.random.default_rng(m + 3 * n + k)
+    base = "q4_0" if wtype == "q4_0_planar" else wtype
+    wd = dev_bytes(make_weights(oracle, base, n, k, rng))
+    if wtype == "q4_0_planar":
+        wd = pb.pack_q4_0_planar(wd, n, k)
+    a = dev_bytes(oracle.quantize(act_kind(base), rng.standard_normal((m, k)).astype(np.float32)))
+    ref = host(pb.mm(wtype, wd, a, m, n, k, path=path))
+    outs = [torch.full((m, n), -7.0, device="cuda") for _ in range(3)]
+    pb.mm_gather(wtype, wd, a, m, n, k, outs, n, path=path)
+    for o in outs:
+        assert host(o).tobytes() == ref.tobytes(), f"{wtype}/{path}/{m}x{n}x{k}"
 
 
 def test_zero_k_and_empty_shapes():
