@@ -56,10 +56,11 @@ constexpr bool kQ8_0Act = WT == kWQ4_0 || WT == kWQ4_0P;
 constexpr uint32_t kWRowSlot = 160;          // >= 144 raw bytes + 8 window slack, multiple of 16
 constexpr int kAScaleStride = 12;
 
-template <int BM_, int BN_, int ST_ = kStages>
+template <int BM_, int BN_, int ST_ = kStages, uint32_t SLOT_ = kWRowSlot>
 struct Cfg {
     static constexpr int BM = BM_, BN = BN_;
     static constexpr int ST = ST_;  // cp.async ring depth of the two-phase kernel
+    static constexpr uint32_t kSlot = SLOT_;  // bytes per raw W row in shared memory
     static constexpr int WM = BM / 2, WN = BN / 4;  // warp tile
     static constexpr int MT = WM / 16, NT = WN / 8;  // m16n8 fragments per warp
     static_assert(MT >= 1 && NT >= 2 && NT % 2 == 0, "tile shape");
@@ -69,7 +70,7 @@ struct Cfg {
     // kAScaleStride words apart so that 8 consecutive rows hit 8 distinct banks.
     static constexpr uint32_t kAScale = BM * kAScaleStride * 4;
     static constexpr uint32_t kAD8K = BM * 4;        // q8_K: d per row
-    static constexpr uint32_t kWRaw = BN * kWRowSlot;
+    static constexpr uint32_t kWRaw = BN * kSlot;
     static constexpr uint32_t kStage = kAQs + kAScale + kAD8K + kWRaw;
     static constexpr uint32_t kBTile = BN * BK;
     static constexpr uint32_t kFold = 8 * BN * 8;    // float2 (s, -M s) per (sub-block, column)
@@ -188,7 +189,7 @@ PFNG_DEV void load_a(const GemmParams &p, int8_t *a_qs, float *a_scale, float *a
 }
 
 // cp.async copies of k-step `ks` of the raw W tile: BN rows x step_bytes,
-// each row into a kWRowSlot-byte slot of `wr`.
+// each row into a C::kSlot-byte slot of `wr`.
 template <int WT, class C>
 PFNG_DEV void load_w(const GemmParams &p, uint8_t *wr, int64_t ks, int64_t n0, int tid) {
     const int64_t K = p.k;
@@ -201,7 +202,7 @@ PFNG_DEV void load_w(const GemmParams &p, uint8_t *wr, int64_t ks, int64_t n0, i
             const bool ok = n < p.n;
             const int64_t off = ch < 8 ? ks * 128 + ch * 16 : K / 2 + ks * 16;
             const uint8_t *src = p.w + (ok ? n * p.row_bytes + off : 0);
-            cp_async16(wr + row * kWRowSlot + ch * 16, src, ok ? 16u : 0u);
+            cp_async16(wr + row * C::kSlot + ch * 16, src, ok ? 16u : 0u);
         }
     } else if (p.w_vec16) {
         // 16-byte chunks per row and k-step: the raw bytes of 256 values
@@ -211,7 +212,7 @@ PFNG_DEV void load_w(const GemmParams &p, uint8_t *wr, int64_t ks, int64_t n0, i
             const int64_t n = n0 + row;
             const bool ok = n < p.n;
             const uint8_t *src = p.w + (ok ? n * p.row_bytes + ks * p.step_bytes + ch * 16 : 0);
-            cp_async16(wr + row * kWRowSlot + ch * 16, src, ok ? 16u : 0u);
+            cp_async16(wr + row * C::kSlot + ch * 16, src, ok ? 16u : 0u);
         }
     } else {
         // word-granular window [start & ~3, start + step_bytes + 3) per row
@@ -224,7 +225,7 @@ PFNG_DEV void load_w(const GemmParams &p, uint8_t *wr, int64_t ks, int64_t n0, i
             const int64_t addr = (start & ~int64_t(3)) + 4 * wd;
             uint32_t bytes = 0;
             if (n < p.n && addr < p.w_total) bytes = p.w_total - addr >= 4 ? 4u : static_cast<uint32_t>(p.w_total - addr);
-            cp_async4(wr + row * kWRowSlot + 4 * wd, p.w + (bytes ? addr : 0), bytes);
+            cp_async4(wr + row * C::kSlot + 4 * wd, p.w + (bytes ? addr : 0), bytes);
         }
     }
 }
@@ -374,6 +375,7 @@ PFNG_DEV uint4 pack_bsum(const int32_t *bsum) {
 // per-(sub-block, column) fold data.  Runs once per CTA per k-step.
 template <int WT, class C>
 PFNG_DEV void decode_w(const GemmParams &p, const Smem<C> &sm, int s, int64_t ks, int64_t n0, int tid) {
+    static_assert(C::kSlot == kWRowSlot, "decode_task reads kWRowSlot-byte rows");
     const uint8_t *wr = sm.w_raw(s);
     int8_t *bt = sm.b_tile();
     float *fold = reinterpret_cast<float *>(sm.fold());
@@ -426,6 +428,40 @@ PFNG_DEV void load_frags_o(uint32_t at_s, uint32_t bt_s, int kb, const FragOff<C
 #pragma unroll
     for (int np = 0; np < C::NT / 2; ++np)
         ldmatrix_x4_s(bf[2 * np][0], bf[2 * np][1], bf[2 * np + 1][0], bf[2 * np + 1][1], bt_s + (fo.b[np] ^ x));
+}
+
+// Direct operands of 32-row tiles for q4_0 in either layout (kDirect): the
+// m16n8k32 B fragment of thread (g, t4) holds column g's values
+// k = 4 t4 .. 4 t4 + 3 and 16 + 4 t4 .. 16 + 4 t4 + 3 of the sub-block,
+// which in a q4_0 block are the low and high nibbles of qs[4 t4 .. 4 t4 + 3]:
+// one 32-bit word of the raw W tile gives both registers, with no B tile,
+// no decode pass and no barrier between them.  Rows of the raw tile start
+// 16-byte aligned (w_vec16 or planar), a ggml block's qs at 18 kb + 2.
+template <int WT>
+PFNG_DEV uint32_t raw_q4_word(const uint8_t *row, int kb, int t4) {
+    if constexpr (WT == kWQ4_0P) {
+        return *reinterpret_cast<const uint32_t *>(row + 16 * kb + 4 * t4);
+    } else {
+        const uint16_t *h = reinterpret_cast<const uint16_t *>(row + 18 * kb + 2 + 4 * t4);
+        return static_cast<uint32_t>(h[0]) | (static_cast<uint32_t>(h[1]) << 16);
+    }
+}
+template <int WT>
+PFNG_DEV uint32_t raw_q4_scale(const uint8_t *row, int kb) {
+    return *reinterpret_cast<const uint16_t *>(row + (WT == kWQ4_0P ? 128 + 2 * kb : 18 * kb));
+}
+template <int WT, class C>
+PFNG_DEV void load_frags_direct(uint32_t at_s, const uint8_t *wr, int kb, const FragOff<C> &fo, int wn, int g, int t4,
+                                uint32_t (&af)[C::MT][4], uint32_t (&bf)[C::NT][2]) {
+    const uint32_t x = static_cast<uint32_t>(kb) * 32u;
+#pragma unroll
+    for (int mt = 0; mt < C::MT; ++mt) ldmatrix_x4_s(af[mt][0], af[mt][1], af[mt][2], af[mt][3], at_s + (fo.a[mt] ^ x));
+#pragma unroll
+    for (int nt = 0; nt < C::NT; ++nt) {
+        const uint32_t q = raw_q4_word<WT>(wr + (wn * C::WN + nt * 8 + g) * C::kSlot, kb, t4);
+        bf[nt][0] = ((q & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+        bf[nt][1] = (((q >> 4) & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+    }
 }
 
 template <class C>
@@ -495,8 +531,9 @@ PFNG_DEV void copy_tile_to_copies(const GemmParams &p) {
     __threadfence_system();
 }
 
-template <int WT, class C, bool kPartials, bool kCopies = false>
+template <int WT, class C, bool kPartials, bool kCopies = false, bool kDirect = false>
 __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
+    static_assert(!kDirect || ((WT == kWQ4_0 || WT == kWQ4_0P) && !kPartials), "direct operands: q4_0 products");
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Smem<C> sm{smem_raw};
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -556,11 +593,11 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
         const int s = static_cast<int>((ks - k0) % ST);
         cp_async_wait<ST - 2>();
         __syncthreads();
-        decode_w<WT, C>(p, sm, s, ks, n0, tid);
+        if constexpr (!kDirect) decode_w<WT, C>(p, sm, s, ks, n0, tid);
         if (ks + ST - 1 < k1)
             load_stage<WT, C>(p, sm, static_cast<int>((ks - k0 + ST - 1) % ST), ks + ST - 1, m0, n0, tid);
         cp_async_commit();
-        __syncthreads();
+        if constexpr (!kDirect) __syncthreads();
 
         const int8_t *at = sm.a_qs(s);
         const int8_t *bt = sm.b_tile();
@@ -601,12 +638,19 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
             uint32_t af[2][MT][4], bf[2][NT][2];
             int res[MT][NT][4];
             const uint32_t at_s = smem_u32(at), bt_s = smem_u32(bt);
-            load_frags_o<C>(at_s, bt_s, 0, fo, af[0], bf[0]);
+            const uint8_t *wr = sm.w_raw(s);
+            auto frags = [&](int kb, uint32_t(&a)[MT][4], uint32_t(&b)[NT][2]) {
+                if constexpr (kDirect)
+                    load_frags_direct<WT, C>(at_s, wr, kb, fo, wn, g, t4, a, b);
+                else
+                    load_frags_o<C>(at_s, bt_s, kb, fo, a, b);
+            };
+            frags(0, af[0], bf[0]);
 #pragma unroll
             for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) mma_s8(res[mt][nt], af[0][mt], bf[0][nt][0], bf[0][nt][1], cin);
-            load_frags_o<C>(at_s, bt_s, 1, fo, af[1], bf[1]);
+            frags(1, af[1], bf[1]);
 #pragma unroll
             for (int kb = 0; kb < 8; ++kb) {
                 const int nx = (kb + 1) & 1;
@@ -620,8 +664,18 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
                 const float2 *fold = sm.fold() + kb * C::BN;
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
-                    const float4 f = *reinterpret_cast<const float4 *>(fold + wn * C::WN + nt * 8 + 2 * t4);
-                    const float2 sv = make_float2(f.x, f.y), cm = make_float2(f.z, f.w);
+                    float2 sv, cm;
+                    if constexpr (kDirect) {
+                        // the fold constants of columns 2 t4, 2 t4 + 1 from the raw tile (store_fold's values)
+                        const uint8_t *row = wr + (wn * C::WN + nt * 8 + 2 * t4) * C::kSlot;
+                        sv = make_float2(f16_bits_to_f32(raw_q4_scale<WT>(row, kb)),
+                                         f16_bits_to_f32(raw_q4_scale<WT>(row + C::kSlot, kb)));
+                        cm = make_float2(-kMagic * sv.x, -kMagic * sv.y);
+                    } else {
+                        const float4 f = *reinterpret_cast<const float4 *>(fold + wn * C::WN + nt * 8 + 2 * t4);
+                        sv = make_float2(f.x, f.y);
+                        cm = make_float2(f.z, f.w);
+                    }
 #pragma unroll
                     for (int mt = 0; mt < MT; ++mt) {
 #pragma unroll
@@ -634,7 +688,7 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
                         if (kb + 1 < 8) mma_s8(res[mt][nt], af[nx][mt], bf[nx][nt][0], bf[nx][nt][1], cin);
                     }
                 }
-                if (kb + 2 < 8) load_frags_o<C>(at_s, bt_s, kb + 2, fo, af[kb & 1], bf[kb & 1]);
+                if (kb + 2 < 8) frags(kb + 2, af[kb & 1], bf[kb & 1]);
             }
         }
 
@@ -745,6 +799,7 @@ struct SmemOv {
 template <int WT, class C, bool kCopies = false>
 __global__ void __launch_bounds__(kThreads) gemm_kernel_ov(const GemmParams p) {
     static_assert(WT != kWQ4_K, "q4_K products run on the two-phase kernel");
+    static_assert(C::kSlot == kWRowSlot, "decode_task reads kWRowSlot-byte rows");
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const SmemOv<C> sm{smem_raw};
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1012,18 +1067,20 @@ cudaError_t launch_pdl(K kernel, const GemmParams &p, uint32_t smem, cudaStream_
     return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
-template <int WT, class C, bool kPartials, bool kCopies = false>
+template <int WT, class C, bool kPartials, bool kCopies = false, bool kDirect = false>
 cudaError_t launch_t(const GemmParams &p, cudaStream_t s) {
-    auto kernel = gemm_kernel<WT, C, kPartials, kCopies>;
+    auto kernel = gemm_kernel<WT, C, kPartials, kCopies, kDirect>;
+    // direct operands use the stage ring only (no B tile, fold data or tables)
+    constexpr uint32_t smem = kDirect ? C::ST * C::kStage : C::kSmem;
     static thread_local bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64 || !configured[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::kSmem));
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) configured[dev] = true;
     }
-    return launch_pdl<C>(kernel, p, C::kSmem, s);
+    return launch_pdl<C>(kernel, p, smem, s);
 }
 
 template <int WT, class C, bool kCopies = false>
@@ -1052,6 +1109,16 @@ cudaError_t launch_t_ov(const GemmParams &p, cudaStream_t s) {
 // slower there: 2048x4096x4096 353 vs 338, 512x4096x4096 90.0 vs 85.9.
 template <int WT, bool kPartials>
 constexpr bool kOvType = !kPartials && WT != kWQ4_K;
+// Direct operands for 32-row q4_0 tiles; PFNG_B200_GEMM_DIRECT=0 selects the
+// decode pass instead (comparisons).  Measured on B200 (us per quantize +
+// GEMM step, direct vs decode pass): 32x4096x4096 14.4 vs 15.7, 32x11008x4096
+// 26.0 vs 29.2, 32x4096x11008 28.4 vs 31.5, 32x32000x4096 54.4 vs 63.1.  A
+// deeper ring, which the smaller shared-memory footprint would allow, was
+// slower (32x32000x4096: 3 stages 56.6, 4 stages 66.3 us).
+inline bool direct_enabled() {
+    const char *e = std::getenv("PFNG_B200_GEMM_DIRECT");
+    return !(e && std::strcmp(e, "0") == 0);
+}
 inline bool ov_enabled() {
     const char *e = std::getenv("PFNG_B200_GEMM_OV");
     return !(e && std::strcmp(e, "0") == 0);
@@ -1069,6 +1136,14 @@ cudaError_t launch_pick(const GemmParams &p, cudaStream_t s) {
             return copies ? launch_t_ov<WT, C, true>(p, s) : launch_t_ov<WT, C>(p, s);
     }
     if constexpr (!kPartials) {
+        if constexpr (C::BM == 32 && (WT == kWQ4_0 || WT == kWQ4_0P)) {
+            // 176-byte row slots (44 words): the eight rows of a fragment read
+            // start on banks 12 r mod 32, so with the four t4 words they hit
+            // all 32 banks (160-byte slots: rows r and r + 4 collide)
+            using D = Cfg<C::BM, C::BN, C::ST, 176>;
+            if ((WT == kWQ4_0P || p.w_vec16) && direct_enabled())
+                return copies ? launch_t<WT, D, false, true, true>(p, s) : launch_t<WT, D, false, false, true>(p, s);
+        }
         if (copies) return launch_t<WT, C, false, true>(p, s);
     }
     return launch_t<WT, C, kPartials>(p, s);
