@@ -376,3 +376,28 @@ def test_split_k_small_m(oracle, monkeypatch, m, n, k):
     monkeypatch.setenv("PFNG_B200_GEMM_SPLITS", "1")
     c1 = host(pb.compute("q4_0", wd, xd, n, path="mma"))
     check_close(c1, oracle.mm("q4_0", w, a, m, n, k), oracle.bound("q4_0", w, a, m, n, k), f"unsplit {m}x{n}x{k}")
+
+
+@pytest.mark.parametrize("layout", ["ggml", "planar"])
+@pytest.mark.parametrize("m,n,k,splits", [(32, 1024, 4096, None), (32, 4000, 2048, "1"), (9, 300, 1536, "1"),
+                                          (17, 640, 4096, None), (32, 130, 256, "1")])
+def test_direct_operands_equal_decode_pass(oracle, monkeypatch, layout, m, n, k, splits):
+    # 32-row q4_0 tiles build the B fragments straight from the raw W tile;
+    # PFNG_B200_GEMM_DIRECT=0 runs the decode pass into the B tile.  Same
+    # products, same fold constants, same order: the same bits, and both
+    # within tolerance of the oracle.
+    if splits:
+        monkeypatch.setenv("PFNG_B200_GEMM_SPLITS", splits)
+    rng = np.random.default_rng(m * 5 + n + k)
+    w = oracle.quantize("q4_0", rng.standard_normal((n, k)).astype(np.float32))
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    a = oracle.quantize("q8_0", x)
+    wd, xd = dev_bytes(w), dev(x)
+    wt = "q4_0"
+    if layout == "planar":
+        wd, wt = pb.pack_q4_0_planar(wd, n, k), "q4_0_planar"
+    c = host(pb.compute(wt, wd, xd, n, path="mma"))
+    check_close(c, oracle.mm("q4_0", w, a, m, n, k), oracle.bound("q4_0", w, a, m, n, k), f"direct {m}x{n}x{k}")
+    monkeypatch.setenv("PFNG_B200_GEMM_DIRECT", "0")
+    c0 = host(pb.compute(wt, wd, xd, n, path="mma"))
+    np.testing.assert_array_equal(c.view(np.uint32), c0.view(np.uint32))
