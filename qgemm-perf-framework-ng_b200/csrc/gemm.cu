@@ -430,7 +430,7 @@ PFNG_DEV void load_frags_o(uint32_t at_s, uint32_t bt_s, int kb, const FragOff<C
         ldmatrix_x4_s(bf[2 * np][0], bf[2 * np][1], bf[2 * np + 1][0], bf[2 * np + 1][1], bt_s + (fo.b[np] ^ x));
 }
 
-// Direct operands of 32-row tiles for q4_0 in either layout (kDirect): the
+// Direct operands of 32- and 64-row tiles for q4_0 in either layout (kDirect): the
 // m16n8k32 B fragment of thread (g, t4) holds column g's values
 // k = 4 t4 .. 4 t4 + 3 and 16 + 4 t4 .. 16 + 4 t4 + 3 of the sub-block,
 // which in a q4_0 block are the low and high nibbles of qs[4 t4 .. 4 t4 + 3]:
@@ -532,7 +532,7 @@ PFNG_DEV void copy_tile_to_copies(const GemmParams &p) {
 }
 
 template <int WT, class C, bool kPartials, bool kCopies = false, bool kDirect = false>
-__global__ void __launch_bounds__(kThreads) gemm_kernel(const GemmParams p) {
+__global__ void __launch_bounds__(kThreads, kDirect && C::BM == 64 ? 2 : 1) gemm_kernel(const GemmParams p) {
     static_assert(!kDirect || ((WT == kWQ4_0 || WT == kWQ4_0P) && !kPartials), "direct operands: q4_0 products");
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Smem<C> sm{smem_raw};
@@ -1109,12 +1109,17 @@ cudaError_t launch_t_ov(const GemmParams &p, cudaStream_t s) {
 // slower there: 2048x4096x4096 353 vs 338, 512x4096x4096 90.0 vs 85.9.
 template <int WT, bool kPartials>
 constexpr bool kOvType = !kPartials && WT != kWQ4_K;
-// Direct operands for 32-row q4_0 tiles; PFNG_B200_GEMM_DIRECT=0 selects the
-// decode pass instead (comparisons).  Measured on B200 (us per quantize +
-// GEMM step, direct vs decode pass): 32x4096x4096 14.4 vs 15.7, 32x11008x4096
-// 26.0 vs 29.2, 32x4096x11008 28.4 vs 31.5, 32x32000x4096 54.4 vs 63.1.  A
-// deeper ring, which the smaller shared-memory footprint would allow, was
-// slower (32x32000x4096: 3 stages 56.6, 4 stages 66.3 us).
+// Direct operands for 32- and 64-row q4_0 tiles (both layouts);
+// PFNG_B200_GEMM_DIRECT=0 selects the decode pass instead (comparisons).
+// Measured on B200 (us per quantize + GEMM step, direct vs decode pass):
+// 32x4096x4096 14.4 vs 15.7, 32x11008x4096 26.0 vs 29.2, 32x4096x11008 28.4
+// vs 31.5, 32x32000x4096 54.4 vs 63.1; on 64-row tiles (vs the overlapped or
+// split two-phase kernel) 480x1536x1536 18.5 vs 20.1, 256x4096x4096 41.8 vs
+// 45.5, 128x4096x4096 25.1 vs 28.8, 64x11008x4096 40.9 vs 44.7.  A deeper
+// ring, which the smaller shared-memory footprint would allow, was slower
+// (32x32000x4096: 3 stages 56.6, 4 stages 66.3 us), and so were three
+// 32-row CTAs per SM at 80 registers (78.7 us).  64-row direct kernels are
+// bounded to two CTAs per SM (<= 128 registers, no spills).
 inline bool direct_enabled() {
     const char *e = std::getenv("PFNG_B200_GEMM_DIRECT");
     return !(e && std::strcmp(e, "0") == 0);
@@ -1131,19 +1136,19 @@ cudaError_t launch_pick(const GemmParams &p, cudaStream_t s) {
     // copies (fp32 C to more destinations): the kernels built with the copy
     // pass; with split-K the reduction stores the copies
     const bool copies = p.ncopies > 0 && p.splits == 1;
+    if constexpr (!kPartials && C::BM <= 64 && (WT == kWQ4_0 || WT == kWQ4_0P)) {
+        // 176-byte row slots (44 words): the eight rows of a fragment read
+        // start on banks 12 r mod 32, so with the four t4 words they hit
+        // all 32 banks (160-byte slots: rows r and r + 4 collide)
+        using D = Cfg<C::BM, C::BN, C::ST, 176>;
+        if ((WT == kWQ4_0P || p.w_vec16) && direct_enabled())
+            return copies ? launch_t<WT, D, false, true, true>(p, s) : launch_t<WT, D, false, false, true>(p, s);
+    }
     if constexpr (kOvType<WT, kPartials> && C::BM > 32) {
         if (p.splits == 1 && ov_enabled())
             return copies ? launch_t_ov<WT, C, true>(p, s) : launch_t_ov<WT, C>(p, s);
     }
     if constexpr (!kPartials) {
-        if constexpr (C::BM == 32 && (WT == kWQ4_0 || WT == kWQ4_0P)) {
-            // 176-byte row slots (44 words): the eight rows of a fragment read
-            // start on banks 12 r mod 32, so with the four t4 words they hit
-            // all 32 banks (160-byte slots: rows r and r + 4 collide)
-            using D = Cfg<C::BM, C::BN, C::ST, 176>;
-            if ((WT == kWQ4_0P || p.w_vec16) && direct_enabled())
-                return copies ? launch_t<WT, D, false, true, true>(p, s) : launch_t<WT, D, false, false, true>(p, s);
-        }
         if (copies) return launch_t<WT, C, false, true>(p, s);
     }
     return launch_t<WT, C, kPartials>(p, s);
