@@ -430,7 +430,7 @@ PFNG_DEV void load_frags_o(uint32_t at_s, uint32_t bt_s, int kb, const FragOff<C
         ldmatrix_x4_s(bf[2 * np][0], bf[2 * np][1], bf[2 * np + 1][0], bf[2 * np + 1][1], bt_s + (fo.b[np] ^ x));
 }
 
-// Direct operands of 32- and 64-row tiles for q4_0 in either layout (kDirect): the
+// Direct operands for q4_0 in either layout (kDirect): the
 // m16n8k32 B fragment of thread (g, t4) holds column g's values
 // k = 4 t4 .. 4 t4 + 3 and 16 + 4 t4 .. 16 + 4 t4 + 3 of the sub-block,
 // which in a q4_0 block are the low and high nibbles of qs[4 t4 .. 4 t4 + 3]:
@@ -1109,7 +1109,7 @@ cudaError_t launch_t_ov(const GemmParams &p, cudaStream_t s) {
 // slower there: 2048x4096x4096 353 vs 338, 512x4096x4096 90.0 vs 85.9.
 template <int WT, bool kPartials>
 constexpr bool kOvType = !kPartials && WT != kWQ4_K;
-// Direct operands for 32- and 64-row q4_0 tiles (both layouts);
+// Direct operands for every q4_0 tile (both layouts, 16-byte aligned rows);
 // PFNG_B200_GEMM_DIRECT=0 selects the decode pass instead (comparisons).
 // Measured on B200 (us per quantize + GEMM step, direct vs decode pass):
 // 32x4096x4096 14.4 vs 15.7, 32x11008x4096 26.0 vs 29.2, 32x4096x11008 28.4
@@ -1119,7 +1119,10 @@ constexpr bool kOvType = !kPartials && WT != kWQ4_K;
 // ring, which the smaller shared-memory footprint would allow, was slower
 // (32x32000x4096: 3 stages 56.6, 4 stages 66.3 us), and so were three
 // 32-row CTAs per SM at 80 registers (78.7 us).  64-row direct kernels are
-// bounded to two CTAs per SM (<= 128 registers, no spills).
+// bounded to two CTAs per SM (<= 128 registers, no spills).  On 128 x 128
+// tiles the direct two-phase kernel also beats the overlapped decode:
+// 2048x11008x4096 589.6 vs 622.7, 2048x4096x4096 242.4 vs 255.4,
+// 512x4096x4096 62.4 vs 65.5, 2048x4096x11008 629.8 vs 661.5.
 inline bool direct_enabled() {
     const char *e = std::getenv("PFNG_B200_GEMM_DIRECT");
     return !(e && std::strcmp(e, "0") == 0);
@@ -1136,7 +1139,7 @@ cudaError_t launch_pick(const GemmParams &p, cudaStream_t s) {
     // copies (fp32 C to more destinations): the kernels built with the copy
     // pass; with split-K the reduction stores the copies
     const bool copies = p.ncopies > 0 && p.splits == 1;
-    if constexpr (!kPartials && C::BM <= 64 && (WT == kWQ4_0 || WT == kWQ4_0P)) {
+    if constexpr (!kPartials && (WT == kWQ4_0 || WT == kWQ4_0P)) {
         // 176-byte row slots (44 words): the eight rows of a fragment read
         // start on banks 12 r mod 32, so with the four t4 words they hit
         // all 32 banks (160-byte slots: rows r and r + 4 collide)

@@ -381,10 +381,12 @@ def test_split_k_small_m(oracle, monkeypatch, m, n, k):
 @pytest.mark.parametrize("layout", ["ggml", "planar"])
 @pytest.mark.parametrize("m,n,k,splits", [(32, 1024, 4096, None), (32, 4000, 2048, "1"), (9, 300, 1536, "1"),
                                           (17, 640, 4096, None), (32, 130, 256, "1"), (40, 1000, 1536, None),
-                                          (64, 2048, 4096, None), (130, 700, 2048, "1"), (480, 1536, 1536, None)])
+                                          (64, 2048, 4096, None), (130, 700, 2048, "1"), (480, 1536, 1536, None),
+                                          (2048, 2048, 512, None), (1100, 3000, 1024, None)])
 def test_direct_operands_equal_decode_pass(oracle, monkeypatch, layout, m, n, k, splits):
-    # 32- and 64-row q4_0 tiles build the B fragments straight from the raw
-    # W tile; PFNG_B200_GEMM_DIRECT=0 runs the decode pass into the B tile.  Same
+    # q4_0 tiles (32, 64 and 128 rows) build the B fragments straight from
+    # the raw W tile; PFNG_B200_GEMM_DIRECT=0 runs the decode pass into the
+    # B tile (the two-phase or the overlapped kernel).  Same
     # products, same fold constants, same order: the same bits, and both
     # within tolerance of the oracle.
     if splits:
