@@ -53,6 +53,7 @@ constexpr float kMagic = 12582912.0f;
 // true when the activations are q8_0 (one fp32 scale per 32 values)
 template <int WT>
 constexpr bool kQ8_0Act = WT == kWQ4_0 || WT == kWQ4_0P;
+constexpr uint32_t kMaxSmemPerCta = 227 * 1024;  // opt-in dynamic shared memory per CTA on sm_100
 constexpr uint32_t kWRowSlot = 160;          // >= 144 raw bytes + 8 window slack, multiple of 16
 constexpr int kAScaleStride = 12;
 
@@ -265,12 +266,15 @@ PFNG_DEV void store_fold(float *fold, int bn, int u, int col, float sv) {
 // tile `wr` into the int8 B tile and the fold constants.  q4_K tasks with
 // u == 0 also write the row's (dmin, -M dmin) pair and packed 6-bit mins to
 // mins_d / mins_pk; no type's decode reads the activations.
-template <int WT, int BN>
+// kTile = false (q4_K with direct operands): only the fold constants and
+// the mins, no B tile.  kSlot: bytes per raw W row.
+template <int WT, int BN, bool kTile = true, uint32_t kSlot = kWRowSlot>
 PFNG_DEV void decode_task(const GemmParams &p, const uint8_t *wr, int8_t *bt, float *fold, const uint2 *grid,
                           int64_t ks, int64_t n0, int task, float *mins_d = nullptr, uint2 *mins_pk = nullptr) {
+    static_assert(kTile || WT == kWQ4_K, "scales-only decode: q4_K");
     const int row = task >> 3, u = task & 7;
     const uint32_t mis = p.w_vec16 ? 0u : static_cast<uint32_t>((n0 + row) * p.row_bytes + ks * p.step_bytes) & 3u;
-    const uint32_t base = row * kWRowSlot + mis;
+    const uint32_t base = row * kSlot + mis;
     if constexpr (WT == kWQ4_0 || WT == kWQ4_0P) {
         uint32_t q[4], dbits;
         if constexpr (WT == kWQ4_0) {
@@ -296,14 +300,16 @@ PFNG_DEV void decode_task(const GemmParams &p, const uint8_t *wr, int8_t *bt, fl
     } else if constexpr (WT == kWQ4_K) {
         // u = (nibble pair pr, half h): 16 payload bytes -> 16 values of sub-blocks 2pr and 2pr+1
         const uint8_t *blk = wr + base;
-        const int pr = u >> 1, h = u & 1;
-        const uint4 v = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * pr + 16 * h);
-        uint4 lo, hi;
-        lo.x = v.x & 0x0f0f0f0fu, lo.y = v.y & 0x0f0f0f0fu, lo.z = v.z & 0x0f0f0f0fu, lo.w = v.w & 0x0f0f0f0fu;
-        hi.x = (v.x >> 4) & 0x0f0f0f0fu, hi.y = (v.y >> 4) & 0x0f0f0f0fu;
-        hi.z = (v.z >> 4) & 0x0f0f0f0fu, hi.w = (v.w >> 4) & 0x0f0f0f0fu;
-        // sub-block 2pr holds k = 64 pr + j, sub-block 2pr + 1 holds k = 64 pr + 32 + j
-        store_pair(bt, row, 4 * pr + h, lo, 4 * pr + 2 + h, hi, pr >= 2);
+        if constexpr (kTile) {
+            const int pr = u >> 1, h = u & 1;
+            const uint4 v = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * pr + 16 * h);
+            uint4 lo, hi;
+            lo.x = v.x & 0x0f0f0f0fu, lo.y = v.y & 0x0f0f0f0fu, lo.z = v.z & 0x0f0f0f0fu, lo.w = v.w & 0x0f0f0f0fu;
+            hi.x = (v.x >> 4) & 0x0f0f0f0fu, hi.y = (v.y >> 4) & 0x0f0f0f0fu;
+            hi.z = (v.z >> 4) & 0x0f0f0f0fu, hi.w = (v.w >> 4) & 0x0f0f0f0fu;
+            // sub-block 2pr holds k = 64 pr + j, sub-block 2pr + 1 holds k = 64 pr + 32 + j
+            store_pair(bt, row, 4 * pr + h, lo, 4 * pr + 2 + h, hi, pr >= 2);
+        }
         // scale / min of sub-block u (llama_reference.cpp:116-121)
         const uint32_t dd = *reinterpret_cast<const uint32_t *>(blk);
         const uint32_t s0 = *reinterpret_cast<const uint32_t *>(blk + 4);
@@ -373,15 +379,14 @@ PFNG_DEV uint4 pack_bsum(const int32_t *bsum) {
 
 // Unpack the raw W tile of stage `s` into the int8 B tile and the
 // per-(sub-block, column) fold data.  Runs once per CTA per k-step.
-template <int WT, class C>
+template <int WT, class C, bool kTile = true>
 PFNG_DEV void decode_w(const GemmParams &p, const Smem<C> &sm, int s, int64_t ks, int64_t n0, int tid) {
-    static_assert(C::kSlot == kWRowSlot, "decode_task reads kWRowSlot-byte rows");
     const uint8_t *wr = sm.w_raw(s);
     int8_t *bt = sm.b_tile();
     float *fold = reinterpret_cast<float *>(sm.fold());
     for (int task = tid; task < C::BN * 8; task += kThreads)
-        decode_task<WT, C::BN>(p, wr, bt, fold, sm.grid(), ks, n0, task, reinterpret_cast<float *>(sm.mins_d()),
-                               sm.mins_pk());
+        decode_task<WT, C::BN, kTile, C::kSlot>(p, wr, bt, fold, sm.grid(), ks, n0, task,
+                                                reinterpret_cast<float *>(sm.mins_d()), sm.mins_pk());
     if constexpr (WT == kWQ4_K) {
         for (int r = tid; r < C::BM; r += kThreads)
             sm.a_pack()[r] = pack_bsum(reinterpret_cast<const int32_t *>(sm.a_scale(s)) + r * kAScaleStride);
@@ -458,9 +463,18 @@ PFNG_DEV void load_frags_direct(uint32_t at_s, const uint8_t *wr, int kb, const 
     for (int mt = 0; mt < C::MT; ++mt) ldmatrix_x4_s(af[mt][0], af[mt][1], af[mt][2], af[mt][3], at_s + (fo.a[mt] ^ x));
 #pragma unroll
     for (int nt = 0; nt < C::NT; ++nt) {
-        const uint32_t q = raw_q4_word<WT>(wr + (wn * C::WN + nt * 8 + g) * C::kSlot, kb, t4);
-        bf[nt][0] = ((q & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
-        bf[nt][1] = (((q >> 4) & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+        const uint8_t *row = wr + (wn * C::WN + nt * 8 + g) * C::kSlot;
+        if constexpr (WT == kWQ4_K) {
+            // sub-block 2 pr + h is nibble h of qs[32 pr + j], j = 0..31 (values 0..15, no offset)
+            const uint8_t *q = row + 16 + 32 * (kb >> 1) + 4 * t4;
+            const int sh = (kb & 1) * 4;
+            bf[nt][0] = (*reinterpret_cast<const uint32_t *>(q) >> sh) & 0x0f0f0f0fu;
+            bf[nt][1] = (*reinterpret_cast<const uint32_t *>(q + 16) >> sh) & 0x0f0f0f0fu;
+        } else {
+            const uint32_t q = raw_q4_word<WT>(row, kb, t4);
+            bf[nt][0] = ((q & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+            bf[nt][1] = (((q >> 4) & 0x0f0f0f0fu) + 0x78787878u) ^ 0x80808080u;
+        }
     }
 }
 
@@ -533,7 +547,8 @@ PFNG_DEV void copy_tile_to_copies(const GemmParams &p) {
 
 template <int WT, class C, bool kPartials, bool kCopies = false, bool kDirect = false>
 __global__ void __launch_bounds__(kThreads, kDirect && C::BM == 64 ? 2 : 1) gemm_kernel(const GemmParams p) {
-    static_assert(!kDirect || ((WT == kWQ4_0 || WT == kWQ4_0P) && !kPartials), "direct operands: q4_0 products");
+    static_assert(!kDirect || ((WT == kWQ4_0 || WT == kWQ4_0P || WT == kWQ4_K) && !kPartials),
+                  "direct operands: q4_0 and q4_K products");
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Smem<C> sm{smem_raw};
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -593,11 +608,16 @@ __global__ void __launch_bounds__(kThreads, kDirect && C::BM == 64 ? 2 : 1) gemm
         const int s = static_cast<int>((ks - k0) % ST);
         cp_async_wait<ST - 2>();
         __syncthreads();
-        if constexpr (!kDirect) decode_w<WT, C>(p, sm, s, ks, n0, tid);
+        // q4_K with direct operands still decodes its 6-bit scales and mins
+        // (fold constants, min term) -- everything but the B tile
+        if constexpr (!kDirect)
+            decode_w<WT, C>(p, sm, s, ks, n0, tid);
+        else if constexpr (WT == kWQ4_K)
+            decode_w<WT, C, false>(p, sm, s, ks, n0, tid);
         if (ks + ST - 1 < k1)
             load_stage<WT, C>(p, sm, static_cast<int>((ks - k0 + ST - 1) % ST), ks + ST - 1, m0, n0, tid);
         cp_async_commit();
-        if constexpr (!kDirect) __syncthreads();
+        if constexpr (!kDirect || WT == kWQ4_K) __syncthreads();
 
         const int8_t *at = sm.a_qs(s);
         const int8_t *bt = sm.b_tile();
@@ -665,7 +685,7 @@ __global__ void __launch_bounds__(kThreads, kDirect && C::BM == 64 ? 2 : 1) gemm
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     float2 sv, cm;
-                    if constexpr (kDirect) {
+                    if constexpr (kDirect && WT != kWQ4_K) {
                         // the fold constants of columns 2 t4, 2 t4 + 1 from the raw tile (store_fold's values)
                         const uint8_t *row = wr + (wn * C::WN + nt * 8 + 2 * t4) * C::kSlot;
                         sv = make_float2(f16_bits_to_f32(raw_q4_scale<WT>(row, kb)),
@@ -1070,8 +1090,10 @@ cudaError_t launch_pdl(K kernel, const GemmParams &p, uint32_t smem, cudaStream_
 template <int WT, class C, bool kPartials, bool kCopies = false, bool kDirect = false>
 cudaError_t launch_t(const GemmParams &p, cudaStream_t s) {
     auto kernel = gemm_kernel<WT, C, kPartials, kCopies, kDirect>;
-    // direct operands use the stage ring only (no B tile, fold data or tables)
-    constexpr uint32_t smem = kDirect ? C::ST * C::kStage : C::kSmem;
+    // direct q4_0 operands use the stage ring only (no B tile, fold data or
+    // tables); q4_K keeps the layout for its fold data and mins
+    constexpr uint32_t smem = kDirect && WT != kWQ4_K ? C::ST * C::kStage : C::kSmem;
+    static_assert(smem <= kMaxSmemPerCta, "dynamic shared memory above the per-CTA limit");
     static thread_local bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1087,6 +1109,7 @@ template <int WT, class C, bool kCopies = false>
 cudaError_t launch_t_ov(const GemmParams &p, cudaStream_t s) {
     auto kernel = gemm_kernel_ov<WT, C, kCopies>;
     constexpr uint32_t smem = SmemOv<C>::kTotal;
+    static_assert(smem <= kMaxSmemPerCta, "dynamic shared memory above the per-CTA limit");
     static_assert(C::BM * (C::BN + 4) * 4 <= smem, "staged C tile of the q8_0 epilogue");
     static thread_local bool configured[64] = {false};
     int dev = 0;
@@ -1139,11 +1162,13 @@ cudaError_t launch_pick(const GemmParams &p, cudaStream_t s) {
     // copies (fp32 C to more destinations): the kernels built with the copy
     // pass; with split-K the reduction stores the copies
     const bool copies = p.ncopies > 0 && p.splits == 1;
-    if constexpr (!kPartials && (WT == kWQ4_0 || WT == kWQ4_0P)) {
+    if constexpr (!kPartials && (WT == kWQ4_0 || WT == kWQ4_0P || WT == kWQ4_K)) {
         // 176-byte row slots (44 words): the eight rows of a fragment read
         // start on banks 12 r mod 32, so with the four t4 words they hit
-        // all 32 banks (160-byte slots: rows r and r + 4 collide)
-        using D = Cfg<C::BM, C::BN, C::ST, 176>;
+        // all 32 banks (160-byte slots: rows r and r + 4 collide).  q4_K
+        // keeps 160-byte slots: its full layout (fold data, mins) with
+        // 176-byte rows would pass the per-CTA limit on 128 x 128 tiles.
+        using D = Cfg<C::BM, C::BN, C::ST, WT == kWQ4_K ? kWRowSlot : 176u>;
         if ((WT == kWQ4_0P || p.w_vec16) && direct_enabled())
             return copies ? launch_t<WT, D, false, true, true>(p, s) : launch_t<WT, D, false, false, true>(p, s);
     }

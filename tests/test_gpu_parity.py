@@ -378,29 +378,32 @@ def test_split_k_small_m(oracle, monkeypatch, m, n, k):
     check_close(c1, oracle.mm("q4_0", w, a, m, n, k), oracle.bound("q4_0", w, a, m, n, k), f"unsplit {m}x{n}x{k}")
 
 
-@pytest.mark.parametrize("layout", ["ggml", "planar"])
+@pytest.mark.parametrize("layout", ["ggml", "planar", "q4_K"])
 @pytest.mark.parametrize("m,n,k,splits", [(32, 1024, 4096, None), (32, 4000, 2048, "1"), (9, 300, 1536, "1"),
                                           (17, 640, 4096, None), (32, 130, 256, "1"), (40, 1000, 1536, None),
                                           (64, 2048, 4096, None), (130, 700, 2048, "1"), (480, 1536, 1536, None),
                                           (2048, 2048, 512, None), (1100, 3000, 1024, None)])
 def test_direct_operands_equal_decode_pass(oracle, monkeypatch, layout, m, n, k, splits):
-    # q4_0 tiles (32, 64 and 128 rows) build the B fragments straight from
-    # the raw W tile; PFNG_B200_GEMM_DIRECT=0 runs the decode pass into the
-    # B tile (the two-phase or the overlapped kernel).  Same
+    # q4_0 and q4_K tiles (32, 64 and 128 rows) build the B fragments
+    # straight from the raw W tile; PFNG_B200_GEMM_DIRECT=0 runs the decode
+    # pass into the B tile (the two-phase or the overlapped kernel).  Same
     # products, same fold constants, same order: the same bits, and both
     # within tolerance of the oracle.
     if splits:
         monkeypatch.setenv("PFNG_B200_GEMM_SPLITS", splits)
+    if layout == "q4_K" and k % 256 != 0:
+        pytest.skip("q4_K needs k % 256 == 0")
     rng = np.random.default_rng(m * 5 + n + k)
-    w = oracle.quantize("q4_0", rng.standard_normal((n, k)).astype(np.float32))
+    base = "q4_K" if layout == "q4_K" else "q4_0"
+    w = oracle.quantize(base, rng.standard_normal((n, k)).astype(np.float32))
     x = rng.standard_normal((m, k)).astype(np.float32)
-    a = oracle.quantize("q8_0", x)
+    a = oracle.quantize(act_kind(base), x)
     wd, xd = dev_bytes(w), dev(x)
-    wt = "q4_0"
+    wt = base
     if layout == "planar":
         wd, wt = pb.pack_q4_0_planar(wd, n, k), "q4_0_planar"
     c = host(pb.compute(wt, wd, xd, n, path="mma"))
-    check_close(c, oracle.mm("q4_0", w, a, m, n, k), oracle.bound("q4_0", w, a, m, n, k), f"direct {m}x{n}x{k}")
+    check_close(c, oracle.mm(base, w, a, m, n, k), oracle.bound(base, w, a, m, n, k), f"direct {m}x{n}x{k}")
     monkeypatch.setenv("PFNG_B200_GEMM_DIRECT", "0")
     c0 = host(pb.compute(wt, wd, xd, n, path="mma"))
     np.testing.assert_array_equal(c.view(np.uint32), c0.view(np.uint32))
