@@ -546,7 +546,7 @@ PFNG_DEV void copy_tile_to_copies(const GemmParams &p) {
 }
 
 template <int WT, class C, bool kPartials, bool kCopies = false, bool kDirect = false>
-__global__ void __launch_bounds__(kThreads, kDirect && C::BM == 64 ? 2 : 1) gemm_kernel(const GemmParams p) {
+__global__ void __launch_bounds__(kThreads, kDirect && (C::BM == 64 || (C::BM == 32 && WT == kWQ4_K)) ? 2 : 1) gemm_kernel(const GemmParams p) {
     static_assert(!kDirect || ((WT == kWQ4_0 || WT == kWQ4_0P || WT == kWQ4_K) && !kPartials),
                   "direct operands: q4_0 and q4_K products");
     extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -1141,8 +1141,9 @@ constexpr bool kOvType = !kPartials && WT != kWQ4_K;
 // 45.5, 128x4096x4096 25.1 vs 28.8, 64x11008x4096 40.9 vs 44.7.  A deeper
 // ring, which the smaller shared-memory footprint would allow, was slower
 // (32x32000x4096: 3 stages 56.6, 4 stages 66.3 us), and so were three
-// 32-row CTAs per SM at 80 registers (78.7 us).  64-row direct kernels are
-// bounded to two CTAs per SM (<= 128 registers, no spills).  On 128 x 128
+// 32-row CTAs per SM at 80 registers (78.7 us).  64-row direct kernels, and
+// 32-row q4_K ones (151 registers unbounded), are bounded to two CTAs per SM
+// (<= 128 registers, no spills; q4_K 32x11008x4096 35.8 -> 31.3 us).  On 128 x 128
 // tiles the direct two-phase kernel also beats the overlapped decode:
 // 2048x11008x4096 589.6 vs 622.7, 2048x4096x4096 242.4 vs 255.4,
 // 512x4096x4096 62.4 vs 65.5, 2048x4096x11008 629.8 vs 661.5.
