@@ -71,6 +71,19 @@ const char *pfng_b200_status_string(int status);
  * a bounded wait since the last call, else PFNG_B200_OK (or a CUDA error). */
 int pfng_b200_check_kernel_error(void *stream);
 
+/* Self-test of the failure path above, for tests and health checks: one
+ * small kernel in which a producer warp arrives on an mbarrier (or, with
+ * skip_arrive != 0, does not) and a consumer warp waits for it through the
+ * same bounded wait every pipelined kernel of the library uses, limited to
+ * `attempts` tries of at most ~1 us each.  A wait that runs out records the
+ * error that pfng_b200_check_kernel_error then returns
+ * (PFNG_B200_ERR_KERNEL_TIMEOUT) and the kernel returns normally, so the
+ * context stays usable.  completed: optional device int, set to 1 if the wait
+ * succeeded and 0 if it gave up.  Asynchronous on `stream`.  The reference
+ * has no device code and no counterpart; its failure convention is the
+ * fail-closed registration of bench/framework/kernel_registry.cpp:13-17. */
+int pfng_b200_selftest_wait(unsigned attempts, int skip_arrive, int *completed, void *stream);
+
 /* ---- activation quantizers ---------------------------------------------
  * x: fp32 [m][ldx] (ldx >= k); y: blocks [m][k / 32] or [m][k / 256].
  * Replace llama_reference::quantize_row_q8_0 (llama_reference.cpp:38-52) and
@@ -120,6 +133,29 @@ int pfng_b200_compute_q4_K(const void *w, const float *x, int64_t ldx, float *c,
 int pfng_b200_compute_iq2_xxs(const void *w, const float *x, int64_t ldx, float *c, int64_t m, int64_t n,
                               int64_t k, int64_t ldc, void *workspace, size_t workspace_bytes, int path,
                               void *stream);
+
+/* ---- prefill: activations quantized once, multiplied by several matrices ---
+ * The projections that read the same layer input (Q/K/V, gate/up) quantize
+ * it once: pfng_b200_prepare_activations quantizes x [m][ldx] (q8_0 for
+ * q4_0 weights, q8_K otherwise, with the quantizers above -- the same bytes)
+ * into the tensor-core GEMM's operand layout in `prepared` (256-byte
+ * aligned, at least pfng_b200_prepared_bytes(wtype, m, k) bytes, 0 for
+ * unsupported arguments); pfng_b200_mm_prepared then runs only the GEMM on
+ * it, as often as needed, for any weight matrix of that type with the same
+ * k.  Needs k % 256 == 0 and 16-byte aligned W (PFNG_B200_ERR_SHAPE /
+ * PFNG_B200_ERR_UNSUPPORTED otherwise).  workspace (optional, at least
+ * pfng_b200_mm_prepared_workspace_size bytes; 0 = none needed) holds the
+ * split-k tiles of small-m shapes; with it C is bit-identical to
+ * pfng_b200_compute_* with PFNG_B200_PATH_MMA, without it those shapes run
+ * unsplit (same error bound, other summation order).
+ * The reference quantizes the activations inside every compute() call
+ * (llama_reference.cpp:213); this hoists that step out of a group of calls. */
+size_t pfng_b200_prepared_bytes(int wtype, int64_t m, int64_t k);
+int pfng_b200_prepare_activations(int wtype, const float *x, int64_t ldx, void *prepared, size_t prepared_bytes,
+                                  int64_t m, int64_t k, void *stream);
+size_t pfng_b200_mm_prepared_workspace_size(int wtype, int64_t m, int64_t n, int64_t k);
+int pfng_b200_mm_prepared(int wtype, const void *w, const void *prepared, float *c, int64_t m, int64_t n, int64_t k,
+                          int64_t ldc, void *workspace, size_t workspace_bytes, void *stream);
 
 /* ---- decode: several weight matrices sharing one activation --------------
  * The projections that read the same layer input (Q/K/V, or gate/up) in ONE
@@ -273,21 +309,26 @@ int pfng_b200_ipc_close(void *ptr);
  * device memory on this call path -- e.g. a server whose memory pool owns the
  * whole GPU from start-up, or a loop that cannot take the device-wide
  * synchronisation of cudaMalloc / cudaFree.  It takes no workspace: its
- * scratch (the quantized activations) is a fixed array of
+ * scratch (the quantized activations and, for the small-m shapes whose k is
+ * split across CTAs, the split products' fp32 tiles) is a fixed array of
  * PFNG_B200_NOALLOC_SCRATCH_BYTES inside the library, held by every GPU that
  * loads the library until the process exits.
  *   - Problems whose scratch would exceed that size (about m * k * 1.25
- *     bytes, m rounded up to 128; e.g. m <= 2048 at k = 4096) return
- *     PFNG_B200_ERR_WORKSPACE; k must be a multiple of 256 and w 16-byte
- *     aligned (else PFNG_B200_ERR_UNSUPPORTED).
+ *     bytes, m rounded up to 128, plus splits * m * n * 4 bytes when k is
+ *     split; e.g. m <= 2048 at k = 4096) return PFNG_B200_ERR_WORKSPACE; k
+ *     must be a multiple of 256 and w 16-byte aligned (else
+ *     PFNG_B200_ERR_UNSUPPORTED).
  *   - The first call on each device looks up the array's device address
  *     (cudaGetSymbolAddress); make that first call before any stream capture.
+ *     The address is cached for the process: do not use the library after a
+ *     cudaDeviceReset.
  *   - All calls on a device share the array, which keeps the last call's
  *     contents; each call rewrites everything it reads, but calls whose
  *     kernels overlap on the GPU (other streams, other host threads) race on
  *     it and must be ordered by the caller.
- * No counterpart in the reference; results equal pfng_b200_compute_q4_0 with
- * PFNG_B200_PATH_MMA. */
+ * No counterpart in the reference.  It makes the kernel choices of
+ * pfng_b200_compute_q4_0 with PFNG_B200_PATH_MMA (split-k factor included),
+ * so C is bit-identical to that call's. */
 #define PFNG_B200_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
 int pfng_b200_compute_q4_0_noalloc(const void *w, const float *x, int64_t ldx, float *c, int64_t m, int64_t n,
                                    int64_t k, int64_t ldc, void *stream);

@@ -487,6 +487,61 @@ int pfng_b200_compute_iq2_xxs(const void *w, const float *x, int64_t ldx, float 
                       path, static_cast<cudaStream_t>(stream));
 }
 
+// ---- prepared activations: quantize once, multiply by several matrices ----
+size_t pfng_b200_prepared_bytes(int wtype, int64_t m, int64_t k) {
+    if (!valid_wtype(wtype) || m <= 0 || k <= 0 || k % 256 != 0) return 0;
+    return split_a_bytes(m, k, block_k(wtype));
+}
+
+int pfng_b200_prepare_activations(int wtype, const float *x, int64_t ldx, void *prepared, size_t prepared_bytes,
+                                  int64_t m, int64_t k, void *stream) {
+    if (!valid_wtype(wtype) || m < 0 || k < 0) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    if (k % 256 != 0) return PFNG_B200_ERR_SHAPE;
+    if (m > 0 && ldx < k) return PFNG_B200_ERR_SHAPE;
+    if (m == 0 || k == 0) return PFNG_B200_OK;
+    if (!x || !prepared) return PFNG_B200_ERR_INVALID_ARGUMENT;
+    if (!aligned(x, 4) || !aligned(prepared, 256)) return PFNG_B200_ERR_ALIGNMENT;
+    const int qk = block_k(wtype);
+    if (prepared_bytes < split_a_bytes(m, k, qk)) return PFNG_B200_ERR_WORKSPACE;
+    DeviceInfo *info = nullptr;
+    int st = device_info(&info);
+    if (st != PFNG_B200_OK) return st;
+    const SplitA sa = split_a_carve(prepared, m, k, qk);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    return status_of(q8_0_act(wtype) ? launch_quantize_q8_0_split(x, ldx, sa, m, k, s)
+                                     : launch_quantize_q8_K_split(x, ldx, sa, m, k, s));
+}
+
+size_t pfng_b200_mm_prepared_workspace_size(int wtype, int64_t m, int64_t n, int64_t k) {
+    if (!valid_wtype(wtype) || m <= 0 || n <= 0 || k <= 0 || k % 256 != 0) return 0;
+    const size_t part = gemm_partial_bytes(m, n, k);
+    return part > 0 ? part + 256 : 0;
+}
+
+int pfng_b200_mm_prepared(int wtype, const void *w, const void *prepared, float *c, int64_t m, int64_t n, int64_t k,
+                          int64_t ldc, void *workspace, size_t workspace_bytes, void *stream) {
+    int st = check_mm(wtype, w, prepared, c, m, n, k, ldc, 0, false, false, PFNG_B200_PATH_MMA);
+    if (st != PFNG_B200_OK) return st;
+    if (k % 256 != 0) return PFNG_B200_ERR_SHAPE;
+    if (m == 0 || n == 0) return PFNG_B200_OK;
+    DeviceInfo *info = nullptr;
+    if (k == 0) {
+        if ((st = device_info(&info)) != PFNG_B200_OK) return st;
+        return status_of(zero_c(c, m, n, ldc, static_cast<cudaStream_t>(stream)));
+    }
+    if (!aligned(prepared, 256)) return PFNG_B200_ERR_ALIGNMENT;
+    if ((st = device_info(&info)) != PFNG_B200_OK) return st;
+    if (!gemm_supported(wtype, m, n, k, w)) return PFNG_B200_ERR_UNSUPPORTED;
+    const SplitA sa = split_a_carve(const_cast<void *>(prepared), m, k, block_k(wtype));
+    GemmArgs g{wtype, w, sa, c, ldc, nullptr, m, n, k, info->error_word};
+    const size_t part = gemm_partial_bytes(m, n, k);
+    if (part > 0 && workspace && workspace_bytes >= part + 256) {
+        g.partial = static_cast<float *>(align_ptr(workspace, 256));
+        g.partial_bytes = part;
+    }
+    return status_of(launch_gemm(g, static_cast<cudaStream_t>(stream)));
+}
+
 int pfng_b200_compute_grouped(int wtype, int count, const void *const *w, const int64_t *n, float *const *c,
                               const int64_t *ldc, const float *x, int64_t ldx, int64_t m, int64_t k, unsigned flags,
                               void *stream) {

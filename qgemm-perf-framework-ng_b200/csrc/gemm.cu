@@ -1094,6 +1094,8 @@ cudaError_t launch_t(const GemmParams &p, cudaStream_t s) {
     // tables); q4_K keeps the layout for its fold data and mins
     constexpr uint32_t smem = kDirect && WT != kWQ4_K ? C::ST * C::kStage : C::kSmem;
     static_assert(smem <= kMaxSmemPerCta, "dynamic shared memory above the per-CTA limit");
+    // the q8_0 epilogue stages the CTA's C tile in the launched shared memory
+    static_assert(C::BM * (C::BN + 4) * 4 <= smem, "staged C tile of the q8_0 epilogue");
     static thread_local bool configured[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);

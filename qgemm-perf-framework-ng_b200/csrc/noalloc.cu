@@ -7,17 +7,25 @@
 // allocation afterwards, or a latency-critical loop that cannot afford the
 // device-wide synchronisation cudaMalloc / cudaFree can cause.  For them this
 // entry point keeps its scratch -- the quantized activation rows of the
-// tensor-core path -- in a fixed array compiled into the library, so a call
-// allocates nothing.
+// tensor-core path and, for the small-m shapes that split k, the split
+// products' fp32 tiles -- in a fixed array compiled into the library, so a
+// call allocates nothing.  It makes the same kernel choices as
+// pfng_b200_compute_q4_0 on the tensor-core path (the same split-k factor
+// included), so its C is bit-identical to that call's.
 //
 // The array is kNoAllocScratchBytes (16 MiB), and every GPU that loads the
 // library holds it until the process exits.  All calls on a device share it
 // and it keeps the previous call's contents.  Every call writes the whole
-// region it later reads (the quantizer fills every padded row) before the
-// matmul reads it, so nothing has to be cleared first; but two calls whose
-// kernels run at the same time on one device (different streams, or
-// different host threads) would overwrite each other's scratch, so callers
-// must keep them ordered.
+// region it later reads (the quantizer fills every padded row, every split
+// writes its whole tile) before anything reads it, so nothing has to be
+// cleared first; but two calls whose kernels run at the same time on one
+// device (different streams, or different host threads) would overwrite
+// each other's scratch, so callers must keep them ordered.
+//
+// The device address of the array is looked up once per device and cached
+// for the life of the process; like the rest of the library's per-device
+// state it does not survive cudaDeviceReset (or a reset of the primary
+// context), after which the library must not be used in this process.
 #include <mutex>
 
 #include "pfng_b200.h"
@@ -77,17 +85,29 @@ extern "C" int pfng_b200_compute_q4_0_noalloc(const void *w, const float *x, int
     if (!w || !x || !c) return PFNG_B200_ERR_INVALID_ARGUMENT;
     if (!aligned(w, 2) || !aligned(x, 4) || !aligned(c, 4)) return PFNG_B200_ERR_ALIGNMENT;
     if (k == 0 || k % 256 != 0 || !aligned(w, 16)) return PFNG_B200_ERR_UNSUPPORTED;  // tensor-core path only
-    if (split_a_bytes(m, k, 32) > kNoAllocScratchBytes) return PFNG_B200_ERR_WORKSPACE;  // beyond the fixed scratch
+    // the split activation operand, then (shapes that split k) the split tiles
+    const size_t a_bytes = split_a_bytes(m, k, 32);
+    if (a_bytes > kNoAllocScratchBytes) return PFNG_B200_ERR_WORKSPACE;  // beyond the fixed scratch
 
     void *scratch = nullptr;
     int st = scratch_for_current_device(&scratch);
     if (st != PFNG_B200_OK) return st;
     if (!gemm_supported(PFNG_B200_Q4_0, m, n, k, w)) return PFNG_B200_ERR_UNSUPPORTED;
 
+    // split-k tiles as pfng_b200_compute_q4_0 carves them from its workspace
+    // (256-byte aligned, behind the activation operand)
+    const size_t part = gemm_partial_bytes(m, n, k);
+    if (part > 0 && a_bytes + part + 256 > kNoAllocScratchBytes) return PFNG_B200_ERR_WORKSPACE;
+
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     const SplitA sa = split_a_carve(scratch, m, k, 32);
     cudaError_t e = launch_quantize_q8_0_split(x, ldx, sa, m, k, s);
     if (e != cudaSuccess) return status_of(e);
     GemmArgs g{PFNG_B200_Q4_0, w, sa, c, ldc, nullptr, m, n, k, device_error_word()};
+    if (part > 0) {
+        const uintptr_t end = reinterpret_cast<uintptr_t>(scratch) + a_bytes;
+        g.partial = reinterpret_cast<float *>((end + 255u) & ~uintptr_t(255));
+        g.partial_bytes = part;
+    }
     return status_of(launch_gemm(g, s));
 }

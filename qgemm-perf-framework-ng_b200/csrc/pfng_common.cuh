@@ -101,11 +101,16 @@ PFNG_DEV bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
 // Every wait in this library is bounded: about 2^20 attempts of <= ~1 us, so
 // a wait that can never complete ends in about a second with `code` recorded.
 constexpr uint32_t kWaitAttempts = 1u << 20;
-PFNG_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, int *flag, int code) {
-    for (uint32_t i = 0; i < kWaitAttempts; ++i)
+// The wait with an explicit attempt limit (the self-test kernel passes a
+// small one); every kernel's waits use kWaitAttempts.
+PFNG_DEV bool mbar_wait_n(uint64_t *bar, uint32_t parity, int *flag, int code, uint32_t attempts) {
+    for (uint32_t i = 0; i < attempts; ++i)
         if (mbar_try_wait(bar, parity)) return true;
     report_error(flag, code);
     return false;
+}
+PFNG_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, int *flag, int code) {
+    return mbar_wait_n(bar, parity, flag, code, kWaitAttempts);
 }
 
 // Bulk (non-tensor) TMA copy global -> this CTA's shared memory, completing

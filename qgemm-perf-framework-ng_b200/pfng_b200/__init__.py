@@ -41,6 +41,7 @@ OUT_F32, OUT_F16, OUT_BF16, OUT_Q8_0 = 0, 1, 2, 3
 OUT_FORMATS = {"f32": OUT_F32, "f16": OUT_F16, "bf16": OUT_BF16, "q8_0": OUT_Q8_0}
 
 OK = 0
+ERR_INVALID_ARGUMENT = -1
 ERR_KERNEL_TIMEOUT = -6
 OVERLAP_WEIGHTS = 1
 
@@ -124,6 +125,16 @@ def _declare(L: ctypes.CDLL) -> None:
         f = getattr(L, f"pfng_b200_{name}")
         f.restype = I
         f.argtypes = [P]
+    L.pfng_b200_prepared_bytes.restype = S
+    L.pfng_b200_prepared_bytes.argtypes = [I, I64, I64]
+    L.pfng_b200_prepare_activations.restype = I
+    L.pfng_b200_prepare_activations.argtypes = [I, P, I64, P, S, I64, I64, P]
+    L.pfng_b200_mm_prepared_workspace_size.restype = S
+    L.pfng_b200_mm_prepared_workspace_size.argtypes = [I, I64, I64, I64]
+    L.pfng_b200_mm_prepared.restype = I
+    L.pfng_b200_mm_prepared.argtypes = [I, P, P, P, I64, I64, I64, I64, P, S, P]
+    L.pfng_b200_selftest_wait.restype = I
+    L.pfng_b200_selftest_wait.argtypes = [ctypes.c_uint, I, P, P]
 
 
 def header_functions() -> list[str]:
@@ -340,6 +351,42 @@ def compute_grouped(wtype, weights, x, ns, outs=None, overlap_weights=False, str
     return outs
 
 
+def prepare_activations(wtype, x, out=None, stream=None):
+    """fp32 x [m][k] (row stride x.stride(0)) quantized once into the
+    tensor-core GEMM's operand layout (pfng_b200_prepare_activations); the
+    result is a flat uint8 tensor for mm_prepared."""
+    import torch
+    wt = _wt(wtype)
+    m, k = x.shape
+    nbytes = lib().pfng_b200_prepared_bytes(wt, m, k)
+    if nbytes == 0:
+        raise PfngError(-2, "prepared_bytes")
+    if out is None:
+        out = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+    _check(lib().pfng_b200_prepare_activations(wt, _ptr(x), x.stride(0), _ptr(out), out.numel(), m, k,
+                                               _stream(stream)), "prepare_activations")
+    return out
+
+
+def mm_prepared_workspace_size(wtype, m: int, n: int, k: int) -> int:
+    return lib().pfng_b200_mm_prepared_workspace_size(_wt(wtype), m, n, k)
+
+
+def mm_prepared(wtype, w, prepared, m: int, n: int, k: int, out=None, workspace=None, stream=None):
+    """C [m][n] = prepared activations . W^T: the tensor-core GEMM alone
+    (pfng_b200_mm_prepared).  workspace=None allocates the split-k tiles
+    the shape needs; pass a zero-size tensor to run unsplit."""
+    import torch
+    wt = _wt(wtype)
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float32, device=w.device)
+    ws = _workspace(mm_prepared_workspace_size(wt, m, n, k), w.device, None) if workspace is None else workspace
+    nbytes = 0 if ws is None else ws.numel()
+    _check(lib().pfng_b200_mm_prepared(wt, _ptr(w), _ptr(prepared), _ptr(out), m, n, k, out.stride(0), _ptr(ws),
+                                       nbytes, _stream(stream)), "mm_prepared")
+    return out
+
+
 def partials(wtype, w, a, m: int, n: int, k: int, path="auto", workspace=None, stream=None):
     """int32 [m][n][k/32] integer sub-block dot products of the chosen kernel path."""
     import torch
@@ -355,6 +402,19 @@ def partials(wtype, w, a, m: int, n: int, k: int, path="auto", workspace=None, s
 
 def check_kernel_error(stream=None) -> None:
     _check(lib().pfng_b200_check_kernel_error(_stream(stream)), "kernel error word")
+
+
+def selftest_wait(attempts: int, skip_arrive: bool, stream=None):
+    """Run the bounded-wait self-test kernel (pfng_b200_selftest_wait) and
+    return (completed, status): whether the consumer's wait succeeded, and
+    what pfng_b200_check_kernel_error reported afterwards (the error word is
+    read and cleared)."""
+    import torch
+    done = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    _check(lib().pfng_b200_selftest_wait(attempts, 1 if skip_arrive else 0, _ptr(done), _stream(stream)),
+           "selftest_wait")
+    status = lib().pfng_b200_check_kernel_error(_stream(stream))
+    return int(done.item()), status
 
 
 # ----------------------------------------------------------------- sharding

@@ -155,3 +155,8 @@ def test_output_format_argument_checks(L):
     assert pb.lib().pfng_b200_compute_out_workspace_size(0, 0, 1, 4096, 4096, 1) == 0
     fused = pb.lib().pfng_b200_compute_out_workspace_size(0, 3, 480, 1536, 1536, 2)
     assert fused == pb.compute_workspace_size("q4_0", 480, 1536, 1536, "mma")
+
+
+def test_selftest_wait_rejects_zero_attempts(L):
+    # checked on the host before any CUDA call
+    assert L.pfng_b200_selftest_wait(0, 1, None, None) == INVALID
