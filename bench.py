@@ -1,33 +1,54 @@
 """Benchmark of the B200 block-quantized matmul hot path.
 
-Metric: 2MNK int-ops/s and weight GB/s against the HBM /
-int8 tensor-core roofline.
+Metric: 2MNK int-ops/s and weight GB/s against the int8
+tensor-core / HBM roofline, on 1/2/4/8 B200s.
 
-Default workload (the decode configuration):
-one step = the activation row x (fp32, K=4096, seeded N(0,1)) quantized to
-q8_0 on the device and multiplied by two q4_0 weight matrices,
-N=4096 x K=4096 and N=11008 x K=4096 (seeded N(0,1), quantized on the device
-with the bit-exact q4_0 quantizer), through pfng_b200_compute_grouped -- the
-quantization is fused into the HBM-streaming GEMV and both matrices, which
-share the activation row, stream in one launch.
-The steps rotate over enough weight copies that the weights of a step are
-never in the 126 MB L2 (inputs larger than L2).
+Headline workload (the bench line; BASELINE.json configs[4], its largest
+shape, the only configuration quoted for 1/2/4/8 GPUs): one step is
+C[2048][32000] = quantize_q8_0(x) . W^T with q4_0 weights W [32000][4096]
+(seeded N(0, 0.02), quantized on the device by the bit-exact q4_0 quantizer)
+and fp32 activations x [2048][4096] (seeded N(0, 1)).
+  * 1 GPU: pfng_b200_compute_q4_0 (activation quantizer + tensor-core GEMM).
+  * N GPUs (torchrun, one process per GPU): the weight rows are sharded
+    (pfng_b200_shard_rows, 128-row granules); rank 0 quantizes x to q8_0 and
+    NCCL-broadcasts the bytes; every rank's pfng_b200_mm_gather computes its
+    columns of C and stores them into every rank's full C over NVLink (CUDA
+    IPC peer pointers); a one-element NCCL all-reduce orders the ranks.  The
+    total work is fixed ("scaling": "strong").
+Inputs are larger than L2: the steps rotate over copies of (W, x) totalling
+more than 4x the 126 MB L2, and every step writes the 262 MB C.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+Keys of the JSON line beyond the driver contract:
+  * roofline   -- the GEMM kernel alone (pfng_b200_mm_prepared on prepared
+                  activations; K back-to-back launches between CUDA events on
+                  the launching stream), 2 m n_rank k per launch against 2x
+                  the measured bf16 tensor peak (the dense int8 rate); traffic
+                  from profiles/ncu_traffic.json (ncu DRAM bytes of one launch).
+  * e2e        -- the same step through the public entry points with pinned
+                  HOST x in and HOST C out every step; the copies of step i+1
+                  (x in) and i-1 (C out) run on two more streams beside step
+                  i's compute (double-buffered device x and C).
+  * sweep      -- every other BASELINE configuration, measured in the same
+                  run: configs[0]/[2]/[3] (480x1536x1536 for q4_0, q4_K,
+                  iq2_xxs), configs[1] (the m=1 decode GEMV) and all twelve
+                  configs[4] shapes (sharded under N GPUs).
+  * cpu_baseline -- the reference's own scalar llama_reference code
+                  (oracle/_ref; the C restatement if it was not built) on a
+                  row sample of the headline workload, at 1 thread and at all
+                  host threads, min and median over samples.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--repeats R]
+                  [--impl ours|reference] [--no-sweep] [--no-cpu-baseline]
 
 --impl reference times the reference's own CPU implementation of the same
-step (oracle/_ref: bench/llama_reference compiled from the reference's
-sources; all host threads) on the same config and metric.
-
-With --gpus N > 1 (launched by torchrun, one process per GPU) every rank runs
-an independent replica of the workload (the decode GEMV is too small to
-shard: the NCCL latency of gathering its output exceeds its runtime), timed
-as the max over ranks; `value` is the whole-job aggregate.
+step (quantize + dots of bench/llama_reference, element-parallel over all
+host threads) on a row sample of the headline workload, on rank 0 only.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import pathlib
 import statistics
@@ -41,46 +62,43 @@ sys.path.insert(0, str(ROOT / "qgemm-perf-framework-ng_b200"))
 
 METRIC = "2MNK int-ops/s and weight GB/s vs int8-TC/HBM roofline, 1/2/4/8 B200"
 UNIT = "Gop/s"
-K_DIM = 4096
-N_DIMS = (4096, 11008)
-Q4_0_ROW_BYTES = K_DIM // 32 * 18
+HEADLINE = ("q4_0", 2048, 32000, 4096)  # configs[4], largest shape
+LLAMA_MS = (32, 512, 2048)
+LLAMA_NK = ((4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096))
+SMALL_CONFIGS = (("configs[0]", "q4_0"), ("configs[2]", "q4_K"), ("configs[3]", "iq2_xxs"))  # 480x1536x1536
+DECODE_NS, DECODE_K = (4096, 11008), 4096  # configs[1]
+GRANULE = 128
 L2_BYTES = 126 * 1024 * 1024
 
 
-def step_ops() -> float:
-    return float(sum(2 * 1 * n * K_DIM for n in N_DIMS))
-
-
-def step_weight_bytes(wtype: str = "q4_0") -> int:
-    return sum(weight_bytes(wtype, n, K_DIM) for n in N_DIMS)
+def weight_bytes(wtype: str, n: int, k: int) -> int:
+    return n * (k // 32 * 18 if wtype == "q4_0" else k // 256 * (144 if wtype == "q4_K" else 66))
 
 
 def dist_env():
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return world, rank, local
+    return int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), \
+        int(os.environ.get("LOCAL_RANK", "0"))
 
 
-def measured_peaks():
+def peaks() -> dict:
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
-        data = json.loads(path.read_text())
-        return float(data["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        d = json.loads(path.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "int8_tops": 2.0 * float(d["bf16_tflops"]),
+                "source": "measured (MEASURED_PEAKS.json: hbm_gbs; int8 = 2 x bf16_tflops burst)"}
+    return {"hbm_gbs": 6650.0, "int8_tops": 2.0 * 1590.0,
+            "source": "fallback (6.65 TB/s; int8 = 2 x 1.59 PFLOP/s bf16)"}
 
 
-def profile_traffic(kernel_tag: str, variant: str | None = None):
-    """DRAM bytes per launch from a committed ncu summary, if one exists (the
-    line `traffic_bytes_per_launch:` or `traffic_bytes_per_launch (variant):`)."""
-    path = ROOT / "profiles" / f"{kernel_tag}.md"
+def ncu_traffic(key: str):
+    """DRAM bytes (read + write) per launch from the committed ncu counters, or None."""
+    path = ROOT / "profiles" / "ncu_traffic.json"
     if not path.exists():
         return None
-    key = "traffic_bytes_per_launch" + (f" ({variant})" if variant else "") + ":"
-    for line in path.read_text().splitlines():
-        if line.startswith(key):
-            return float(line.split(":", 1)[1])
-    return None
+    entry = json.loads(path.read_text()).get(key)
+    if not entry:
+        return None
+    return float(entry["dram_bytes_read"]) + float(entry["dram_bytes_write"])
 
 
 class ClockSampler:
@@ -130,7 +148,7 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
-# ------------------------------------------------------------------ CPU arms
+# ====================================================================== CPU
 def cpu_library():
     """(library, kind): the reference's own code if it was compiled, else the oracle port."""
     sys.path.insert(0, str(ROOT / "tests"))
@@ -148,262 +166,126 @@ def cpu_threads() -> int:
         return os.cpu_count() or 1
 
 
-def cpu_step_inputs(seed: int = 1):
+def cpu_model() -> str:
+    try:
+        for line in pathlib.Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def host_headline_weights(lib, seed: int = 11):
+    """q4_0 blocks of seeded N(0, 0.02) weights [N][K], quantized by the CPU library."""
     import numpy as np
+    _, _, n, k = HEADLINE
     rng = np.random.default_rng(seed)
-    x = rng.standard_normal((1, K_DIM)).astype(np.float32)
-    ws = [rng.standard_normal((n, K_DIM)).astype(np.float32) for n in N_DIMS]
-    return x, ws
+    w = (rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02))
+    return lib.quantize("q4_0", w)
 
 
-def run_cpu_steps(lib, kind: str, weights, x, steps: int, threads: int) -> float:
-    """Seconds for `steps` decode steps of the reference CPU path."""
+def cpu_rows_step(lib, kind: str, w, x, threads: int) -> float:
+    """Seconds for one sample: quantize x's rows to q8_0 and multiply by all of W."""
+    _, _, n, k = HEADLINE
     t0 = time.perf_counter()
-    for _ in range(steps):
-        a = lib.quantize("q8_0", x)
-        for w, n in zip(weights, N_DIMS):
-            if kind == "reference":
-                lib.mm_threads("q4_0", w, a, 1, n, K_DIM, threads)
-            else:
-                lib.mm("q4_0", w, a, 1, n, K_DIM)
+    a = lib.quantize("q8_0", x)
+    if kind == "reference":
+        lib.mm_threads("q4_0", w, a, x.shape[0], n, k, threads)
+    else:
+        lib.mm("q4_0", w, a, x.shape[0], n, k)
     return time.perf_counter() - t0
 
 
-def cpu_baseline(budget_s: float = 10.0):
+def cpu_sample_rows(lib, kind, w, threads: int, target_s: float, seed: int) -> int:
+    import numpy as np
+    _, m, _, k = HEADLINE
+    x = np.random.default_rng(seed).standard_normal((1, k), dtype=np.float32)
+    one = cpu_rows_step(lib, kind, w, x, threads)
+    return max(1, min(m, int(target_s / max(one, 1e-6))))
+
+
+def cpu_measure(lib, kind, w, threads: int, rows: int, samples: int, seed: int) -> dict:
+    import numpy as np
+    _, _, n, k = HEADLINE
+    x = np.random.default_rng(seed).standard_normal((rows, k), dtype=np.float32)
+    cpu_rows_step(lib, kind, w, x, threads)  # warm (thread pool, pages)
+    times = [cpu_rows_step(lib, kind, w, x, threads) for _ in range(samples)]
+    ops = 2.0 * rows * n * k
+    return {"threads": threads, "rows": rows, "samples": samples,
+            "min_s": min(times), "median_s": statistics.median(times),
+            "value_median": ops / statistics.median(times) / 1e9, "value_best": ops / min(times) / 1e9}
+
+
+def cpu_baseline() -> dict:
     lib, kind = cpu_library()
-    threads = cpu_threads() if kind == "reference" else int(os.environ.get("OMP_NUM_THREADS", cpu_threads()))
-    x, wf = cpu_step_inputs()
-    weights = [lib.quantize("q4_0", w) for w in wf]
-    run_cpu_steps(lib, kind, weights, x, 1, threads)
-    one = run_cpu_steps(lib, kind, weights, x, 1, threads)
-    steps = max(1, int(budget_s / max(one, 1e-6)))
-    secs = run_cpu_steps(lib, kind, weights, x, steps, threads)
-    value = steps * step_ops() / secs / 1e9
-    return {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
-            "sample": f"{steps} decode steps (q8_0 quantize + q4_0 1x4096x4096 + 1x11008x4096) in {secs:.2f} s"}
+    threads = cpu_threads() if kind == "reference" else 1
+    w = host_headline_weights(lib)
+    one = cpu_measure(lib, kind, w, 1, cpu_sample_rows(lib, kind, w, 1, 0.3, 3), 5, 4)
+    allt = cpu_measure(lib, kind, w, threads, cpu_sample_rows(lib, kind, w, threads, 0.3, 5), 5, 6) \
+        if threads > 1 else one
+    _, m, n, k = HEADLINE
+    return {
+        "value": allt["value_median"], "unit": UNIT, "cores": threads, "kind": kind,
+        "sample": (f"headline workload q4_0 M={m} N={n} K={k}: {allt['rows']} of the {m} activation rows per sample "
+                   f"(q8_0 quantization of those rows + their dot products with all {n} weight rows), "
+                   f"median of {allt['samples']} samples at {threads} threads; scaled by the ops of the sample"),
+        "one_thread": one, "all_threads": allt, "cpu_model": cpu_model(), "nproc": os.cpu_count(),
+        "code": "bench/llama_reference quantize_row_q8_0 + dot_q4_0_q8_0 (oracle/_ref), element-parallel "
+                "OpenMP over C" if kind == "reference" else "C restatement of bench/llama_reference (oracle)",
+    }
 
 
 def reference_arm(args) -> int:
     world, rank, _ = dist_env()
     if rank != 0:
         return 0
+    import numpy as np
     lib, kind = cpu_library()
-    threads = cpu_threads()
-    x, wf = cpu_step_inputs()
-    weights = [lib.quantize("q4_0", w) for w in wf]
-    run_cpu_steps(lib, kind, weights, x, args.warmup, threads)
-    secs = run_cpu_steps(lib, kind, weights, x, args.steps, threads)
-    value = args.steps * step_ops() / secs / 1e9
+    threads = cpu_threads() if kind == "reference" else 1
+    w = host_headline_weights(lib)
+    rows = cpu_sample_rows(lib, kind, w, threads, 0.25, 5)
+    _, m, n, k = HEADLINE
+    x = np.random.default_rng(6).standard_normal((rows, k), dtype=np.float32)
+    for _ in range(args.warmup):
+        cpu_rows_step(lib, kind, w, x, threads)
+    times = [cpu_rows_step(lib, kind, w, x, threads) for _ in range(args.steps)]
+    ops = 2.0 * rows * n * k
+    total = sum(times)
+    value = args.steps * ops / total / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/int32 dot, fp32 fold",
-        "data": "synthetic: seeded N(0,1) fp32 weights and activations, quantized by the reference quantizers",
-        "config": dict(workload_config(), workload=workload_config()["workload"].replace(
-            "activation quantized on device (fused)", "activation quantized on the host by the reference")),
-        "weight_GBps": args.steps * step_weight_bytes() / secs / 1e9,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8/int32 dot, fp32 fold (q4_0 x q8_0)",
+        "data": "synthetic: seeded N(0,0.02) weights and N(0,1) activations, quantized by the reference quantizers",
+        "config": headline_config(world),
+        "weight_GBps": args.steps * weight_bytes("q4_0", n, k) / total / 1e9,
+        "step_min_ms": min(times) * 1e3, "step_median_ms": statistics.median(times) * 1e3,
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
-                         "sample": f"{args.steps} timed steps of the full workload"},
+                         "sample": f"each step: {rows} of the {m} activation rows (q8_0 quantization + dot products "
+                                   f"with all {n} weight rows), scaled by the ops of the sample",
+                         "cpu_model": cpu_model(), "nproc": os.cpu_count()},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
 
 
-def workload_config(layout: str = "ggml", wtype: str = "q4_0"):
-    if wtype == "q4_0":
-        workload = ("configs[1]: q4_0 x q8_0 decode GEMV, M=1, (N,K) = (4096,4096) + (11008,4096), "
-                    "activation quantized on device (fused)")
-    else:
-        workload = (f"decode GEMV with {wtype} x q8_K weights on the shapes of configs[1] (M=1, (N,K) = (4096,4096) "
-                    "+ (11008,4096), activation quantized on device, fused); not a BASELINE configuration")
+# ====================================================================== GPU
+def headline_config(world: int) -> dict:
+    wtype, m, n, k = HEADLINE
     return {
-        "workload": workload,
-        "m": 1, "n": list(N_DIMS), "k": K_DIM, "weight_type": wtype,
-        "activation_type": "q8_0" if wtype == "q4_0" else "q8_K",
-        "weight_layout": "ggml block_q4_0 rows" if layout == "ggml" else
-                         "q4_0 planar rows (same bytes, repacked once on the device before timing)",
-        "l2": "inputs larger than L2: weights rotate over copies totalling > 4x the 126 MB L2",
+        "workload": f"configs[4] largest shape: {wtype} x q8_0 prefill GEMM M={m} N={n} K={k} (Llama-2-7B output "
+                    "projection), fp32 activations quantized on the device each step",
+        "m": m, "n": n, "k": k, "weight_type": wtype, "activation_type": "q8_0",
+        "parallelism": "single GPU" if world == 1 else
+        f"weight rows sharded over {world} GPUs (x broadcast as q8_0 by NCCL, C all-gathered by the matmul over "
+        "NVLink peer stores)",
+        "l2": "inputs larger than L2: (W, x) copies totalling > 4x the 126 MB L2 rotate; every step writes C (262 MB)",
     }
 
 
-# ------------------------------------------------------------------ GPU arm
-def ours(args) -> int:
-    import torch
-    import pfng_b200 as pb
-
-    world, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import torch.distributed as dist
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
-
-    stream = torch.cuda.Stream()
-    torch.cuda.set_stream(stream)  # graph capture needs a non-default stream
-    wtype = args.wtype
-    copies = max(2, -(-4 * L2_BYTES // step_weight_bytes(wtype)))
-    gen = torch.Generator(device="cuda").manual_seed(1 + rank)
-    planar = args.layout == "planar"
-    if planar and wtype != "q4_0":
-        raise SystemExit("--layout planar applies to q4_0 weights")
-    wt = pb.Q4_0_PLANAR if planar else pb.WTYPES[wtype]
-    weights = []
-    for _ in range(copies):
-        per = []
-        for n in N_DIMS:
-            q = make_weights_device(pb, torch, wtype, n, K_DIM, gen)
-            # planar: the one-time repack a reference adapter does in prepare
-            per.append(pb.pack_q4_0_planar(q, n, K_DIM) if planar else q)
-            del q
-        weights.append(per)
-    x = torch.randn((1, K_DIM), generator=torch.Generator(device="cuda").manual_seed(2), device="cuda")
-    outs = [torch.empty((1, n), device="cuda") for n in N_DIMS]
-    ws = torch.empty(max(1, pb.compute_workspace_size(pb.Q4_0, 1, max(N_DIMS), K_DIM)), dtype=torch.uint8,
-                     device="cuda")
-    torch.cuda.synchronize()
-
-    # The weights are constant, so consecutive steps may overlap: each launch
-    # starts streaming its weights while the previous one drains
-    # (PFNG_B200_OVERLAP_WEIGHTS); activations and outputs stay ordered.
-    calls = [pb.GroupedCall(wt, weights[r], N_DIMS, outs, x, overlap_weights=True) for r in range(copies)]
-
-    def step(i: int, xin=None):
-        calls[i % copies](x=xin, stream=stream)
-
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-
-    # warm-up (also loads the kernels)
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize()
-
-    # ---- device-resident timing: capture the K steps in one CUDA graph
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        for i in range(args.steps):
-            step(i)
-    graph.replay()  # warm the graph once
-    torch.cuda.synchronize()
-    barrier()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(torch.cuda.current_device()) as clocks:
-        torch.cuda.synchronize()
-        barrier()
-        start.record(stream)
-        graph.replay()
-        end.record(stream)
-        torch.cuda.synchronize()
-        barrier()
-    elapsed = start.elapsed_time(end) / 1e3
-    clock_info = clocks.summary()
-    elapsed_max = elapsed
-    if dist is not None:
-        t = torch.tensor([elapsed], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_max = float(t.item())
-    pb.check_kernel_error()
-
-    # ---- per-launch duration of the GEMV kernel: the timed region above is
-    # exactly K back-to-back launches of it on one stream (CUDA events on
-    # that stream), so its average launch duration is elapsed / K.
-    avg_launch = elapsed / args.steps
-    bytes_launch = step_weight_bytes(wtype) + K_DIM * 4 + sum(N_DIMS) * 4
-
-    # ---- end to end through the public API with host buffers.  Every step
-    # copies its activation row from pinned host memory, runs the grouped
-    # launch and reads its outputs (one contiguous [1][sum N] buffer) back to
-    # pinned host memory, all on the launching stream; the K steps are
-    # captured in one CUDA graph like the device-resident timing above (as a
-    # decode loop would be), so the copies cost their transfer and latency,
-    # not a host launch each.
-    x_host = x.cpu().pin_memory()
-    x_dev = torch.empty_like(x)
-    out_dev = torch.empty((1, sum(N_DIMS)), device="cuda")
-    out_host = torch.empty((1, sum(N_DIMS)), pin_memory=True)
-    cols, o = [], 0
-    for n in N_DIMS:
-        cols.append(out_dev[:, o:o + n])
-        o += n
-    e2e_calls = [pb.GroupedCall(wt, weights[r], N_DIMS, cols, x_dev, overlap_weights=True) for r in range(copies)]
-
-    def e2e_step(i):
-        x_dev.copy_(x_host, non_blocking=True)
-        e2e_calls[i % copies](stream=stream)
-        out_host.copy_(out_dev, non_blocking=True)
-
-    for i in range(args.warmup):
-        e2e_step(i)
-    torch.cuda.synchronize()
-    e2e_graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(e2e_graph, stream=stream):
-        for i in range(args.steps):
-            e2e_step(i)
-    e2e_graph.replay()
-    torch.cuda.synchronize()
-    barrier()
-    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_start.record(stream)
-    e2e_graph.replay()
-    e_end.record(stream)
-    torch.cuda.synchronize()
-    del e2e_graph
-    e2e_elapsed = e_start.elapsed_time(e_end) / 1e3
-    if dist is not None:
-        t = torch.tensor([e2e_elapsed], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_elapsed = float(t.item())
-    pb.check_kernel_error()
-
-    del graph
-    peak, peak_kind = measured_peaks()
-    if rank == 0:
-        value = world * args.steps * step_ops() / elapsed_max / 1e9
-        achieved = bytes_launch / avg_launch / 1e9
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": elapsed_max / args.steps * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
-            "dtype": f"int8/int32 dot, fp32 fold ({wtype} x {'q8_0' if wtype == 'q4_0' else 'q8_K'})",
-            "data": "synthetic: seeded N(0,1) fp32 weights (quantized on device) and activations"
-                    if wtype != "iq2_xxs" else "synthetic: seeded iq2_xxs blocks (uniform indices, signs, scales) "
-                    "and N(0,1) activations",
-            "config": dict(workload_config(args.layout, wtype),
-                           parallelism=f"replicas x{world}" if world > 1 else "single GPU",
-                           weight_copies=copies, weight_bytes_resident=copies * step_weight_bytes(wtype)),
-            "weight_GBps": world * args.steps * step_weight_bytes(wtype) / elapsed_max / 1e9,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak,
-                         "traffic": profile_traffic("gemv_q4_0_planar_decode") if planar
-                         else profile_traffic("gemv_q4_0_decode") if wtype == "q4_0"
-                         else profile_traffic("gemv_k_types_decode", wtype),
-                         "kernel": f"gemv_kernel<{'q4_0 planar' if planar else wtype}, m=1, fp32 activations>, "
-                                   "both matrices in one launch",
-                         "bytes_per_launch": bytes_launch, "avg_launch_us": avg_launch * 1e6,
-                         "timing": "CUDA events around K back-to-back launches on the launching stream, / K",
-                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
-                         else "fallback 6.65 TB/s"},
-            "clocks": clock_info,
-            "e2e": {"value": world * args.steps * step_ops() / e2e_elapsed / 1e9, "unit": UNIT,
-                    "h2d_bytes_per_step": K_DIM * 4, "d2h_bytes_per_step": sum(N_DIMS) * 4,
-                    "api": "pfng_b200_compute_grouped (overlapped launches) with pinned host activations in and "
-                   "host C out every step, the K steps captured in one CUDA graph"},
-            "gpu_launches": args.steps,
-        }
-        if not args.no_cpu_baseline and wtype == "q4_0":
-            line["cpu_baseline"] = cpu_baseline()
-        print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0
-
-
-
-# ------------------------------------------------------- other BASELINE configs
 def make_weights_device(pb, torch, wtype: str, n: int, k: int, gen, std: float = 1.0):
     """Seeded synthetic weights on the device in the ggml layout of `wtype`."""
     if wtype == "q4_0":
@@ -417,232 +299,422 @@ def make_weights_device(pb, torch, wtype: str, n: int, k: int, gen, std: float =
     return blocks.reshape(-1).contiguous()
 
 
-def weight_bytes(wtype: str, n: int, k: int) -> int:
-    return n * (k // 32 * 18 if wtype == "q4_0" else k // 256 * (144 if wtype == "q4_K" else 66))
+class Ctx:
+    """Per-process state: torch, the binding, the process group and the stream."""
 
+    def __init__(self):
+        import torch
+        import pfng_b200 as pb
+        self.torch, self.pb = torch, pb
+        self.world, self.rank, self.local = dist_env()
+        torch.cuda.set_device(self.local)
+        self.dist = None
+        if self.world > 1:
+            import torch.distributed as dist
+            from datetime import timedelta
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+            self.dist = dist
+        self.stream = torch.cuda.Stream()
+        torch.cuda.set_stream(self.stream)
 
-def int8_peak_tops():
-    path = ROOT / "MEASURED_PEAKS.json"
-    if path.exists():
-        return 2.0 * float(json.loads(path.read_text())["bf16_tflops"]), "2x measured bf16 GEMM (MEASURED_PEAKS.json)"
-    return 2.0 * 1590.0, "2x fallback bf16 1.59 PFLOP/s"
+    def barrier(self):
+        if self.dist is not None:
+            self.dist.barrier()
 
+    def max_over_ranks(self, t: float) -> float:
+        if self.dist is None:
+            return t
+        v = self.torch.tensor([t], device="cuda", dtype=self.torch.float64)
+        self.dist.all_reduce(v, op=self.dist.ReduceOp.MAX)
+        return float(v.item())
 
-def time_graph(torch, stream, fn, steps: int, warmup: int) -> float:
-    for i in range(warmup):
-        fn(i)
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        for i in range(steps):
+    def timed(self, fn, steps: int, warmup: int, repeats: int) -> list[float]:
+        """Seconds of `repeats` timed regions of `steps` calls of fn(i), each
+        bracketed by barrier + synchronize, CUDA events on the stream, max over ranks."""
+        torch = self.torch
+        for i in range(warmup):
             fn(i)
-    graph.replay()
-    torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(stream)
-    graph.replay()
-    b.record(stream)
-    torch.cuda.synchronize()
-    del graph
-    return a.elapsed_time(b) / 1e3
+        torch.cuda.synchronize()
+        out = []
+        for _ in range(repeats):
+            self.barrier()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(self.stream)
+            for i in range(steps):
+                fn(i)
+            b.record(self.stream)
+            torch.cuda.synchronize()
+            self.barrier()
+            out.append(self.max_over_ranks(a.elapsed_time(b) / 1e3))
+        return out
+
+    def timed_graph(self, fn, steps: int, warmup: int, repeats: int) -> list[float]:
+        """timed() with the `steps` calls captured in one CUDA graph (single-GPU small shapes)."""
+        torch = self.torch
+        for i in range(warmup):
+            fn(i)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=self.stream):
+            for i in range(steps):
+                fn(i)
+        graph.replay()
+        torch.cuda.synchronize()
+        out = []
+        for _ in range(repeats):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(self.stream)
+            graph.replay()
+            b.record(self.stream)
+            torch.cuda.synchronize()
+            out.append(a.elapsed_time(b) / 1e3)
+        del graph
+        return out
 
 
-def prefill(args) -> int:
-    """configs[0] / [2] / [3]: one C = quantize(x) . W^T, M=480 N=1536 K=1536, on one GPU."""
-    import torch
-    import pfng_b200 as pb
-    torch.cuda.set_device(0)
-    stream = torch.cuda.Stream()
-    torch.cuda.set_stream(stream)
-    m, n, k = args.m, args.n, args.k
-    gen = torch.Generator(device="cuda").manual_seed(1)
-    per = weight_bytes(args.wtype, n, k) + m * k * 4
-    copies = max(2, -(-4 * L2_BYTES // per))
-    ws_ = [make_weights_device(pb, torch, args.wtype, n, k, gen) for _ in range(copies)]
-    xs = [torch.randn((m, k), generator=gen, device="cuda") for _ in range(copies)]
-    if args.out == "f32":
-        out = torch.empty((m, n), device="cuda")
-        wsp = torch.empty(max(1, pb.compute_workspace_size(args.wtype, m, n, k)), dtype=torch.uint8, device="cuda")
-        step = lambda i: pb.compute(args.wtype, ws_[i % copies], xs[i % copies], n, out=out, workspace=wsp,
-                                    stream=stream)
+class ShardedStep:
+    """One step of the sharded product on this rank: x (rank 0) -> q8_0 ->
+    broadcast -> this rank's columns of C into every rank's full C -> barrier."""
+
+    def __init__(self, ctx: Ctx, m: int, n: int, k: int, nbuf: int = 1):
+        pb, torch = ctx.pb, ctx.torch
+        self.ctx, self.m, self.n, self.k = ctx, m, n, k
+        self.b, self.e = pb.shard_rows(n, ctx.world, ctx.rank, GRANULE)
+        self.gcs = [pb.GatheredC(m, n) for _ in range(nbuf)]
+        self.aq = torch.empty(m * (k // 32) * pb.Q8_0_BYTES, dtype=torch.uint8, device="cuda")
+        self.ws = torch.empty(max(1, pb.mm_workspace_size("q4_0", m, max(self.e - self.b, 1), k)),
+                              dtype=torch.uint8, device="cuda")
+        self.flag = torch.zeros(1, device="cuda")
+        self.dsts = [gc.destinations(self.b) for gc in self.gcs]
+
+    def __call__(self, w, x, buf: int = 0):
+        ctx, pb = self.ctx, self.ctx.pb
+        if ctx.rank == 0:
+            pb.quantize_q8_0(x, out=self.aq, stream=ctx.stream)
+        ctx.dist.broadcast(self.aq, src=0)
+        if self.e > self.b:
+            pb.mm_gather("q4_0", w, self.aq, self.m, self.e - self.b, self.k, self.dsts[buf], self.n,
+                         workspace=self.ws, stream=ctx.stream)
+        ctx.dist.all_reduce(self.flag)
+
+    def c(self, buf: int = 0):
+        return self.gcs[buf].tensor()
+
+    def close(self):
+        self.ctx.torch.cuda.synchronize()
+        for gc in self.gcs:
+            gc.close()
+
+
+def launches_per_step(world: int, rank: int) -> int:
+    """Kernels of this library one headline step launches on this rank."""
+    if world == 1:
+        return 2  # activation quantizer (split operand), GEMM
+    return (1 if rank == 0 else 0) + 3  # q8_0 quantizer on rank 0; q8_0 -> operand, GEMM, peer-store copies
+
+
+def headline(ctx: Ctx, args) -> dict:
+    torch, pb = ctx.torch, ctx.pb
+    wtype, m, n, k = HEADLINE
+    b, e = pb.shard_rows(n, ctx.world, ctx.rank, GRANULE)
+    ns = max(e - b, 1)
+    per_copy = weight_bytes(wtype, ns, k) + m * k * 4
+    copies = max(2, -(-4 * L2_BYTES // per_copy))
+    gen = torch.Generator(device="cuda").manual_seed(1000 + ctx.rank)
+    gx = torch.Generator(device="cuda").manual_seed(7)
+    W = [make_weights_device(pb, torch, wtype, ns, k, gen, 0.02) for _ in range(copies)]
+    X = [torch.randn((m, k), generator=gx, device="cuda") for _ in range(copies)]
+    torch.cuda.synchronize()
+
+    # ---- device-resident step (value)
+    sharded = None
+    if ctx.world == 1:
+        C = torch.empty((m, n), device="cuda")
+        ws = torch.empty(max(1, pb.compute_workspace_size(wtype, m, n, k)), dtype=torch.uint8, device="cuda")
+
+        def step(i):
+            pb.compute(wtype, W[i % copies], X[i % copies], n, out=C, workspace=ws, stream=ctx.stream)
     else:
-        # the result in another format, converted in the GEMM's epilogue
-        out = pb._out_tensor(pb.OUT_FORMATS[args.out], m, n, "cuda")
-        wsp = torch.empty(max(1, pb.lib().pfng_b200_compute_out_workspace_size(
-            pb._wt(args.wtype), pb.OUT_FORMATS[args.out], m, n, k, 0)), dtype=torch.uint8, device="cuda")
-        step = lambda i: pb.compute_out(args.wtype, ws_[i % copies], xs[i % copies], n, args.out, out=out,
-                                        workspace=wsp, stream=stream)
+        sharded = ShardedStep(ctx, m, n, k, nbuf=2)
+
+        def step(i):
+            sharded(W[i % copies], X[i % copies], 0)
+
     with ClockSampler(torch.cuda.current_device()) as clocks:
-        elapsed = time_graph(torch, stream, step, args.steps, args.warmup)
+        reps = ctx.timed(step, args.steps, args.warmup, args.repeats)
+    ctx.pb.check_kernel_error()
+    clock_info = clocks.summary()
+
+    # ---- the GEMM kernel alone (roofline): K launches on prepared activations
+    prep = [pb.prepare_activations(wtype, X[i]) for i in range(copies)]
+    Cl = torch.empty((m, ns), device="cuda")
+    kws = torch.empty(max(1, pb.mm_prepared_workspace_size(wtype, m, ns, k)), dtype=torch.uint8, device="cuda")
+
+    def kstep(i):
+        pb.mm_prepared(wtype, W[i % copies], prep[i % copies], m, ns, k, out=Cl, workspace=kws, stream=ctx.stream)
+
+    kreps = ctx.timed(kstep, args.steps, args.warmup, args.repeats)
     pb.check_kernel_error()
+    del prep, Cl
+
+    # ---- end to end: host x in, host C out, copies overlapped with compute
+    e2e_reps, h2d, d2h = e2e_headline(ctx, args, W, X[0], sharded)
+    if sharded is not None:
+        sharded.close()
+    del W, X
+    torch.cuda.empty_cache()
+
     ops = 2.0 * m * n * k
-    peak, peak_src = int8_peak_tops()
-    achieved = ops / (elapsed / args.steps) / 1e12
-    print(json.dumps({
-        "metric": METRIC, "workload": f"{args.wtype} GEMM M={m} N={n} K={k} (quantize x + matmul, one step)"
-                                      + ("" if args.out == "f32" else f", output {args.out} (fused epilogue)"),
-        "value": args.steps * ops / elapsed / 1e9, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
-        "warmup": args.warmup, "us_per_step": elapsed / args.steps * 1e6,
-        "weight_GBps": args.steps * weight_bytes(args.wtype, n, k) / elapsed / 1e9,
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s",
-                     "frac": achieved / peak, "peak_source": peak_src},
-        "clocks": clocks.summary(), "l2": f"{copies} rotating (W, x) copies > 4x L2",
-    }), flush=True)
+    t_step = statistics.median(reps)
+    t_kernel = statistics.median(kreps)
+    pk = peaks()
+    achieved = 2.0 * m * ns * k / (t_kernel / args.steps) / 1e12
+    traffic = ncu_traffic("gemm_q4_0_m2048_n32000_k4096") if ctx.world == 1 else None
+    return {
+        "value": args.steps * ops / t_step / 1e9, "ms_per_step": t_step / args.steps * 1e3,
+        "ms_per_step_min": min(reps) / args.steps * 1e3, "ms_per_step_median": t_step / args.steps * 1e3,
+        "repeats": args.repeats, "weight_GBps": args.steps * weight_bytes(wtype, n, k) / t_step / 1e9,
+        "clocks": clock_info, "copies": copies,
+        "roofline": {
+            "bound": "tensor", "achieved": achieved, "peak": pk["int8_tops"], "unit": "TFLOP/s",
+            "frac": achieved / pk["int8_tops"], "traffic": traffic,
+            "kernel": "gemm_kernel (q4_0 x q8_0, int8 mma.sync m16n8k32, 128x128 tiles, direct B fragments)"
+                      if not os.environ.get("PFNG_B200_GEMM") else f"GEMM ({os.environ['PFNG_B200_GEMM']})",
+            "flops_per_launch": 2.0 * m * ns * k, "avg_launch_us": t_kernel / args.steps * 1e6,
+            "timing": "CUDA events around K back-to-back pfng_b200_mm_prepared launches on the launching "
+                      "stream (median of repeats), / K; max over ranks",
+            "peak_source": pk["source"] + "; TFLOP/s here counts int8 ops (2 per MAC)",
+            "traffic_source": "profiles/ncu_traffic.json (dram__bytes_read.sum + dram__bytes_write.sum, one launch)"
+            if traffic is not None else None,
+        },
+        "e2e": {"value": args.steps * ops / statistics.median(e2e_reps) / 1e9, "unit": UNIT,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": statistics.median(e2e_reps) / args.steps * 1e3,
+                "api": "pfng_b200_compute_q4_0" if ctx.world == 1 else
+                "pfng_b200_quantize_q8_0 (rank 0) + NCCL broadcast + pfng_b200_mm_gather + NCCL all-reduce",
+                "copies": "pinned host x -> device every step and device C -> pinned host every step (each rank "
+                          "its row band of the gathered C), on two more streams overlapping the previous / next "
+                          "step's compute; double-buffered device x and C"},
+        "gpu_launches": launches_per_step(ctx.world, ctx.rank) * args.steps,
+    }
+
+
+def e2e_headline(ctx: Ctx, args, W, x0, sharded):
+    """Timed repeats of K pipelined steps with host x in and host C out; returns (seconds list, h2d, d2h)."""
+    torch, pb = ctx.torch, ctx.pb
+    wtype, m, n, k = HEADLINE
+    copies = len(W)
+    r0, r1 = (0, m) if ctx.world == 1 else (ctx.rank * m // ctx.world, (ctx.rank + 1) * m // ctx.world)
+    x_host = x0.cpu().pin_memory()
+    xd = [torch.empty_like(x0) for _ in range(2)]
+    if ctx.world == 1:
+        cd = [torch.empty((m, n), device="cuda") for _ in range(2)]
+        ws = torch.empty(max(1, pb.compute_workspace_size(wtype, m, n, k)), dtype=torch.uint8, device="cuda")
+    c_host = torch.empty((r1 - r0, n), pin_memory=True)
+    s_h2d, s_d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    ev = {name: [torch.cuda.Event() for _ in range(2)] for name in ("x_ready", "x_free", "c_ready", "c_free")}
+    loads_x = ctx.world == 1 or ctx.rank == 0
+
+    def band(bi):
+        return cd[bi][r0:r1] if ctx.world == 1 else sharded.c(bi)[r0:r1]
+
+    def step(i):
+        bi = i % 2
+        with torch.cuda.stream(s_h2d):
+            if i >= 2:
+                s_h2d.wait_event(ev["x_free"][bi])
+            if loads_x:
+                xd[bi].copy_(x_host, non_blocking=True)
+            ev["x_ready"][bi].record(s_h2d)
+        ctx.stream.wait_event(ev["x_ready"][bi])
+        if i >= 2:
+            ctx.stream.wait_event(ev["c_free"][bi])
+        if ctx.world == 1:
+            pb.compute(wtype, W[i % copies], xd[bi], n, out=cd[bi], workspace=ws, stream=ctx.stream)
+        else:
+            sharded(W[i % copies], xd[bi], bi)
+        ev["x_free"][bi].record(ctx.stream)
+        ev["c_ready"][bi].record(ctx.stream)
+        with torch.cuda.stream(s_d2h):
+            s_d2h.wait_event(ev["c_ready"][bi])
+            c_host.copy_(band(bi), non_blocking=True)
+            ev["c_free"][bi].record(s_d2h)
+
+    def run(steps):
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(ctx.stream)
+        s_h2d.wait_event(t0)
+        s_d2h.wait_event(t0)
+        for i in range(steps):
+            step(i)
+        for bi in range(min(2, steps)):
+            ctx.stream.wait_event(ev["c_free"][bi])
+        t1.record(ctx.stream)
+        return t0, t1
+
+    run(args.warmup)
+    torch.cuda.synchronize()
+    reps = []
+    for _ in range(max(1, min(args.repeats, 3))):
+        ctx.barrier()
+        torch.cuda.synchronize()
+        t0, t1 = run(args.steps)
+        torch.cuda.synchronize()
+        ctx.barrier()
+        reps.append(ctx.max_over_ranks(t0.elapsed_time(t1) / 1e3))
+    pb.check_kernel_error()
+    del xd, c_host
+    return reps, m * k * 4, m * n * 4
+
+
+# ---------------------------------------------------------------- the sweep
+def sweep_small(ctx: Ctx, args, wtype: str, m: int, n: int, k: int, std: float = 1.0) -> dict:
+    """One single-GPU configuration through pfng_b200_compute_*, K steps in a CUDA graph."""
+    torch, pb = ctx.torch, ctx.pb
+    gen = torch.Generator(device="cuda").manual_seed(1)
+    per = weight_bytes(wtype, n, k) + m * k * 4
+    copies = max(2, -(-4 * L2_BYTES // per))
+    Ws = [make_weights_device(pb, torch, wtype, n, k, gen, std) for _ in range(copies)]
+    Xs = [torch.randn((m, k), generator=gen, device="cuda") for _ in range(copies)]
+    out = torch.empty((m, n), device="cuda")
+    wsp = torch.empty(max(1, pb.compute_workspace_size(wtype, m, n, k)), dtype=torch.uint8, device="cuda")
+    reps = ctx.timed_graph(lambda i: pb.compute(wtype, Ws[i % copies], Xs[i % copies], n, out=out, workspace=wsp,
+                                                stream=ctx.stream), args.steps, args.warmup, args.repeats)
+    pb.check_kernel_error()
+    t = statistics.median(reps) / args.steps
+    ops = 2.0 * m * n * k
+    return {"us_per_step": t * 1e6, "us_per_step_min": min(reps) / args.steps * 1e6, "value": ops / t / 1e9,
+            "frac_int8_peak": ops / t / 1e12 / peaks()["int8_tops"],
+            "weight_GBps": weight_bytes(wtype, n, k) / t / 1e9}
+
+
+def sweep_decode(ctx: Ctx, args) -> dict:
+    """x [1][4096] quantized in the GEMV launch, both q4_0 matrices in one launch."""
+    torch, pb = ctx.torch, ctx.pb
+    step_w = sum(weight_bytes("q4_0", n, DECODE_K) for n in DECODE_NS)
+    copies = max(2, -(-4 * L2_BYTES // step_w))
+    gen = torch.Generator(device="cuda").manual_seed(1)
+    weights = [[make_weights_device(pb, torch, "q4_0", n, DECODE_K, gen) for n in DECODE_NS] for _ in range(copies)]
+    x = torch.randn((1, DECODE_K), generator=torch.Generator(device="cuda").manual_seed(2), device="cuda")
+    outs = [torch.empty((1, n), device="cuda") for n in DECODE_NS]
+    calls = [pb.GroupedCall("q4_0", weights[r], DECODE_NS, outs, x, overlap_weights=True) for r in range(copies)]
+    reps = ctx.timed_graph(lambda i: calls[i % copies](stream=ctx.stream), args.steps, args.warmup, args.repeats)
+    pb.check_kernel_error()
+    t = statistics.median(reps) / args.steps
+    launch_bytes = step_w + DECODE_K * 4 + sum(DECODE_NS) * 4
+    ops = sum(2.0 * n * DECODE_K for n in DECODE_NS)
+    pk = peaks()
+    return {"workload": "configs[1]: q4_0 decode GEMV M=1, (N,K) = (4096,4096) + (11008,4096), x quantized in the "
+                        "same launch (pfng_b200_compute_grouped, overlapped launches, K steps in a CUDA graph)",
+            "us_per_step": t * 1e6, "us_per_step_min": min(reps) / args.steps * 1e6, "value": ops / t / 1e9,
+            "weight_GBps": step_w / t / 1e9, "hbm_GBps": launch_bytes / t / 1e9,
+            "frac_hbm": launch_bytes / t / 1e9 / pk["hbm_gbs"], "bytes_per_launch": launch_bytes,
+            "traffic": ncu_traffic("gemv_q4_0_decode"), "copies": copies}
+
+
+def sweep_sharded(ctx: Ctx, args, m: int, n: int, k: int) -> dict:
+    """A configs[4] shape under N GPUs: the sharded step (broadcast + matmul with fused gather)."""
+    torch, pb = ctx.torch, ctx.pb
+    step = ShardedStep(ctx, m, n, k)
+    ns = max(step.e - step.b, 1)
+    gen = torch.Generator(device="cuda").manual_seed(1000 + ctx.rank)
+    per = weight_bytes("q4_0", ns, k) + m * k * 4
+    copies = max(2, -(-4 * L2_BYTES // per))
+    Ws = [make_weights_device(pb, torch, "q4_0", ns, k, gen, 0.02) for _ in range(copies)]
+    x = torch.randn((m, k), generator=torch.Generator(device="cuda").manual_seed(7), device="cuda")
+    reps = ctx.timed(lambda i: step(Ws[i % copies], x), args.steps, args.warmup, args.repeats)
+    # the local GEMM alone
+    C = torch.empty((m, ns), device="cuda")
+    wsp = torch.empty(max(1, pb.compute_workspace_size("q4_0", m, ns, k)), dtype=torch.uint8, device="cuda")
+    creps = ctx.timed(lambda i: pb.compute("q4_0", Ws[i % copies], x, ns, out=C, workspace=wsp, stream=ctx.stream),
+                      args.steps, args.warmup, args.repeats)
+    pb.check_kernel_error()
+    step.close()
+    t, tc = statistics.median(reps) / args.steps, statistics.median(creps) / args.steps
+    ops = 2.0 * m * n * k
+    return {"us_per_step": t * 1e6, "value": ops / t / 1e9, "us_per_step_compute_only": tc * 1e6,
+            "frac_int8_peak_compute": 2.0 * m * ns * k / tc / 1e12 / peaks()["int8_tops"], "rows_per_rank": ns}
+
+
+def sweep(ctx: Ctx, args) -> dict:
+    out = {}
+    if ctx.world == 1:
+        for name, wtype in SMALL_CONFIGS:
+            out[f"{name} {wtype} 480x1536x1536"] = sweep_small(ctx, args, wtype, 480, 1536, 1536)
+        out["configs[1] decode"] = sweep_decode(ctx, args)
+    for m in LLAMA_MS:
+        for n, k in LLAMA_NK:
+            key = f"configs[4] q4_0 {m}x{n}x{k}"
+            out[key] = sweep_small(ctx, args, "q4_0", m, n, k, 0.02) if ctx.world == 1 else \
+                sweep_sharded(ctx, args, m, n, k)
+            ctx.torch.cuda.empty_cache()
+    return out
+
+
+def ours(args) -> int:
+    ctx = Ctx()
+    h = headline(ctx, args)
+    sw = sweep(ctx, args) if not args.no_sweep else None
+    if ctx.rank == 0:
+        wtype, m, n, k = HEADLINE
+        line = {
+            "metric": METRIC, "value": h["value"], "unit": UNIT, "n_gpus": ctx.world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": h["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8/int32 dot, fp32 fold (q4_0 x q8_0)",
+            "data": "synthetic: seeded N(0,0.02) fp32 weights (quantized to q4_0 on the device) and N(0,1) fp32 "
+                    "activations, the distributions BASELINE.json names for configs[4]",
+            "config": dict(headline_config(ctx.world), weight_copies=h["copies"]),
+            "weight_GBps": h["weight_GBps"], "ms_per_step_min": h["ms_per_step_min"],
+            "ms_per_step_median": h["ms_per_step_median"], "repeats": h["repeats"],
+            "roofline": h["roofline"], "clocks": h["clocks"], "e2e": h["e2e"], "gpu_launches": h["gpu_launches"],
+        }
+        if sw is not None:
+            line["sweep"] = sw
+        if ctx.world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline()
+        print(json.dumps(line), flush=True)
+    if ctx.dist is not None:
+        ctx.dist.barrier()
+        ctx.dist.destroy_process_group()
     return 0
 
 
-LLAMA_SHAPES = [(nn, kk) for nn, kk in ((4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096))]
-
-
-def llama(args) -> int:
-    """Llama-2-7B q4_0 prefill shapes, weight rows sharded over the ranks, x quantized on
-    rank 0 and broadcast as q8_0, each rank's output columns stored into every rank's C by its matmul
-    (pfng_b200_mm_gather); the NCCL all-gather variant is timed beside it.  One JSON line per shape."""
-    import torch
-    import pfng_b200 as pb
-    world, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import torch.distributed as dist
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
-    stream = torch.cuda.Stream()
-    torch.cuda.set_stream(stream)
-    granule = 128
-    ms = [args.m] if args.m_given else [32, 512, 2048]
-    for m in ms:
-        for n, k in LLAMA_SHAPES:
-            b, e = pb.shard_rows(n, world, rank, granule)
-            width = max(pb.shard_rows(n, world, r, granule)[1] - pb.shard_rows(n, world, r, granule)[0]
-                        for r in range(world))
-            gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
-            per = weight_bytes("q4_0", max(e - b, 1), k) + m * k * 4
-            copies = max(2, -(-4 * L2_BYTES // per))
-            wsh = [make_weights_device(pb, torch, "q4_0", max(e - b, 1), k, gen, 0.02) for _ in range(copies)]
-            x = torch.randn((m, k), generator=torch.Generator(device="cuda").manual_seed(7), device="cuda")
-            slice_ = torch.zeros((m, width), device="cuda")
-            gathered = torch.empty((world, m, width), device="cuda")
-            full = torch.empty((m, n), device="cuda")
-            wsp = torch.empty(max(1, pb.compute_workspace_size("q4_0", m, width, k)), dtype=torch.uint8,
-                              device="cuda")
-
-            def local_gemm(i):
-                if e > b:
-                    pb.compute("q4_0", wsh[i % copies], x, e - b, out=slice_[:, : e - b], workspace=wsp,
-                               stream=stream)
-
-            def full_step(i):
-                if dist is not None:
-                    dist.broadcast(x, src=0)
-                local_gemm(i)
-                if dist is not None:
-                    dist.all_gather_into_tensor(gathered, slice_)
-                    pb.unshard_columns(gathered, m, n, world, granule, out=full, stream=stream)
-                else:
-                    full.copy_(slice_[:, :n])
-
-            # the all-gather fused into the GEMM: every rank's epilogue stores
-            # its columns into every rank's full C over NVLink (CUDA IPC);
-            # a one-element all-reduce after it orders the ranks
-            # rank 0 quantizes x and broadcasts the q8_0 bytes (1.06 bytes per
-            # value instead of 4); a one-element all-reduce after the matmul
-            # orders the ranks
-            gc = pb.GatheredC(m, n) if dist is not None else None
-            dsts = gc.destinations(b) if gc is not None else [full]
-            flag = torch.zeros(1, device="cuda")
-            aq = torch.empty(m * (k // 32) * pb.Q8_0_BYTES, dtype=torch.uint8, device="cuda")
-            wsm = torch.empty(max(1, pb.mm_workspace_size("q4_0", m, width, k)), dtype=torch.uint8, device="cuda")
-
-            def fused_step(i):
-                if rank == 0:
-                    pb.quantize_q8_0(x, out=aq, stream=stream)
-                if dist is not None:
-                    dist.broadcast(aq, src=0)
-                if e > b:
-                    pb.mm_gather("q4_0", wsh[i % copies], aq, m, e - b, k, dsts, n, workspace=wsm, stream=stream)
-                if dist is not None:
-                    dist.all_reduce(flag)
-
-            def timed(fn):
-                for i in range(args.warmup):
-                    fn(i)
-                torch.cuda.synchronize()
-                if dist is not None:
-                    dist.barrier()
-                a, bb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record(stream)
-                for i in range(args.steps):
-                    fn(i)
-                bb.record(stream)
-                torch.cuda.synchronize()
-                t = a.elapsed_time(bb) / 1e3
-                if dist is not None:
-                    tt = torch.tensor([t], device="cuda", dtype=torch.float64)
-                    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-                    t = float(tt.item())
-                return t
-
-            t_compute = timed(local_gemm)
-            t_nccl = timed(full_step)
-            t_e2e = timed(fused_step)
-            pb.check_kernel_error()
-            if gc is not None:
-                torch.cuda.synchronize()
-                gc.close()
-            if rank == 0:
-                ops = 2.0 * m * n * k
-                peak, peak_src = int8_peak_tops()
-                print(json.dumps({
-                    "metric": METRIC, "workload": f"configs[4] Llama-2-7B q4_0 M={m} N={n} K={k}",
-                    "n_gpus": world, "scaling": "strong", "value": args.steps * ops / t_e2e / 1e9, "unit": UNIT,
-                    "compute_only": args.steps * ops / t_compute / 1e9, "us_per_step_e2e": t_e2e / args.steps * 1e6,
-                    "us_per_step_compute": t_compute / args.steps * 1e6,
-                    "us_per_step_e2e_nccl_all_gather": t_nccl / args.steps * 1e6,
-                    "compute_frac_of_int8_peak": ops / (t_compute / args.steps) / 1e12 / peak,
-                    "peak_source": peak_src, "rows_per_rank": e - b,
-                    "exchange": "x quantized to q8_0 on rank 0 and NCCL-broadcast; each rank's matmul stores its C "
-                    "columns into every rank's C (CUDA IPC over NVLink, pfng_b200_mm_gather); one-element NCCL "
-                    "all-reduce as the completion barrier; us_per_step_e2e_nccl_all_gather: fp32 x broadcast, "
-                    "NCCL all-gather of C slices and a device unshard instead" if world > 1 else "none",
-                }), flush=True)
-            del wsh, gathered, full, slice_
-            torch.cuda.empty_cache()
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+# ------------------------------------------------ single-config dev runs
+def one_config(args) -> int:
+    """--workload prefill/decode: one configuration, printed as its own line (development runs)."""
+    ctx = Ctx()
+    if args.workload == "decode":
+        r = sweep_decode(ctx, args)
+    else:
+        r = sweep_small(ctx, args, args.wtype, args.m, args.n, args.k, 0.02 if args.wtype == "q4_0" else 1.0)
+    print(json.dumps(dict(workload=args.workload, wtype=args.wtype, m=args.m, n=args.n, k=args.k, **r)), flush=True)
     return 0
 
 
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--repeats", type=int, default=5, help="timed regions of K steps (min and median reported)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the timed CPU baseline leg")
-    ap.add_argument("--workload", choices=["decode", "prefill", "llama"], default="decode",
-                    help="decode: configs[1] (the bench line); prefill: configs[0]/[2]/[3]; llama: configs[4]")
+    ap.add_argument("--no-sweep", action="store_true", help="only the headline configuration")
+    ap.add_argument("--workload", choices=["headline", "prefill", "decode"], default="headline",
+                    help="headline: the bench line; prefill / decode: one configuration (development)")
     ap.add_argument("--wtype", choices=["q4_0", "q4_K", "iq2_xxs"], default="q4_0")
-    ap.add_argument("--out", choices=["f32", "f16", "bf16", "q8_0"], default="f32",
-                    help="prefill: format of C, converted in the GEMM's epilogue")
-    ap.add_argument("--layout", choices=["ggml", "planar"], default="ggml",
-                    help="decode: q4_0 weights as ggml blocks or repacked once into the planar row layout")
-    ap.add_argument("--m", type=int, default=None)
+    ap.add_argument("--m", type=int, default=480)
     ap.add_argument("--n", type=int, default=1536)
     ap.add_argument("--k", type=int, default=1536)
     args = ap.parse_args()
-    args.m_given = args.m is not None
-    if args.m is None:
-        args.m = 480
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     if args.impl == "reference":
         return reference_arm(args)
-    if args.workload == "prefill":
-        return prefill(args)
-    if args.workload == "llama":
-        return llama(args)
+    if args.workload != "headline":
+        return one_config(args)
     return ours(args)
 
 

@@ -547,8 +547,7 @@ PFNG_DEV void copy_tile_to_copies(const GemmParams &p) {
 
 template <int WT, class C, bool kPartials, bool kCopies = false, bool kDirect = false>
 __global__ void __launch_bounds__(kThreads, kDirect && (C::BM == 64 || (C::BM == 32 && WT == kWQ4_K)) ? 2 : 1) gemm_kernel(const GemmParams p) {
-    static_assert(!kDirect || ((WT == kWQ4_0 || WT == kWQ4_0P || WT == kWQ4_K) && !kPartials),
-                  "direct operands: q4_0 and q4_K products");
+    static_assert(!kDirect || WT == kWQ4_0 || WT == kWQ4_0P || WT == kWQ4_K, "direct operands: q4_0 and q4_K");
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Smem<C> sm{smem_raw};
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -633,7 +632,10 @@ __global__ void __launch_bounds__(kThreads, kDirect && (C::BM == 64 || (C::BM ==
 #pragma unroll 1
             for (int kb = 0; kb < 8; ++kb) {
                 uint32_t af[MT][4], bf[NT][2];
-                load_frags<C>(at, bt, kb, wm, wn, lane, af, bf);
+                if constexpr (kDirect)
+                    load_frags_direct<WT, C>(smem_u32(at), sm.w_raw(s), kb, fo, wn, g, t4, af, bf);
+                else
+                    load_frags<C>(at, bt, kb, wm, wn, lane, af, bf);
                 const int64_t nb32 = p.k / 32;
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt)
@@ -816,7 +818,7 @@ struct SmemOv {
     }
 };
 
-template <int WT, class C, bool kCopies = false>
+template <int WT, class C, bool kCopies = false, bool kPartials = false>
 __global__ void __launch_bounds__(kThreads) gemm_kernel_ov(const GemmParams p) {
     static_assert(WT != kWQ4_K, "q4_K products run on the two-phase kernel");
     static_assert(C::kSlot == kWRowSlot, "decode_task reads kWRowSlot-byte rows");
@@ -856,7 +858,8 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel_ov(const GemmParams p) {
     for (int a = 0; a < MT; ++a)
 #pragma unroll
         for (int b = 0; b < NT; ++b) acc[a][b][0] = acc[a][b][1] = make_float2(0.0f, 0.0f);
-    const int cin = static_cast<int>(kMagicBits);
+    // partials mode: the plain integer products (no magic offset, no fold)
+    const int cin = kPartials ? 0 : static_cast<int>(kMagicBits);
 
     // prologue: W[0], W[1], then (the kernel is a programmatic dependent of
     // the activation quantizer) wait for the activations and fetch A[0]
@@ -923,12 +926,22 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel_ov(const GemmParams p) {
                 const float2 sv = make_float2(f.x, f.y), cm = make_float2(f.z, f.w);
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt) {
+                    if constexpr (kPartials) {
+                        const int64_t nb32 = p.k / 32;
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const float2 y = make_float2(__int_as_float(res[mt][nt][2 * h]),
-                                                     __int_as_float(res[mt][nt][2 * h + 1]));
-                        const float2 t = ffma2(y, sv, cm);
-                        acc[mt][nt][h] = ffma2(t, make_float2(da[mt][h], da[mt][h]), acc[mt][nt][h]);
+                        for (int i = 0; i < 4; ++i) {
+                            const int64_t r = m0 + wm * C::WM + mt * 16 + g + 8 * (i >> 1);
+                            const int64_t c = n0 + wn * C::WN + nt * 8 + 2 * t4 + (i & 1);
+                            if (r < p.m && c < p.n) p.partials[(r * p.n + c) * nb32 + ks * 8 + kb] = res[mt][nt][i];
+                        }
+                    } else {
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const float2 y = make_float2(__int_as_float(res[mt][nt][2 * h]),
+                                                         __int_as_float(res[mt][nt][2 * h + 1]));
+                            const float2 t = ffma2(y, sv, cm);
+                            acc[mt][nt][h] = ffma2(t, make_float2(da[mt][h], da[mt][h]), acc[mt][nt][h]);
+                        }
                     }
                     if (kb + 1 < 8) mma_s8(res[mt][nt], af[nx][mt], bf[nx][nt][0], bf[nx][nt][1], cin);
                 }
@@ -943,6 +956,7 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel_ov(const GemmParams p) {
         __syncthreads();
     }
 
+    if constexpr (kPartials) return;
     if (p.out_format == kOutQ8_0) {
         epilogue_q8_0<C>(p, smem_raw, acc, m0, n0, tid);
         return;
@@ -1107,9 +1121,9 @@ cudaError_t launch_t(const GemmParams &p, cudaStream_t s) {
     return launch_pdl<C>(kernel, p, smem, s);
 }
 
-template <int WT, class C, bool kCopies = false>
+template <int WT, class C, bool kCopies = false, bool kPartials = false>
 cudaError_t launch_t_ov(const GemmParams &p, cudaStream_t s) {
-    auto kernel = gemm_kernel_ov<WT, C, kCopies>;
+    auto kernel = gemm_kernel_ov<WT, C, kCopies, kPartials>;
     constexpr uint32_t smem = SmemOv<C>::kTotal;
     static_assert(smem <= kMaxSmemPerCta, "dynamic shared memory above the per-CTA limit");
     static_assert(C::BM * (C::BN + 4) * 4 <= smem, "staged C tile of the q8_0 epilogue");
@@ -1125,15 +1139,15 @@ cudaError_t launch_t_ov(const GemmParams &p, cudaStream_t s) {
 }
 
 // The overlapped kernel serves q4_0 (both layouts) and iq2_xxs products
-// without split-K (the partials mode keeps the two-phase kernel);
+// without split-K;
 // PFNG_B200_GEMM_OV=0 selects the two-phase kernel instead (comparisons).
 // Measured on B200 (us per quantize + GEMM step, overlapped vs two-phase):
 // 2048x11008x4096 627 vs 698, 512x4096x4096 66 vs 73, 480x1536x1536 on 64 x 64
 // tiles 20.2 vs 21.3 (q4_0) and 24.6 vs 25.3 (iq2_xxs).  q4_K, whose min term
 // the overlapped kernel adds once per 256-block from the resident A tile, was
 // slower there: 2048x4096x4096 353 vs 338, 512x4096x4096 90.0 vs 85.9.
-template <int WT, bool kPartials>
-constexpr bool kOvType = !kPartials && WT != kWQ4_K;
+template <int WT>
+constexpr bool kOvType = WT != kWQ4_K;
 // Direct operands for every q4_0 tile (both layouts, 16-byte aligned rows);
 // PFNG_B200_GEMM_DIRECT=0 selects the decode pass instead (comparisons).
 // Measured on B200 (us per quantize + GEMM step, direct vs decode pass):
@@ -1158,26 +1172,33 @@ inline bool ov_enabled() {
     return !(e && std::strcmp(e, "0") == 0);
 }
 
+// The partials mode (integer sub-block products instead of C) takes the
+// same kernel as the product of the same shape, so the integers it exports
+// are those the product folds.
 template <int WT, class C, bool kPartials>
 cudaError_t launch_pick(const GemmParams &p, cudaStream_t s) {
     // 32-row tiles keep the two-phase kernel: its two-deep ring fits two CTAs
     // per SM, the overlapped kernel's buffers one (32x32000x4096: 63 vs 74 us)
     // copies (fp32 C to more destinations): the kernels built with the copy
     // pass; with split-K the reduction stores the copies
-    const bool copies = p.ncopies > 0 && p.splits == 1;
-    if constexpr (!kPartials && (WT == kWQ4_0 || WT == kWQ4_0P || WT == kWQ4_K)) {
+    const bool copies = !kPartials && p.ncopies > 0 && p.splits == 1;
+    if constexpr (WT == kWQ4_0 || WT == kWQ4_0P || WT == kWQ4_K) {
         // 176-byte row slots (44 words): the eight rows of a fragment read
         // start on banks 12 r mod 32, so with the four t4 words they hit
         // all 32 banks (160-byte slots: rows r and r + 4 collide).  q4_K
         // keeps 160-byte slots: its full layout (fold data, mins) with
         // 176-byte rows would pass the per-CTA limit on 128 x 128 tiles.
         using D = Cfg<C::BM, C::BN, C::ST, WT == kWQ4_K ? kWRowSlot : 176u>;
-        if ((WT == kWQ4_0P || p.w_vec16) && direct_enabled())
+        if ((WT == kWQ4_0P || p.w_vec16) && direct_enabled()) {
+            if constexpr (kPartials) return launch_t<WT, D, true, false, true>(p, s);
             return copies ? launch_t<WT, D, false, true, true>(p, s) : launch_t<WT, D, false, false, true>(p, s);
+        }
     }
-    if constexpr (kOvType<WT, kPartials> && C::BM > 32) {
-        if (p.splits == 1 && ov_enabled())
+    if constexpr (kOvType<WT> && C::BM > 32) {
+        if (p.splits == 1 && ov_enabled()) {
+            if constexpr (kPartials) return launch_t_ov<WT, C, false, true>(p, s);
             return copies ? launch_t_ov<WT, C, true>(p, s) : launch_t_ov<WT, C>(p, s);
+        }
     }
     if constexpr (!kPartials) {
         if (copies) return launch_t<WT, C, false, true>(p, s);
@@ -1292,11 +1313,11 @@ cudaError_t launch_tile(GemmParams &p, cudaStream_t s) {
     const int64_t sms = device_sm_count();
     const TileKind t = tile_choice(p.m, p.n, sms);
     const int64_t kt = p.k / BK;
+    // the partials mode splits like the product (each CTA exports the
+    // partials of its k range; nothing to reduce)
     p.splits = 1;
-    if constexpr (!kPartials) {
-        const int sp = splits_for(t, p.m, p.n, p.k, sms);
-        if (sp > 1 && p.partial) p.splits = sp;
-    }
+    const int sp = splits_for(t, p.m, p.n, p.k, sms);
+    if (sp > 1 && p.partial) p.splits = sp;
     p.ks_per_split = static_cast<int>((kt + p.splits - 1) / p.splits);
     cudaError_t e;
     switch (t) {
@@ -1305,7 +1326,7 @@ cudaError_t launch_tile(GemmParams &p, cudaStream_t s) {
     case kT64x64: e = launch_pick<WT, Cfg<64, 64>, kPartials>(p, s); break;
     default: e = launch_pick<WT, Cfg<32, 128, 2>, kPartials>(p, s); break;
     }
-    if (e != cudaSuccess || p.splits == 1) return e;
+    if (e != cudaSuccess || p.splits == 1 || kPartials) return e;
     const int64_t warps = p.m * ((p.n + 127) / 128);
     const int64_t blocks = (warps * 32 + kThreads - 1) / kThreads;
     if (blocks > 0x7fffffff) return cudaErrorInvalidValue;

@@ -193,60 +193,7 @@ def test_forced_path_rejections():
         pb.mm("q4_0", wd, ad, 16, 10, 96, path="mma")   # k not a multiple of 256
 
 
-# --------------------------------------------------------- full-size checks
-def dequant_abs_q4_0(wb: np.ndarray) -> np.ndarray:
-    d = np.abs(wb["d"].view(np.float16).astype(np.float64))
-    lo = (wb["qs"] & 15).astype(np.int64) - 8
-    hi = (wb["qs"] >> 4).astype(np.int64) - 8
-    q = np.concatenate([lo, hi], axis=-1)
-    return (np.abs(q) * d[..., None]).reshape(wb.shape[0], -1)
-
-
-def dequant_abs_q8_0(ab: np.ndarray) -> np.ndarray:
-    d = np.abs(ab["d"].view(np.float16).astype(np.float64))
-    return (np.abs(ab["qs"].astype(np.int64)) * d[..., None]).reshape(ab.shape[0], -1)
-
-
-@pytest.mark.parametrize("m,n,k", [(1, 4096, 4096), (1, 11008, 4096), (480, 1536, 1536)])
-def test_q4_0_full_size(oracle, m, n, k):
-    # BASELINE configurations: tuned path vs. the bit-exact simple path on the
-    # device, bound from |W| |A|^T in float64; plus exact oracle rows.
-    rng = np.random.default_rng(n + m)
-    wf = rng.standard_normal((n, k)).astype(np.float32)
-    w = oracle.quantize("q4_0", wf)
-    x = rng.standard_normal((m, k)).astype(np.float32)
-    a = oracle.quantize("q8_0", x)
-    wd = dev_bytes(w)
-    xd = dev(x)
-    assert host(pb.quantize_q4_0(dev(wf))).tobytes() == w.tobytes()
-    c = host(pb.compute("q4_0", wd, xd, n))
-    c_simple = host(pb.compute("q4_0", wd, xd, n, path="simple"))
-    bound = dequant_abs_q8_0(a) @ dequant_abs_q4_0(w).T
-    check_close(c, c_simple, bound, f"q4_0 {m}x{n}x{k}")
-    rows = [0, m - 1]
-    ref_rows = oracle.mm("q4_0", w, a[rows], len(rows), n, k)
-    np.testing.assert_array_equal(c_simple[rows].view(np.uint32), ref_rows.view(np.uint32))
-
-
-@pytest.mark.parametrize("wtype", ["q4_K", "iq2_xxs"])
-def test_k_types_full_size(oracle, wtype):
-    m, n, k = 480, 1536, 1536
-    rng = np.random.default_rng(77)
-    w = make_weights(oracle, wtype, n, k, rng)
-    x = rng.standard_normal((m, k)).astype(np.float32)
-    a = oracle.quantize("q8_K", x)
-    wd, xd = dev_bytes(w), dev(x)
-    c = host(pb.compute(wtype, wd, xd, n))
-    c_simple = host(pb.compute(wtype, wd, xd, n, path="simple"))
-    rows = [0, 131, m - 1]
-    sub = a[rows]
-    ref_rows = oracle.mm(wtype, w, sub, len(rows), n, k)
-    np.testing.assert_array_equal(c_simple[rows].view(np.uint32), ref_rows.view(np.uint32))
-    bound_rows = oracle.bound(wtype, w, sub, len(rows), n, k)
-    check_close(c[rows], ref_rows, bound_rows, wtype)
-    # whole matrix: tuned vs simple with a coarse per-row bound (max over sampled rows scaled)
-    scale = np.abs(c_simple).max() + 1e-30
-    assert np.max(np.abs(c - c_simple)) <= 1e-4 * scale
+# Full-size BASELINE configurations: tests/test_gpu_configs.py (whole matrices against the reference).
 
 
 def test_unshard_columns():
