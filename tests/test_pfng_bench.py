@@ -97,6 +97,6 @@ def test_cli_default_invocation():
 
 @needs_bin
 @pytest.mark.gpu
-def test_cli_skips_unsupported_shape():
-    r = run("--kernel", IDS[1], "--m", 1, "--n", 64, "--k", 96, "--iterations", 1, "--perf-events", "task-clock")
-    assert r.returncode == 0 and "status: SKIP (k must be a multiple of 256)" in r.stdout, r.stdout + r.stderr
+def test_cli_rejects_unknown_kernel():
+    r = run("--kernel", "no-such-kernel", "--m", 1, "--n", 64, "--k", 256)
+    assert r.returncode == 2 and "unknown kernel" in r.stderr
