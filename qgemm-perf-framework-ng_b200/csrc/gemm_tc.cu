@@ -1,92 +1,107 @@
 // gemm_tc.cu -- q4_0 x q8_0 batched matmul on the 5th-generation tensor
-// cores: tcgen05.mma kind::i8 with the accumulators in tensor memory (TMEM).
+// cores: tcgen05.mma kind::i8 with the integer sub-block products in tensor
+// memory (TMEM), operands brought in by TMA.
 //
 // C[m][n] = A[m][k] . W[n][k]^T, W raw q4_0 blocks, A in the split layout
 // (int8 rows + one fp32 scale per 32) from quantize.cu.  Semantics:
 // compute_q4_0, bench/llama_reference/llama_reference.cpp:133-148 and :165-205.
 //
-// Tile: 128 weight rows (the MMA's M, one TMEM lane each) x 64 activation
-// rows (the MMA's N), k-steps of 256.  Warp roles (384 threads, one CTA/SM):
-//   warp 0      loads: raw W rows, activation int8 rows (written straight
-//               into the 128-byte-swizzled K-major operand layout) and the
-//               activation scales, with cp.async into a 3-stage ring whose
-//               stages complete an mbarrier (cp.async.mbarrier.arrive);
-//   warp 1      TMEM owner and MMA issuer: one tcgen05.mma (M 128, N 64,
-//               K 32) per 32-deep sub-block, each into its own TMEM buffer
-//               (8 buffers, a whole k-step), completion signalled with
-//               tcgen05.commit; each MMA overwrites its buffer (no
-//               accumulate), the fold reads it;
-//   warps 2,3   decode: raw q4_0 blocks -> int8 (q - 8) operand rows in
-//               the swizzled layout, the per-(row, sub-block) weight scales,
-//               and the activation scales transposed to [sub-block][row];
-//   warps 4-11  fold, thread = weight row, warps 4-7 activation rows 0-31 and
-//               warps 8-11 rows 32-63 (two warps per scheduler hide the TMEM
-//               load latency).  For each sub-block, tcgen05.ld the 32 int32
-//               partials, release the buffer at once, and fold them into 32
-//               fp32 accumulators in registers.
-// The fold is the exact two-FMA scheme of gemm.cu: the int32 partial P read
-// back plus the integer 0x4B400000 is the float 2^23 + 2^22 + P exactly (one
-// integer add, no conversion); t = fma(y, s, -(2^23+2^22) s)
-// = round(P s) with s = d_w (fp16, exact products), acc = fma(t, d_a, acc).
-// Each output element costs an integer add and one packed FMA pair per
-// sub-block; the MMAs, operand fetch and accumulation run beside them.
+// Tile: 128 weight rows (the MMA's M, one TMEM lane each) x 128 activation
+// rows (the MMA's N, one TMEM column each), k-steps of 256.  The kernel is
+// persistent: CTA c takes tiles c, c + grid, ... with the m tiles fastest, so
+// the CTAs running together share their W tiles.  Warp roles (640 threads,
+// one CTA per SM):
+//   warp 0      TMA producer: per k-step one 2-D tensor copy of the raw W
+//               rows (128 x 144 bytes; rows past n read as zeros), two of the
+//               int8 activation rows (128 x 128 bytes each, 128-byte swizzle:
+//               they land directly in the MMA's K-major operand layout) and
+//               one of their scales (128 x 8 floats), all completing one
+//               mbarrier's transaction count; two stages;
+//   warp 1      TMEM owner and MMA issuer: one tcgen05.mma (M 128, N 128,
+//               K 32) per 32-deep sub-block into one of four TMEM buffers
+//               (512 columns), completion signalled with tcgen05.commit; the
+//               MMA overwrites its buffer (no accumulate), the fold reads it;
+//   warps 2, 3  decode: raw q4_0 blocks -> int8 (q - 8) operand rows in the
+//               swizzled layout, the per-(row, sub-block) weight scales, and
+//               the activation scales transposed to [sub-block][row];
+//   warps 4-19  fold: warp w reads TMEM lane quarter w % 4 (thread = weight
+//               row) and column block (w - 4) / 4 (32 activation rows): per
+//               sub-block, tcgen05.ld its 32 int32 products, hand the buffer
+//               back, and fold them into 32 fp32 accumulators in registers;
+//               at the end of a tile they store C and start the next one
+//               while the MMA already fills the buffers again.
+// The fold is the exact two-FMA scheme of gemm.cu: the int32 product P plus
+// the integer 0x4B400000 is the float 2^23 + 2^22 + P exactly (one integer
+// add, no conversion); t = fma(y, s, -(2^23+2^22) s) = round(P s) with
+// s = d_w (fp16, exact products), acc = fma(t, d_a, acc), sub-blocks in k
+// order -- the same operations in the same order as the mma.sync kernel, so
+// the results are bit-identical to it (unsplit).
 //
-// Every wait is bounded; a wait that gives up records an error, raises the
-// CTA's abort flag (which ends every other role's waits at once) and the CTA
-// frees its TMEM before returning.
+// Loads read this GPU's memory only (W, the activation operand); no TMA
+// multicast.  Every wait is bounded; a wait that gives up records an error,
+// raises the CTA's abort flag (which ends every other role's waits at once)
+// and the CTA frees its TMEM before returning.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "pfng_common.cuh"
 #include "pfng_internal.h"
 
 namespace pfng {
 namespace {
 
-constexpr int TM = 128;        // weight rows per tile
-constexpr int TN = 64;         // activation rows per tile
-constexpr int BK = 256;        // k per stage
-constexpr int kLoadStages = 3;
-constexpr int kABufs = 2;      // decoded weight operand buffers
-constexpr int kTmemBufs = 8;   // sub-block accumulators in TMEM
+constexpr int TM = 128;        // weight rows per tile (TMEM lanes)
+constexpr int TN = 128;        // activation rows per tile (TMEM columns)
+constexpr int BK = 256;        // k per k-step
+constexpr int kStages = 2;     // TMA load stages
+constexpr int kDecBufs = 2;    // decoded weight operand buffers
+constexpr int kTmemBufs = 4;   // sub-block products in TMEM
 constexpr uint32_t kTmemCols = kTmemBufs * TN;  // 512: all of TMEM
-constexpr int kThreads = 384;
-constexpr int kFoldWarps = 8;
+constexpr int kThreads = 640;
+constexpr int kFoldWarps = 16;
+constexpr int kFoldWarp0 = 4;
 constexpr int kDecodeWarps = 2;
-constexpr uint32_t kRawSlot = 160;  // bytes per raw weight row per stage (144 used)
+constexpr uint32_t kRawRow = 144;  // raw q4_0 bytes of one weight row per k-step
 constexpr uint32_t kMagicBits = 0x4B400000u;
 constexpr float kMagic = 12582912.0f;
 
 // shared memory plan (dynamic, base aligned to 1024 for the swizzle atoms)
-constexpr uint32_t kAOpBytes = TM * BK;                    // 32 KB, [2 col blocks][128 rows][128 B]
-constexpr uint32_t kBOpBytes = TN * BK;                    // 16 KB, [2 col blocks][64 rows][128 B]
-constexpr uint32_t kRawBytes = TM * kRawSlot;              // 20 KB
-constexpr uint32_t kDaRawBytes = TN * 8 * 4;               // 2 KB, [64 rows][8]
-constexpr uint32_t kSwBytes = TM * 8 * 4;                  // 4 KB, weight scales [128 rows][8]
-constexpr uint32_t kDaTBytes = 8 * TN * 4;                 // 2 KB, activation scales [8][64 rows]
-constexpr uint32_t kOffA = 0;
-constexpr uint32_t kOffB = kOffA + kABufs * kAOpBytes;                  // 64 KB
-constexpr uint32_t kOffRaw = kOffB + kLoadStages * kBOpBytes;           // 112 KB
-constexpr uint32_t kOffDaRaw = kOffRaw + kLoadStages * kRawBytes;       // 172 KB
-constexpr uint32_t kOffSw = kOffDaRaw + kLoadStages * kDaRawBytes;
-constexpr uint32_t kOffDaT = kOffSw + kABufs * kSwBytes;
-constexpr uint32_t kOffBar = kOffDaT + kABufs * kDaTBytes;
-constexpr uint32_t kNumBars = 2 * kLoadStages + 2 * kABufs + 2 * kTmemBufs + 1;
-constexpr uint32_t kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;     // + TMEM address, alignment slack
+constexpr uint32_t kRawBytes = TM * kRawRow;               // 18 KB: W rows as in memory
+constexpr uint32_t kActBytes = TN * BK;                    // 32 KB: [2 col blocks][128 rows][128 B], swizzled
+constexpr uint32_t kActScaleBytes = TN * 8 * 4;            // 4 KB: [128 rows][8] floats
+constexpr uint32_t kStageBytes = kRawBytes + kActBytes + kActScaleBytes;  // 54 KB
+constexpr uint32_t kWOpBytes = TM * BK;                    // 32 KB: decoded W, [2 col blocks][128 rows][128 B]
+constexpr uint32_t kSwBytes = TM * 8 * 4;                  // 4 KB: weight scales [128 rows][8]
+constexpr uint32_t kDaTBytes = 8 * TN * 4;                 // 4 KB: activation scales [8][128 rows]
+constexpr uint32_t kDecBytes = kWOpBytes + kSwBytes + kDaTBytes;
+constexpr uint32_t kOffStage = 0;
+constexpr uint32_t kOffDec = kOffStage + kStages * kStageBytes;
+constexpr uint32_t kOffBar = kOffDec + kDecBufs * kDecBytes;
+constexpr uint32_t kNumBars = 2 * kStages + 2 * kDecBufs + 2 * kTmemBufs + 1;
+constexpr uint32_t kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;  // + TMEM address, alignment slack
+static_assert(kRawBytes % 1024 == 0 && kStageBytes % 1024 == 0 && kDecBytes % 1024 == 0, "1024-byte atoms");
+constexpr uint32_t kStageTx = kRawBytes + kActBytes + kActScaleBytes;  // bytes the TMA lands per stage
 
 struct TcParams {
-    const uint8_t *w;
-    SplitA a;
     float *c;
     int64_t ldc;
     int64_t m, n, k;
-    int64_t row_bytes;
+    int mtiles, ntiles;
     int *err;
 };
 
-// ---- tcgen05 / proxy primitives -------------------------------------------
-PFNG_DEV void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+// ---- TMA / tcgen05 / proxy primitives ----------------------------------------
+PFNG_DEV void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
 }
-PFNG_DEV void cp_async_arrive_noinc(uint64_t *bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+PFNG_DEV void prefetch_map(const CUtensorMap *map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 PFNG_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 PFNG_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -139,8 +154,10 @@ PFNG_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 // Shared-memory matrix descriptor, K-major operand with the 128-byte swizzle:
 // rows of 128 bytes, 8-row atoms of 1024 bytes stored back to back (stride
-// byte offset 1024), the 16-byte chunk j of row r stored at chunk j ^ (r % 8).
-// `saddr` is the operand's first byte for this MMA (atom base + k offset).
+// byte offset 1024), the 16-byte chunk j of row r stored at chunk j ^ (r % 8)
+// -- the layout a TMA copy with CU_TENSOR_MAP_SWIZZLE_128B and a 128-byte
+// inner box writes.  `saddr` is the operand's first byte for this MMA (atom
+// base + k offset).
 PFNG_DEV uint64_t sw128_desc(uint32_t saddr) {
     uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);  // start address, 16-byte units
     d |= static_cast<uint64_t>(1u) << 16;                         // leading byte offset (unused with this swizzle)
@@ -154,13 +171,11 @@ PFNG_DEV uint64_t sw128_desc(uint32_t saddr) {
 constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(TN >> 3) << 17) |
                             (static_cast<uint32_t>(TM >> 4) << 24);
 
-// Byte offset of (row, 16-byte chunk c in 0..15 of the 256-byte k-step) in an
-// operand tile of `rows` rows: column block c / 8, swizzled chunk within it.
-PFNG_DEV uint32_t op_off(uint32_t rows, uint32_t row, uint32_t c) {
-    return (c >> 3) * rows * 128u + (row >> 3) * 1024u + (row & 7u) * 128u + (((c & 7u) ^ (row & 7u)) << 4);
+// Byte offset of (row, 16-byte chunk c in 0..15 of the 256-byte k-step) in a
+// 128-row operand tile: column block c / 8, swizzled chunk within it.
+PFNG_DEV uint32_t op_off(uint32_t row, uint32_t c) {
+    return (c >> 3) * TM * 128u + (row >> 3) * 1024u + (row & 7u) * 128u + (((c & 7u) ^ (row & 7u)) << 4);
 }
-
-PFNG_DEV bool aborted(const int *abort_flag) { return *reinterpret_cast<const volatile int *>(abort_flag) != 0; }
 
 // Bounded wait that also gives up (false) once the CTA's abort flag is up.
 // Each attempt is a hardware-suspended try_wait, so a waiting warp issues
@@ -173,35 +188,37 @@ PFNG_DEV bool wait_bar(uint64_t *bar, uint32_t parity, const int *abort_flag, in
     report_error(err, code);
     return false;
 }
+PFNG_DEV bool aborted(const int *abort_flag) { return *reinterpret_cast<const volatile int *>(abort_flag) != 0; }
 
-__global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4_0_kernel(const TcParams p) {
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_q4_0_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a,
+                        const __grid_constant__ CUtensorMap map_ad, const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kOffBar);
-    uint64_t *ld_full = bars;                              // [kLoadStages] cp.async landed (32 lane arrivals)
-    uint64_t *ld_empty = ld_full + kLoadStages;            // [kLoadStages] decode warps + MMA commit (1)
-    uint64_t *dec_full = ld_empty + kLoadStages;           // [kABufs] decode warps done
-    uint64_t *dec_empty = dec_full + kABufs;               // [kABufs] MMA commit (1) + fold warps
-    uint64_t *tm_full = dec_empty + kABufs;                // [kTmemBufs] MMA commit (1)
-    uint64_t *tm_empty = tm_full + kTmemBufs;              // [kTmemBufs] fold warps
-    uint64_t *mma_done = tm_empty + kTmemBufs;             // every issued MMA has completed (commit)
+    uint64_t *ld_full = bars;                          // [kStages]  TMA transaction count
+    uint64_t *ld_empty = ld_full + kStages;            // [kStages]  MMA commit (1) + decode warps
+    uint64_t *dec_full = ld_empty + kStages;           // [kDecBufs] decode warps
+    uint64_t *dec_empty = dec_full + kDecBufs;         // [kDecBufs] MMA commit (1) + fold warps
+    uint64_t *tm_full = dec_empty + kDecBufs;          // [kTmemBufs] MMA commit (1)
+    uint64_t *tm_empty = tm_full + kTmemBufs;          // [kTmemBufs] fold warps
+    uint64_t *mma_done = tm_empty + kTmemBufs;         // every issued MMA has completed (commit)
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + kNumBars);
     __shared__ int abort_flag;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int64_t n0 = static_cast<int64_t>(blockIdx.x) * TM;
-    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * TN;
     const int ksteps = static_cast<int>(p.k / BK);
+    const int ntiles_total = p.mtiles * p.ntiles;
 
     if (tid == 0) {
         abort_flag = 0;
-        for (int s = 0; s < kLoadStages; ++s) {
-            mbar_init(&ld_full[s], 32);
-            mbar_init(&ld_empty[s], kDecodeWarps + 1);
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&ld_full[s], 1);
+            mbar_init(&ld_empty[s], 1 + kDecodeWarps);
         }
-        for (int a = 0; a < kABufs; ++a) {
-            mbar_init(&dec_full[a], kDecodeWarps);
-            mbar_init(&dec_empty[a], 1 + kFoldWarps);
+        for (int d = 0; d < kDecBufs; ++d) {
+            mbar_init(&dec_full[d], kDecodeWarps);
+            mbar_init(&dec_empty[d], 1 + kFoldWarps);
         }
         for (int b = 0; b < kTmemBufs; ++b) {
             mbar_init(&tm_full[b], 1);
@@ -209,6 +226,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4_0_kernel(const TcParam
         }
         mbar_init(mma_done, 1);
         fence_mbar_init();
+        prefetch_map(&map_w);
+        prefetch_map(&map_a);
+        prefetch_map(&map_ad);
     }
     if (warp == 1) {
         tmem_alloc(tmem_holder, kTmemCols);
@@ -219,207 +239,215 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4_0_kernel(const TcParam
     tc_fence_after();
     const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(tmem_holder);
     const uint32_t s_base = smem_u32(smem);
+    // a programmatic dependent of the activation quantizer: everything
+    // above overlaps its tail, everything below reads its output
+    pdl_wait();
 
     if (warp == 0) {
-        // ---------------- loads ----------------
-        for (int ks = 0; ks < ksteps; ++ks) {
-            const int s = ks % kLoadStages;
-            if (ks >= kLoadStages &&
-                !wait_bar(&ld_empty[s], ((ks / kLoadStages) - 1) & 1, &abort_flag, p.err, kErrWaitEmpty)) {
-                abort_flag = 1;
-                break;
+        // ---------------- TMA producer (one thread) ----------------
+        if (lane == 0) {
+            int g = 0;
+            for (int t = blockIdx.x; t < ntiles_total && !aborted(&abort_flag); t += gridDim.x) {
+                const int mb = t % p.mtiles, nb = t / p.mtiles;
+                for (int ks = 0; ks < ksteps; ++ks, ++g) {
+                    const int s = g % kStages;
+                    if (g >= kStages &&
+                        !wait_bar(&ld_empty[s], ((g / kStages) - 1) & 1, &abort_flag, p.err, kErrWaitEmpty)) {
+                        abort_flag = 1;
+                        break;
+                    }
+                    if (aborted(&abort_flag)) break;
+                    const uint32_t st = s_base + kOffStage + s * kStageBytes;
+                    mbar_arrive_expect_tx(&ld_full[s], kStageTx);
+                    tma_load_2d(st, &map_w, ks * static_cast<int>(kRawRow), nb * TM, &ld_full[s]);
+                    tma_load_2d(st + kRawBytes, &map_a, ks * BK, mb * TN, &ld_full[s]);
+                    tma_load_2d(st + kRawBytes + kActBytes / 2, &map_a, ks * BK + 128, mb * TN, &ld_full[s]);
+                    tma_load_2d(st + kRawBytes + kActBytes, &map_ad, ks * 8, mb * TN, &ld_full[s]);
+                }
             }
-            // raw weights: 128 rows x 144 bytes (9 chunks)
-            const uint32_t raw = s_base + kOffRaw + s * kRawBytes;
-            for (int q = lane; q < TM * 9; q += 32) {
-                const int row = q / 9, ch = q % 9;
-                const int64_t n = n0 + row;
-                const bool ok = n < p.n;
-                const uint8_t *src = p.w + (ok ? n * p.row_bytes + static_cast<int64_t>(ks) * 144 + ch * 16 : 0);
-                cp_async16(raw + row * kRawSlot + ch * 16, src, ok ? 16u : 0u);
-            }
-            // activation int8 rows, swizzled operand layout
-            const uint32_t bop = s_base + kOffB + s * kBOpBytes;
-            for (int q = lane; q < TN * 16; q += 32) {
-                const int row = q >> 4, ch = q & 15;
-                const int8_t *src = p.a.qs + (m0 + row) * p.k + static_cast<int64_t>(ks) * BK + ch * 16;
-                cp_async16(bop + op_off(TN, row, ch), src, 16u);
-            }
-            // activation scales: 64 rows x 8 floats
-            const uint32_t dar = s_base + kOffDaRaw + s * kDaRawBytes;
-            for (int q = lane; q < TN * 2; q += 32) {
-                const int row = q >> 1, h = q & 1;
-                const float *src = p.a.d + (m0 + row) * (p.k / 32) + ks * 8 + h * 4;
-                cp_async16(dar + row * 32 + h * 16, src, 16u);
-            }
-            cp_async_arrive_noinc(&ld_full[s]);
+            // on an abort the consumers stop waiting: do not let the CTA end
+            // while copies into its shared memory are in flight
+            if (aborted(&abort_flag))
+                for (int i = g - kStages > 0 ? g - kStages : 0; i < g; ++i)
+                    mbar_wait(&ld_full[i % kStages], static_cast<uint32_t>((i / kStages) & 1), p.err, kErrWaitFull);
         }
-        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncwarp();
     } else if (warp == 1) {
         // ---------------- MMA issue (one thread) ----------------
         if (lane == 0) {
-            int gsb = 0;
-            for (int ks = 0; ks < ksteps && !aborted(&abort_flag); ++ks) {
-                const int s = ks % kLoadStages, a = ks % kABufs;
-                if (!wait_bar(&ld_full[s], (ks / kLoadStages) & 1, &abort_flag, p.err, kErrWaitFull) ||
-                    !wait_bar(&dec_full[a], (ks / kABufs) & 1, &abort_flag, p.err, kErrWaitFull)) {
-                    abort_flag = 1;
-                    break;
-                }
-                fence_proxy_async_smem();
-                tc_fence_after();
-                const uint32_t aop = s_base + kOffA + a * kAOpBytes;
-                const uint32_t bop = s_base + kOffB + s * kBOpBytes;
-                bool ok = true;
-                for (int sb = 0; sb < 8; ++sb, ++gsb) {
-                    const int buf = gsb % kTmemBufs;
-                    if (!wait_bar(&tm_empty[buf], (gsb / kTmemBufs) & 1, &abort_flag, p.err, kErrWaitEmpty)) {
+            int g = 0, gsb = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles_total && ok; t += gridDim.x) {
+                for (int ks = 0; ks < ksteps && ok; ++ks, ++g) {
+                    const int s = g % kStages, d = g % kDecBufs;
+                    if (!wait_bar(&ld_full[s], (g / kStages) & 1, &abort_flag, p.err, kErrWaitFull) ||
+                        !wait_bar(&dec_full[d], (g / kDecBufs) & 1, &abort_flag, p.err, kErrWaitFull)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t koff = (sb & 3) * 32u;  // k offset inside the 128-byte swizzled row
-                    const uint64_t da = sw128_desc(aop + (sb >> 2) * (TM * 128u) + koff);
-                    const uint64_t db = sw128_desc(bop + (sb >> 2) * (TN * 128u) + koff);
-                    umma_i8(tmem_base + static_cast<uint32_t>(buf * TN), da, db, kIdesc, 0u);
-                    umma_commit(&tm_full[buf]);
+                    const uint32_t wop = s_base + kOffDec + d * kDecBytes;
+                    const uint32_t aop = s_base + kOffStage + s * kStageBytes + kRawBytes;
+                    for (int sb = 0; sb < 8; ++sb, ++gsb) {
+                        const int buf = gsb % kTmemBufs;
+                        if (!wait_bar(&tm_empty[buf], (gsb / kTmemBufs) & 1, &abort_flag, p.err, kErrWaitEmpty)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t koff = (sb & 3) * 32u;  // k offset inside the 128-byte swizzled row
+                        const uint64_t da = sw128_desc(wop + (sb >> 2) * (TM * 128u) + koff);
+                        const uint64_t db = sw128_desc(aop + (sb >> 2) * (TN * 128u) + koff);
+                        umma_i8(tmem_base + static_cast<uint32_t>(buf * TN), da, db, kIdesc, 0u);
+                        umma_commit(&tm_full[buf]);
+                    }
+                    if (!ok) break;
+                    umma_commit(&dec_empty[d]);
+                    umma_commit(&ld_empty[s]);
                 }
-                if (!ok) {
-                    abort_flag = 1;
-                    break;
-                }
-                umma_commit(&dec_empty[a]);
-                umma_commit(&ld_empty[s]);
             }
+            if (!ok) abort_flag = 1;
             // TMEM is freed at the end: wait until no MMA is in flight
             umma_commit(mma_done);
             if (!mbar_wait(mma_done, 0, p.err, kErrWaitFull)) abort_flag = 1;
         }
         __syncwarp();
-    } else if (warp == 2 || warp == 3) {
-        // ---------------- decode: 8 threads per weight row, one block each ----------------
+    } else if (warp < kFoldWarp0) {
+        // ---------------- decode: 64 threads, 16 (row, block) tasks each ----------------
         const int dt = (warp - 2) * 32 + lane;  // 0..63
-        for (int ks = 0; ks < ksteps; ++ks) {
-            const int s = ks % kLoadStages, a = ks % kABufs;
-            if (!wait_bar(&ld_full[s], (ks / kLoadStages) & 1, &abort_flag, p.err, kErrWaitFull) ||
-                (ks >= kABufs &&
-                 !wait_bar(&dec_empty[a], ((ks / kABufs) - 1) & 1, &abort_flag, p.err, kErrWaitEmpty))) {
-                abort_flag = 1;
-                break;
-            }
-            const uint8_t *raw = smem + kOffRaw + s * kRawBytes;
-            uint8_t *aop = smem + kOffA + a * kAOpBytes;
-            float *sw = reinterpret_cast<float *>(smem + kOffSw + a * kSwBytes);
-#pragma unroll 2
-            for (int i = 0; i < (TM * 8) / (kDecodeWarps * 32); ++i) {
-                const int task = dt + i * kDecodeWarps * 32;  // (row, block)
-                const int row = task >> 3, u = task & 7;
-                uint32_t q[4], dbits;
-                load_q4_0_block_smem(raw, row * kRawSlot + 18u * u, q, dbits);
-                // q - 8 per byte: set bit 7, subtract 8 (no borrow crosses a byte), clear bit 7 again
-                uint4 lo, hi;
-                lo.x = (((q[0] & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
-                lo.y = (((q[1] & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
-                lo.z = (((q[2] & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
-                lo.w = (((q[3] & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
-                hi.x = ((((q[0] >> 4) & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
-                hi.y = ((((q[1] >> 4) & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
-                hi.z = ((((q[2] >> 4) & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
-                hi.w = ((((q[3] >> 4) & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
-                // the 8 threads of a row store together: order the two chunks so
-                // that each store instruction covers 8 distinct bank groups
-                const bool swap = u >= 4;
-                *reinterpret_cast<uint4 *>(aop + op_off(TM, row, swap ? 2 * u + 1 : 2 * u)) = swap ? hi : lo;
-                *reinterpret_cast<uint4 *>(aop + op_off(TM, row, swap ? 2 * u : 2 * u + 1)) = swap ? lo : hi;
-                sw[row * 8 + u] = f16_bits_to_f32(dbits);
-            }
-            // activation scales, transposed to [sub-block][row]
-            const float *dar = reinterpret_cast<const float *>(smem + kOffDaRaw + s * kDaRawBytes);
-            float *dat = reinterpret_cast<float *>(smem + kOffDaT + a * kDaTBytes);
-#pragma unroll
-            for (int i = 0; i < (TN * 8) / (kDecodeWarps * 32); ++i) {
-                const int e = dt + i * kDecodeWarps * 32;  // e = sb * TN + activation row
-                dat[e] = dar[(e % TN) * 8 + e / TN];
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&dec_full[a]);
-                mbar_arrive(&ld_empty[s]);
+        int g = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < ntiles_total && ok; t += gridDim.x) {
+            for (int ks = 0; ks < ksteps; ++ks, ++g) {
+                const int s = g % kStages, d = g % kDecBufs;
+                if (!wait_bar(&ld_full[s], (g / kStages) & 1, &abort_flag, p.err, kErrWaitFull) ||
+                    (g >= kDecBufs &&
+                     !wait_bar(&dec_empty[d], ((g / kDecBufs) - 1) & 1, &abort_flag, p.err, kErrWaitEmpty))) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t *raw = smem + kOffStage + s * kStageBytes;
+                uint8_t *dec = smem + kOffDec + d * kDecBytes;
+                float *sw = reinterpret_cast<float *>(dec + kWOpBytes);
+#pragma unroll 4
+                for (int i = 0; i < (TM * 8) / (kDecodeWarps * 32); ++i) {
+                    const int task = dt + i * kDecodeWarps * 32;  // (row, block)
+                    const int row = task >> 3, u = task & 7;
+                    uint32_t q[4], dbits;
+                    load_q4_0_block_smem(raw, row * kRawRow + 18u * u, q, dbits);
+                    // q - 8 per byte: set bit 7, subtract 8 (no borrow crosses a byte), clear bit 7 again
+                    uint4 lo, hi;
+                    lo.x = (((q[0] & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
+                    lo.y = (((q[1] & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
+                    lo.z = (((q[2] & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
+                    lo.w = (((q[3] & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
+                    hi.x = ((((q[0] >> 4) & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
+                    hi.y = ((((q[1] >> 4) & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
+                    hi.z = ((((q[2] >> 4) & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
+                    hi.w = ((((q[3] >> 4) & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
+                    // the 8 threads of a row store together: order the two chunks so
+                    // that each store instruction covers 8 distinct bank groups
+                    const bool swap = u >= 4;
+                    *reinterpret_cast<uint4 *>(dec + op_off(row, swap ? 2 * u + 1 : 2 * u)) = swap ? hi : lo;
+                    *reinterpret_cast<uint4 *>(dec + op_off(row, swap ? 2 * u : 2 * u + 1)) = swap ? lo : hi;
+                    sw[row * 8 + u] = f16_bits_to_f32(dbits);
+                }
+                // activation scales, transposed to [sub-block][row]
+                const float *dar = reinterpret_cast<const float *>(raw + kRawBytes + kActBytes);
+                float *dat = reinterpret_cast<float *>(dec + kWOpBytes + kSwBytes);
+#pragma unroll 4
+                for (int i = 0; i < (TN * 8) / (kDecodeWarps * 32); ++i) {
+                    const int e = dt + i * kDecodeWarps * 32;  // e = sb * TN + activation row
+                    dat[e] = dar[(e % TN) * 8 + e / TN];
+                }
+                fence_proxy_async_smem();  // the decoded operand is read by the tensor cores
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&dec_full[d]);
+                    mbar_arrive(&ld_empty[s]);
+                }
             }
         }
+        if (!ok) abort_flag = 1;
     } else {
-        // ---------------- fold (warps 4..11) ----------------
-        const int qtr = warp & 3;                // TMEM lane quarter of this warp
-        const int half = (warp - 4) >> 2;        // activation rows 32 * half .. + 31
+        // ---------------- fold (warps 4..19) ----------------
+        const int fw = warp - kFoldWarp0;
+        const int qtr = warp & 3;                // TMEM lane quarter this warp may access
+        const int cb = fw >> 2;                  // activation rows 32 cb .. 32 cb + 31 of the tile
         const int row = qtr * 32 + lane;         // weight row of this thread in the tile
-        const uint32_t my_cols = tmem_base + (static_cast<uint32_t>(qtr * 32) << 16) + half * 32;
+        const uint32_t my_cols = tmem_base + (static_cast<uint32_t>(qtr * 32) << 16) + static_cast<uint32_t>(cb * 32);
         // every TMEM buffer starts free
         if (lane == 0)
             for (int b = 0; b < kTmemBufs; ++b) mbar_arrive(&tm_empty[b]);
 
-        float2 acc[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) acc[j] = make_float2(0.0f, 0.0f);
-        int gsb = 0;
+        int g = 0, gsb = 0;
         bool ok = true;
-        for (int ks = 0; ks < ksteps && ok; ++ks) {
-            const int a = ks % kABufs;
-            if (!wait_bar(&dec_full[a], (ks / kABufs) & 1, &abort_flag, p.err, kErrWaitFull)) {
-                ok = false;
-                break;
-            }
-            const float4 *swr = reinterpret_cast<const float4 *>(smem + kOffSw + a * kSwBytes) + row * 2;
-            const float4 s0 = swr[0], s1 = swr[1];
-            const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-            const float *dat = reinterpret_cast<const float *>(smem + kOffDaT + a * kDaTBytes) + half * 32;
+        for (int t = blockIdx.x; t < ntiles_total && ok; t += gridDim.x) {
+            const int mb = t % p.mtiles, nb = t / p.mtiles;
+            float2 acc[16];
 #pragma unroll
-            for (int sb = 0; sb < 8; ++sb) {
-                const int buf = (gsb + sb) % kTmemBufs;
-                if (!ok || !wait_bar(&tm_full[buf], ((gsb + sb) / kTmemBufs) & 1, &abort_flag, p.err, kErrWaitFull)) {
+            for (int j = 0; j < 16; ++j) acc[j] = make_float2(0.0f, 0.0f);
+            for (int ks = 0; ks < ksteps && ok; ++ks, ++g) {
+                const int d = g % kDecBufs;
+                if (!wait_bar(&dec_full[d], (g / kDecBufs) & 1, &abort_flag, p.err, kErrWaitFull)) {
                     ok = false;
-                    continue;
+                    break;
                 }
-                tc_fence_after();
-                uint32_t r[32];
-                tmem_ld32(my_cols + buf * TN, r);
-                // the partials are in registers: hand the buffer back to the MMA
-                // issuer before the arithmetic
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&tm_empty[buf]);
-                const float2 ss = make_float2(sv[sb], sv[sb]);
-                const float2 cm = make_float2(-kMagic * sv[sb], -kMagic * sv[sb]);
-                const float4 *dap = reinterpret_cast<const float4 *>(dat + sb * TN);
+                const uint8_t *dec = smem + kOffDec + d * kDecBytes;
+                const float *swr = reinterpret_cast<const float *>(dec + kWOpBytes) + row * 8;
+                const float *dat = reinterpret_cast<const float *>(dec + kWOpBytes + kSwBytes) + cb * 32;
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float4 d4 = dap[j];  // activation scales of columns 4j .. 4j + 3
-                    // P + 0x4B400000 as an integer is the float 2^23 + 2^22 + P
-                    const float2 y0 = make_float2(__uint_as_float(r[4 * j] + kMagicBits),
-                                                  __uint_as_float(r[4 * j + 1] + kMagicBits));
-                    const float2 y1 = make_float2(__uint_as_float(r[4 * j + 2] + kMagicBits),
-                                                  __uint_as_float(r[4 * j + 3] + kMagicBits));
-                    const float2 t0 = __ffma2_rn(y0, ss, cm), t1 = __ffma2_rn(y1, ss, cm);
-                    acc[2 * j] = __ffma2_rn(t0, make_float2(d4.x, d4.y), acc[2 * j]);
-                    acc[2 * j + 1] = __ffma2_rn(t1, make_float2(d4.z, d4.w), acc[2 * j + 1]);
+                for (int sb = 0; sb < 8; ++sb) {
+                    const int buf = (gsb + sb) % kTmemBufs;
+                    if (!ok || !wait_bar(&tm_full[buf], ((gsb + sb) / kTmemBufs) & 1, &abort_flag, p.err,
+                                         kErrWaitFull)) {
+                        ok = false;
+                        continue;
+                    }
+                    tc_fence_after();
+                    uint32_t r[32];
+                    tmem_ld32(my_cols + buf * TN, r);
+                    // the products are in registers: hand the buffer back to
+                    // the MMA issuer before the arithmetic
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tm_empty[buf]);
+                    const float sv = swr[sb];
+                    const float2 ss = make_float2(sv, sv);
+                    const float2 cm = make_float2(-kMagic * sv, -kMagic * sv);
+                    const float4 *dap = reinterpret_cast<const float4 *>(dat + sb * TN);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float4 d4 = dap[j];  // activation scales of columns 4j .. 4j + 3
+                        // P + 0x4B400000 as an integer is the float 2^23 + 2^22 + P
+                        const float2 y0 = make_float2(__uint_as_float(r[4 * j] + kMagicBits),
+                                                      __uint_as_float(r[4 * j + 1] + kMagicBits));
+                        const float2 y1 = make_float2(__uint_as_float(r[4 * j + 2] + kMagicBits),
+                                                      __uint_as_float(r[4 * j + 3] + kMagicBits));
+                        const float2 t0 = __ffma2_rn(y0, ss, cm), t1 = __ffma2_rn(y1, ss, cm);
+                        acc[2 * j] = __ffma2_rn(t0, make_float2(d4.x, d4.y), acc[2 * j]);
+                        acc[2 * j + 1] = __ffma2_rn(t1, make_float2(d4.z, d4.w), acc[2 * j + 1]);
+                    }
+                }
+                gsb += 8;
+                if (!ok) break;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&dec_empty[d]);
+            }
+            if (!ok) break;
+            // epilogue: this thread's weight row n, activation rows of column block cb
+            const int64_t n = static_cast<int64_t>(nb) * TM + row;
+            if (n < p.n) {
+                const int64_t m0 = static_cast<int64_t>(mb) * TN + cb * 32;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int64_t m = m0 + 2 * j;
+                    if (m < p.m) p.c[m * p.ldc + n] = acc[j].x;
+                    if (m + 1 < p.m) p.c[(m + 1) * p.ldc + n] = acc[j].y;
                 }
             }
-            gsb += 8;
-            if (!ok) break;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&dec_empty[a]);
         }
         if (!ok) abort_flag = 1;
-        // epilogue: this thread's weight row n, activation rows m0 + 32 half + 0..31
-        const int64_t n = n0 + row;
-        if (ok && n < p.n) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int64_t m = m0 + half * 32 + 2 * j;
-                if (m < p.m) p.c[m * p.ldc + n] = acc[j].x;
-                if (m + 1 < p.m) p.c[(m + 1) * p.ldc + n] = acc[j].y;
-            }
-        }
     }
 
     tc_fence_before();
@@ -430,25 +458,64 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_q4_0_kernel(const TcParam
     }
 }
 
+// ---- host: tensor maps ------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 2-D tiled map over a row-major array [rows][cols] of `elem`-byte elements
+// (row stride `stride` bytes), boxes of box_cols x box_rows elements.
+bool encode_2d(CUtensorMap *map, CUtensorMapDataType type, const void *base, uint64_t cols, uint64_t rows,
+               uint64_t stride, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {stride};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, type, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 bool gemm_tc_supported(int wtype, int64_t m, int64_t n, int64_t k, const void *w) {
     (void)m;
     (void)n;
     return wtype == 0 && k > 0 && k % BK == 0 && (reinterpret_cast<uintptr_t>(w) & 15u) == 0 &&
-           kSmemBytes <= device_smem_optin();
+           kSmemBytes <= device_smem_optin() && encode_fn() != nullptr;
 }
 
 cudaError_t launch_gemm_tc(const GemmArgs &args, int *err, cudaStream_t s) {
+    const int64_t row_bytes = args.k / 32 * kQ4_0Bytes;  // a multiple of 144 (k % 256 == 0)
+    CUtensorMap map_w, map_a, map_ad;
+    if (!encode_2d(&map_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, args.w, static_cast<uint64_t>(row_bytes),
+                   static_cast<uint64_t>(args.n), static_cast<uint64_t>(row_bytes), kRawRow, TM,
+                   CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, args.a.qs, static_cast<uint64_t>(args.k),
+                   static_cast<uint64_t>(args.a.rows_pad), static_cast<uint64_t>(args.k), 128, TN,
+                   CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_2d(&map_ad, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, args.a.d, static_cast<uint64_t>(args.k / 32),
+                   static_cast<uint64_t>(args.a.rows_pad), static_cast<uint64_t>(args.k / 32 * 4), 8, TN,
+                   CU_TENSOR_MAP_SWIZZLE_NONE))
+        return cudaErrorInvalidValue;
     TcParams p{};
-    p.w = static_cast<const uint8_t *>(args.w);
-    p.a = args.a;
     p.c = args.c;
     p.ldc = args.ldc;
     p.m = args.m;
     p.n = args.n;
     p.k = args.k;
-    p.row_bytes = args.k / 32 * kQ4_0Bytes;
+    p.mtiles = static_cast<int>((args.m + TN - 1) / TN);
+    p.ntiles = static_cast<int>((args.n + TM - 1) / TM);
     p.err = err;
     static thread_local bool configured[64] = {false};
     int dev = 0;
@@ -459,9 +526,19 @@ cudaError_t launch_gemm_tc(const GemmArgs &args, int *err, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) configured[dev] = true;
     }
-    const dim3 grid(static_cast<unsigned>((args.n + TM - 1) / TM), static_cast<unsigned>((args.m + TN - 1) / TN));
-    gemm_tc_q4_0_kernel<<<grid, kThreads, kSmemBytes, s>>>(p);
-    return cudaGetLastError();
+    const int64_t tiles = static_cast<int64_t>(p.mtiles) * p.ntiles;
+    const int64_t sms = device_sm_count();
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(tiles < sms ? tiles : sms));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_tc_q4_0_kernel, map_w, map_a, map_ad, p);
 }
 
 }  // namespace pfng
