@@ -24,12 +24,15 @@
 //   warps 2, 3  decode: raw q4_0 blocks -> int8 (q - 8) operand rows in the
 //               swizzled layout, the per-(row, sub-block) weight scales, and
 //               the activation scales transposed to [sub-block][row];
-//   warps 4-19  fold: warp w reads TMEM lane quarter w % 4 (thread = weight
-//               row) and column block (w - 4) / 4 (32 activation rows): per
-//               sub-block, tcgen05.ld its 32 int32 products, hand the buffer
-//               back, and fold them into 32 fp32 accumulators in registers;
-//               at the end of a tile they store C and start the next one
-//               while the MMA already fills the buffers again.
+//   warps 4-19  fold: warp w reads TMEM lane quarter w % 4 and column block
+//               (w - 4) / 4 (32 activation rows) with two 16x256b loads per
+//               sub-block -- thread t holds weight rows t/4 + {0, 8, 16, 24}
+//               of the quarter and activation rows 8 j + 2 (t % 4) + {0, 1},
+//               j = 0..3, so one activation scale serves four rows and one
+//               weight scale eight columns -- hands the buffer back, and folds
+//               the 32 products into 32 fp32 accumulators in registers; at
+//               the end of a tile they store C and start the next one while
+//               the MMA already fills the buffers again.
 // The fold is the exact two-FMA scheme of gemm.cu: the int32 product P plus
 // the integer 0x4B400000 is the float 2^23 + 2^22 + P exactly (one integer
 // add, no conversion); t = fma(y, s, -(2^23+2^22) s) = round(P s) with
@@ -138,16 +141,20 @@ PFNG_DEV void umma_commit(uint64_t *bar) {
         "=r"(x[17]), "=r"(x[18]), "=r"(x[19]), "=r"(x[20]), "=r"(x[21]), "=r"(x[22]), "=r"(x[23]), "=r"(x[24]), \
         "=r"(x[25]), "=r"(x[26]), "=r"(x[27]), "=r"(x[28]), "=r"(x[29]), "=r"(x[30]), "=r"(x[31])
 
-// 32 consecutive TMEM columns of this warp's 32 lanes: thread t gets lane t.
-// The load and its wait are one statement, so no use of the outputs can be
-// scheduled before the data has arrived.
-PFNG_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+// Two 16x256b.x4 loads (lanes base .. base + 15 at ta, base + 16 .. base + 31
+// at tb; 32 consecutive columns each) and their wait, as one statement.
+// Each load gives thread t, for column chunk j = 0..3, registers
+// 4 j + {0, 1} = lane t/4, columns 8 j + 2 (t % 4) + {0, 1} and
+// 4 j + {2, 3} = lane t/4 + 8, the same columns.
+PFNG_DEV void tmem_ld_16x256b_2x4(uint32_t ta, uint32_t tb, uint32_t (&r)[32]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+        "tcgen05.ld.sync.aligned.16x256b.x4.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%32];\n\t"
+        "tcgen05.ld.sync.aligned.16x256b.x4.b32 {%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+        "%29, %30, %31}, [%33];\n\t"
         "tcgen05.wait::ld.sync.aligned;"
         : PFNG_R32(r)
-        : "r"(taddr)
+        : "r"(ta), "r"(tb)
         : "memory");
 }
 #undef PFNG_R32
@@ -374,8 +381,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int fw = warp - kFoldWarp0;
         const int qtr = warp & 3;                // TMEM lane quarter this warp may access
         const int cb = fw >> 2;                  // activation rows 32 cb .. 32 cb + 31 of the tile
-        const int row = qtr * 32 + lane;         // weight row of this thread in the tile
-        const uint32_t my_cols = tmem_base + (static_cast<uint32_t>(qtr * 32) << 16) + static_cast<uint32_t>(cb * 32);
+        const int r0 = qtr * 32 + (lane >> 2);   // weight rows r0 + {0, 8, 16, 24} of the tile
+        const int c0 = cb * 32 + 2 * (lane & 3); // activation rows c0 + 8 j + {0, 1}
+        const uint32_t ta = tmem_base + (static_cast<uint32_t>(qtr * 32) << 16) + static_cast<uint32_t>(cb * 32);
+        const uint32_t tb = ta + (16u << 16);
         // every TMEM buffer starts free
         if (lane == 0)
             for (int b = 0; b < kTmemBufs; ++b) mbar_arrive(&tm_empty[b]);
@@ -384,9 +393,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int t = blockIdx.x; t < ntiles_total && ok; t += gridDim.x) {
             const int mb = t % p.mtiles, nb = t / p.mtiles;
-            float2 acc[16];
+            // acc[h][j][s]: weight row r0 + 16 h + 8 s, activation rows c0 + 8 j + {0, 1}
+            float2 acc[2][4][2];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) acc[j] = make_float2(0.0f, 0.0f);
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[h][j][0] = acc[h][j][1] = make_float2(0.0f, 0.0f);
             for (int ks = 0; ks < ksteps && ok; ++ks, ++g) {
                 const int d = g % kDecBufs;
                 if (!wait_bar(&dec_full[d], (g / kDecBufs) & 1, &abort_flag, p.err, kErrWaitFull)) {
@@ -394,8 +406,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 const uint8_t *dec = smem + kOffDec + d * kDecBytes;
-                const float *swr = reinterpret_cast<const float *>(dec + kWOpBytes) + row * 8;
-                const float *dat = reinterpret_cast<const float *>(dec + kWOpBytes + kSwBytes) + cb * 32;
+                const float *swr = reinterpret_cast<const float *>(dec + kWOpBytes) + r0 * 8;
+                const float *dat = reinterpret_cast<const float *>(dec + kWOpBytes + kSwBytes) + c0;
 #pragma unroll
                 for (int sb = 0; sb < 8; ++sb) {
                     const int buf = (gsb + sb) % kTmemBufs;
@@ -406,28 +418,36 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     tc_fence_after();
                     uint32_t r[32];
-                    tmem_ld32(my_cols + buf * TN, r);
+                    tmem_ld_16x256b_2x4(ta + buf * TN, tb + buf * TN, r);
                     // the products are in registers: hand the buffer back to
                     // the MMA issuer before the arithmetic
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&tm_empty[buf]);
-                    const float sv = swr[sb];
-                    const float2 ss = make_float2(sv, sv);
-                    const float2 cm = make_float2(-kMagic * sv, -kMagic * sv);
-                    const float4 *dap = reinterpret_cast<const float4 *>(dat + sb * TN);
+                    // weight scales of rows r0 + 8 i (i = 2 h + s), activation scales of the columns
+                    float sv[4];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const float4 d4 = dap[j];  // activation scales of columns 4j .. 4j + 3
-                        // P + 0x4B400000 as an integer is the float 2^23 + 2^22 + P
-                        const float2 y0 = make_float2(__uint_as_float(r[4 * j] + kMagicBits),
-                                                      __uint_as_float(r[4 * j + 1] + kMagicBits));
-                        const float2 y1 = make_float2(__uint_as_float(r[4 * j + 2] + kMagicBits),
-                                                      __uint_as_float(r[4 * j + 3] + kMagicBits));
-                        const float2 t0 = __ffma2_rn(y0, ss, cm), t1 = __ffma2_rn(y1, ss, cm);
-                        acc[2 * j] = __ffma2_rn(t0, make_float2(d4.x, d4.y), acc[2 * j]);
-                        acc[2 * j + 1] = __ffma2_rn(t1, make_float2(d4.z, d4.w), acc[2 * j + 1]);
-                    }
+                    for (int i = 0; i < 4; ++i) sv[i] = swr[i * 64 + sb];
+                    float2 da[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) da[j] = *reinterpret_cast<const float2 *>(dat + sb * TN + 8 * j);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+#pragma unroll
+                        for (int ss = 0; ss < 2; ++ss) {
+                            const float s1 = sv[2 * h + ss];
+                            const float2 sc = make_float2(s1, s1);
+                            const float2 cm = make_float2(-kMagic * s1, -kMagic * s1);
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                // P + 0x4B400000 as an integer is the float 2^23 + 2^22 + P
+                                const uint32_t *q = r + 16 * h + 4 * j + 2 * ss;
+                                const float2 y = make_float2(__uint_as_float(q[0] + kMagicBits),
+                                                             __uint_as_float(q[1] + kMagicBits));
+                                const float2 tt = __ffma2_rn(y, sc, cm);
+                                acc[h][j][ss] = __ffma2_rn(tt, da[j], acc[h][j][ss]);
+                            }
+                        }
                 }
                 gsb += 8;
                 if (!ok) break;
@@ -435,17 +455,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) mbar_arrive(&dec_empty[d]);
             }
             if (!ok) break;
-            // epilogue: this thread's weight row n, activation rows of column block cb
-            const int64_t n = static_cast<int64_t>(nb) * TM + row;
-            if (n < p.n) {
-                const int64_t m0 = static_cast<int64_t>(mb) * TN + cb * 32;
+            // epilogue: C[m][n] for this thread's 4 weight rows x 8 activation rows
+            const int64_t m0 = static_cast<int64_t>(mb) * TN + c0;
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int64_t m = m0 + 2 * j;
-                    if (m < p.m) p.c[m * p.ldc + n] = acc[j].x;
-                    if (m + 1 < p.m) p.c[(m + 1) * p.ldc + n] = acc[j].y;
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int ss = 0; ss < 2; ++ss) {
+                    const int64_t n = static_cast<int64_t>(nb) * TM + r0 + 16 * h + 8 * ss;
+                    if (n >= p.n) continue;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int64_t m = m0 + 8 * j;
+                        if (m < p.m) p.c[m * p.ldc + n] = acc[h][j][ss].x;
+                        if (m + 1 < p.m) p.c[(m + 1) * p.ldc + n] = acc[h][j][ss].y;
+                    }
                 }
-            }
         }
         if (!ok) abort_flag = 1;
     }
