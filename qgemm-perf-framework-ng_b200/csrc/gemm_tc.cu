@@ -40,8 +40,8 @@
 // order -- the same operations in the same order as the mma.sync kernel, so
 // the results are bit-identical to it (unsplit).
 //
-// Loads read this GPU's memory only (W, the activation operand); no TMA
-// multicast.  Every wait is bounded; a wait that gives up records an error,
+// Loads read this GPU's memory only (W, the activation operand), each CTA
+// its own copy.  Every wait is bounded; a wait that gives up records an error,
 // raises the CTA's abort flag (which ends every other role's waits at once)
 // and the CTA frees its TMEM before returning.
 #include <cuda.h>
@@ -143,21 +143,40 @@ PFNG_DEV void umma_commit(uint64_t *bar) {
 
 // Two 16x256b.x4 loads (lanes base .. base + 15 at ta, base + 16 .. base + 31
 // at tb; 32 consecutive columns each) and their wait, as one statement.
-// Each load gives thread t, for column chunk j = 0..3, registers
+// Each load gives thread t, for column chunk j = 0..3, the values
 // 4 j + {0, 1} = lane t/4, columns 8 j + 2 (t % 4) + {0, 1} and
-// 4 j + {2, 3} = lane t/4 + 8, the same columns.
-PFNG_DEV void tmem_ld_16x256b_2x4(uint32_t ta, uint32_t tb, uint32_t (&r)[32]) {
+// 4 j + {2, 3} = lane t/4 + 8, the same columns; value v of the second load
+// is number 16 + v.  They come back packed in pairs (d[p] = values 2 p and
+// 2 p + 1), the operand pairs of the packed fmas.
+PFNG_DEV void tmem_ld_16x256b_2x4(uint32_t ta, uint32_t tb, uint64_t (&d)[16]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.16x256b.x4.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15}, [%32];\n\t"
-        "tcgen05.ld.sync.aligned.16x256b.x4.b32 {%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
-        "%29, %30, %31}, [%33];\n\t"
-        "tcgen05.wait::ld.sync.aligned;"
-        : PFNG_R32(r)
+        "{\n\t.reg .b32 a<32>;\n\t"
+        "tcgen05.ld.sync.aligned.16x256b.x4.b32 {a0, a1, a2, a3, a4, a5, a6, a7, a8, a9, a10, a11, a12, a13, a14, a15}, [%16];\n\t"
+        "tcgen05.ld.sync.aligned.16x256b.x4.b32 {a16, a17, a18, a19, a20, a21, a22, a23, a24, a25, a26, a27, a28, a29, a30, a31}, [%17];\n\t"
+        "tcgen05.wait::ld.sync.aligned;\n\t"
+        "mov.b64 %0, {a0, a1};\n\t"
+        "mov.b64 %1, {a2, a3};\n\t"
+        "mov.b64 %2, {a4, a5};\n\t"
+        "mov.b64 %3, {a6, a7};\n\t"
+        "mov.b64 %4, {a8, a9};\n\t"
+        "mov.b64 %5, {a10, a11};\n\t"
+        "mov.b64 %6, {a12, a13};\n\t"
+        "mov.b64 %7, {a14, a15};\n\t"
+        "mov.b64 %8, {a16, a17};\n\t"
+        "mov.b64 %9, {a18, a19};\n\t"
+        "mov.b64 %10, {a20, a21};\n\t"
+        "mov.b64 %11, {a22, a23};\n\t"
+        "mov.b64 %12, {a24, a25};\n\t"
+        "mov.b64 %13, {a26, a27};\n\t"
+        "mov.b64 %14, {a28, a29};\n\t"
+        "mov.b64 %15, {a30, a31};\n\t"
+        "}"
+        : "=l"(d[0]), "=l"(d[1]), "=l"(d[2]), "=l"(d[3]), "=l"(d[4]), "=l"(d[5]), "=l"(d[6]), "=l"(d[7]), "=l"(d[8]), "=l"(d[9]), "=l"(d[10]), "=l"(d[11]), "=l"(d[12]), "=l"(d[13]), "=l"(d[14]), "=l"(d[15])
         : "r"(ta), "r"(tb)
         : "memory");
 }
 #undef PFNG_R32
+
 
 // Shared-memory matrix descriptor, K-major operand with the 128-byte swizzle:
 // rows of 128 bytes, 8-row atoms of 1024 bytes stored back to back (stride
@@ -196,6 +215,18 @@ PFNG_DEV bool wait_bar(uint64_t *bar, uint32_t parity, const int *abort_flag, in
     return false;
 }
 PFNG_DEV bool aborted(const int *abort_flag) { return *reinterpret_cast<const volatile int *>(abort_flag) != 0; }
+// The same wait for the roles off the critical path (producer, MMA issuer,
+// decode): after each failed attempt the thread sleeps, so that its polling
+// does not take issue slots from the fold warps on its scheduler.
+PFNG_DEV bool wait_bar_sleep(uint64_t *bar, uint32_t parity, const int *abort_flag, int *err, int code) {
+    for (uint32_t i = 0; i < kWaitAttempts; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 15u) == 15u && *reinterpret_cast<const volatile int *>(abort_flag)) return false;
+        __nanosleep(128);
+    }
+    report_error(err, code);
+    return false;
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_q4_0_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a,
@@ -259,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int ks = 0; ks < ksteps; ++ks, ++g) {
                     const int s = g % kStages;
                     if (g >= kStages &&
-                        !wait_bar(&ld_empty[s], ((g / kStages) - 1) & 1, &abort_flag, p.err, kErrWaitEmpty)) {
+                        !wait_bar_sleep(&ld_empty[s], ((g / kStages) - 1) & 1, &abort_flag, p.err, kErrWaitEmpty)) {
                         abort_flag = 1;
                         break;
                     }
@@ -287,8 +318,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int t = blockIdx.x; t < ntiles_total && ok; t += gridDim.x) {
                 for (int ks = 0; ks < ksteps && ok; ++ks, ++g) {
                     const int s = g % kStages, d = g % kDecBufs;
-                    if (!wait_bar(&ld_full[s], (g / kStages) & 1, &abort_flag, p.err, kErrWaitFull) ||
-                        !wait_bar(&dec_full[d], (g / kDecBufs) & 1, &abort_flag, p.err, kErrWaitFull)) {
+                    if (!wait_bar_sleep(&ld_full[s], (g / kStages) & 1, &abort_flag, p.err, kErrWaitFull) ||
+                        !wait_bar_sleep(&dec_full[d], (g / kDecBufs) & 1, &abort_flag, p.err, kErrWaitFull)) {
                         ok = false;
                         break;
                     }
@@ -297,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint32_t aop = s_base + kOffStage + s * kStageBytes + kRawBytes;
                     for (int sb = 0; sb < 8; ++sb, ++gsb) {
                         const int buf = gsb % kTmemBufs;
-                        if (!wait_bar(&tm_empty[buf], (gsb / kTmemBufs) & 1, &abort_flag, p.err, kErrWaitEmpty)) {
+                        if (!wait_bar_sleep(&tm_empty[buf], (gsb / kTmemBufs) & 1, &abort_flag, p.err, kErrWaitEmpty)) {
                             ok = false;
                             break;
                         }
@@ -327,9 +358,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = blockIdx.x; t < ntiles_total && ok; t += gridDim.x) {
             for (int ks = 0; ks < ksteps; ++ks, ++g) {
                 const int s = g % kStages, d = g % kDecBufs;
-                if (!wait_bar(&ld_full[s], (g / kStages) & 1, &abort_flag, p.err, kErrWaitFull) ||
+                if (!wait_bar_sleep(&ld_full[s], (g / kStages) & 1, &abort_flag, p.err, kErrWaitFull) ||
                     (g >= kDecBufs &&
-                     !wait_bar(&dec_empty[d], ((g / kDecBufs) - 1) & 1, &abort_flag, p.err, kErrWaitEmpty))) {
+                     !wait_bar_sleep(&dec_empty[d], ((g / kDecBufs) - 1) & 1, &abort_flag, p.err, kErrWaitEmpty))) {
                     ok = false;
                     break;
                 }
@@ -417,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         continue;
                     }
                     tc_fence_after();
-                    uint32_t r[32];
+                    uint64_t r[16];
                     tmem_ld_16x256b_2x4(ta + buf * TN, tb + buf * TN, r);
                     // the products are in registers: hand the buffer back to
                     // the MMA issuer before the arithmetic
@@ -441,9 +472,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                             for (int j = 0; j < 4; ++j) {
                                 // P + 0x4B400000 as an integer is the float 2^23 + 2^22 + P
-                                const uint32_t *q = r + 16 * h + 4 * j + 2 * ss;
-                                const float2 y = make_float2(__uint_as_float(q[0] + kMagicBits),
-                                                             __uint_as_float(q[1] + kMagicBits));
+                                const uint64_t q = r[8 * h + 2 * j + ss];
+                                const float2 y = make_float2(__uint_as_float(static_cast<uint32_t>(q) + kMagicBits),
+                                                             __uint_as_float(static_cast<uint32_t>(q >> 32) + kMagicBits));
                                 const float2 tt = __ffma2_rn(y, sc, cm);
                                 acc[h][j][ss] = __ffma2_rn(tt, da[j], acc[h][j][ss]);
                             }
