@@ -9,7 +9,7 @@
 // Tile: 128 weight rows (the MMA's M, one TMEM lane each) x 128 activation
 // rows (the MMA's N, one TMEM column each), k-steps of 256.  The kernel is
 // persistent: CTA c takes tiles c, c + grid, ... with the m tiles fastest, so
-// the CTAs running together share their W tiles.  Warp roles (640 threads,
+// the CTAs running together share their W tiles.  Warp roles (576 threads,
 // one CTA per SM):
 //   warp 0      TMA producer: per k-step one 2-D tensor copy of the raw W
 //               rows (128 x 144 bytes; rows past n read as zeros), two of the
@@ -21,11 +21,16 @@
 //               K 32) per 32-deep sub-block into one of four TMEM buffers
 //               (512 columns), completion signalled with tcgen05.commit; the
 //               MMA overwrites its buffer (no accumulate), the fold reads it;
-//   warps 2, 3  decode: raw q4_0 blocks -> int8 (q - 8) operand rows in the
-//               swizzled layout, the per-(row, sub-block) weight scales, and
-//               the activation scales transposed to [sub-block][row];
-//   warps 4-19  fold: warp w reads TMEM lane quarter w % 4 and column block
-//               (w - 4) / 4 (32 activation rows) with two 16x256b loads per
+//   warps 2-17  decode and fold.  Decode: before folding k-step g each warp
+//               decodes its 1/16 of k-step g + 1 (8 weight rows: raw q4_0
+//               blocks -> int8 (q - 8) operand rows in the swizzled layout,
+//               their scales, and activation scales transposed to
+//               [sub-block][row]) -- spread over all 16 warps so that every
+//               scheduler carries the same load (with separate decode warps,
+//               the fold warps sharing a scheduler with them set the pace
+//               and the others waited for the MMA 20 % of the time).
+//               Fold: warp w reads TMEM lane quarter w % 4 and column block
+//               (w - 2) / 4 (32 activation rows) with two 16x256b loads per
 //               sub-block -- thread t holds weight rows t/4 + {0, 8, 16, 24}
 //               of the quarter and activation rows 8 j + 2 (t % 4) + {0, 1},
 //               j = 0..3, so one activation scale serves four rows and one
@@ -62,10 +67,9 @@ constexpr int kStages = 2;     // TMA load stages
 constexpr int kDecBufs = 2;    // decoded weight operand buffers
 constexpr int kTmemBufs = 4;   // sub-block products in TMEM
 constexpr uint32_t kTmemCols = kTmemBufs * TN;  // 512: all of TMEM
-constexpr int kThreads = 640;
+constexpr int kThreads = 576;
 constexpr int kFoldWarps = 16;
-constexpr int kFoldWarp0 = 4;
-constexpr int kDecodeWarps = 2;
+constexpr int kFoldWarp0 = 2;
 constexpr uint32_t kRawRow = 144;  // raw q4_0 bytes of one weight row per k-step
 constexpr uint32_t kMagicBits = 0x4B400000u;
 constexpr float kMagic = 12582912.0f;
@@ -215,14 +219,34 @@ PFNG_DEV bool wait_bar(uint64_t *bar, uint32_t parity, const int *abort_flag, in
     return false;
 }
 PFNG_DEV bool aborted(const int *abort_flag) { return *reinterpret_cast<const volatile int *>(abort_flag) != 0; }
-// The same wait for the roles off the critical path (producer, MMA issuer,
-// decode): after each failed attempt the thread sleeps, so that its polling
-// does not take issue slots from the fold warps on its scheduler.
+// The wait of the roles off the critical path (producer, MMA issuer): each
+// attempt may suspend the thread for up to 20 us (or until the phase
+// completes), so that its polling does not take issue slots from the fold
+// warps on its scheduler; the wait is bounded by ~1 s of wall time
+// (%globaltimer), whatever the suspensions actually last.
+PFNG_DEV uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+PFNG_DEV bool mbar_try_wait_long(uint64_t *bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 20000;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
 PFNG_DEV bool wait_bar_sleep(uint64_t *bar, uint32_t parity, const int *abort_flag, int *err, int code) {
-    for (uint32_t i = 0; i < kWaitAttempts; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 15u) == 15u && *reinterpret_cast<const volatile int *>(abort_flag)) return false;
-        __nanosleep(128);
+    if (mbar_try_wait_long(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        if (mbar_try_wait_long(bar, parity)) return true;
+        if (*reinterpret_cast<const volatile int *>(abort_flag)) return false;
+        if (global_ns() - t0 > 1000000000ull) break;
     }
     report_error(err, code);
     return false;
@@ -231,12 +255,14 @@ PFNG_DEV bool wait_bar_sleep(uint64_t *bar, uint32_t parity, const int *abort_fl
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_q4_0_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_a,
                         const __grid_constant__ CUtensorMap map_ad, const TcParams p) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023u) & ~uintptr_t(1023));
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // the 1024-byte aligned base as an offset into the shared array, so that
+    // the compiler keeps shared-memory (not generic) accesses
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kOffBar);
     uint64_t *ld_full = bars;                          // [kStages]  TMA transaction count
-    uint64_t *ld_empty = ld_full + kStages;            // [kStages]  MMA commit (1) + decode warps
-    uint64_t *dec_full = ld_empty + kStages;           // [kDecBufs] decode warps
+    uint64_t *ld_empty = ld_full + kStages;            // [kStages]  MMA commit (1) + fold warps (decode)
+    uint64_t *dec_full = ld_empty + kStages;           // [kDecBufs] fold warps (decode)
     uint64_t *dec_empty = dec_full + kDecBufs;         // [kDecBufs] MMA commit (1) + fold warps
     uint64_t *tm_full = dec_empty + kDecBufs;          // [kTmemBufs] MMA commit (1)
     uint64_t *tm_empty = tm_full + kTmemBufs;          // [kTmemBufs] fold warps
@@ -252,10 +278,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         abort_flag = 0;
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&ld_full[s], 1);
-            mbar_init(&ld_empty[s], 1 + kDecodeWarps);
+            mbar_init(&ld_empty[s], 1 + kFoldWarps);
         }
         for (int d = 0; d < kDecBufs; ++d) {
-            mbar_init(&dec_full[d], kDecodeWarps);
+            mbar_init(&dec_full[d], kFoldWarps);
             mbar_init(&dec_empty[d], 1 + kFoldWarps);
         }
         for (int b = 0; b < kTmemBufs; ++b) {
@@ -350,65 +376,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!mbar_wait(mma_done, 0, p.err, kErrWaitFull)) abort_flag = 1;
         }
         __syncwarp();
-    } else if (warp < kFoldWarp0) {
-        // ---------------- decode: 64 threads, 16 (row, block) tasks each ----------------
-        const int dt = (warp - 2) * 32 + lane;  // 0..63
-        int g = 0;
-        bool ok = true;
-        for (int t = blockIdx.x; t < ntiles_total && ok; t += gridDim.x) {
-            for (int ks = 0; ks < ksteps; ++ks, ++g) {
-                const int s = g % kStages, d = g % kDecBufs;
-                if (!wait_bar_sleep(&ld_full[s], (g / kStages) & 1, &abort_flag, p.err, kErrWaitFull) ||
-                    (g >= kDecBufs &&
-                     !wait_bar_sleep(&dec_empty[d], ((g / kDecBufs) - 1) & 1, &abort_flag, p.err, kErrWaitEmpty))) {
-                    ok = false;
-                    break;
-                }
-                const uint8_t *raw = smem + kOffStage + s * kStageBytes;
-                uint8_t *dec = smem + kOffDec + d * kDecBytes;
-                float *sw = reinterpret_cast<float *>(dec + kWOpBytes);
-#pragma unroll 4
-                for (int i = 0; i < (TM * 8) / (kDecodeWarps * 32); ++i) {
-                    const int task = dt + i * kDecodeWarps * 32;  // (row, block)
-                    const int row = task >> 3, u = task & 7;
-                    uint32_t q[4], dbits;
-                    load_q4_0_block_smem(raw, row * kRawRow + 18u * u, q, dbits);
-                    // q - 8 per byte: set bit 7, subtract 8 (no borrow crosses a byte), clear bit 7 again
-                    uint4 lo, hi;
-                    lo.x = (((q[0] & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
-                    lo.y = (((q[1] & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
-                    lo.z = (((q[2] & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
-                    lo.w = (((q[3] & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
-                    hi.x = ((((q[0] >> 4) & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
-                    hi.y = ((((q[1] >> 4) & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
-                    hi.z = ((((q[2] >> 4) & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
-                    hi.w = ((((q[3] >> 4) & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
-                    // the 8 threads of a row store together: order the two chunks so
-                    // that each store instruction covers 8 distinct bank groups
-                    const bool swap = u >= 4;
-                    *reinterpret_cast<uint4 *>(dec + op_off(row, swap ? 2 * u + 1 : 2 * u)) = swap ? hi : lo;
-                    *reinterpret_cast<uint4 *>(dec + op_off(row, swap ? 2 * u : 2 * u + 1)) = swap ? lo : hi;
-                    sw[row * 8 + u] = f16_bits_to_f32(dbits);
-                }
-                // activation scales, transposed to [sub-block][row]
-                const float *dar = reinterpret_cast<const float *>(raw + kRawBytes + kActBytes);
-                float *dat = reinterpret_cast<float *>(dec + kWOpBytes + kSwBytes);
-#pragma unroll 4
-                for (int i = 0; i < (TN * 8) / (kDecodeWarps * 32); ++i) {
-                    const int e = dt + i * kDecodeWarps * 32;  // e = sb * TN + activation row
-                    dat[e] = dar[(e % TN) * 8 + e / TN];
-                }
-                fence_proxy_async_smem();  // the decoded operand is read by the tensor cores
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&dec_full[d]);
-                    mbar_arrive(&ld_empty[s]);
-                }
-            }
-        }
-        if (!ok) abort_flag = 1;
     } else {
-        // ---------------- fold (warps 4..19) ----------------
+        // ---------------- decode + fold (warps 2..17) ----------------
         const int fw = warp - kFoldWarp0;
         const int qtr = warp & 3;                // TMEM lane quarter this warp may access
         const int cb = fw >> 2;                  // activation rows 32 cb .. 32 cb + 31 of the tile
@@ -416,91 +385,154 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int c0 = cb * 32 + 2 * (lane & 3); // activation rows c0 + 8 j + {0, 1}
         const uint32_t ta = tmem_base + (static_cast<uint32_t>(qtr * 32) << 16) + static_cast<uint32_t>(cb * 32);
         const uint32_t tb = ta + (16u << 16);
+        // k-steps of this CTA: global index g = tile i * ksteps + ks
+        const int my_tiles = (ntiles_total - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                             static_cast<int>(gridDim.x);
+        const int total = my_tiles * ksteps;
         // every TMEM buffer starts free
         if (lane == 0)
             for (int b = 0; b < kTmemBufs; ++b) mbar_arrive(&tm_empty[b]);
 
-        int g = 0, gsb = 0;
-        bool ok = true;
-        for (int t = blockIdx.x; t < ntiles_total && ok; t += gridDim.x) {
-            const int mb = t % p.mtiles, nb = t / p.mtiles;
-            // acc[h][j][s]: weight row r0 + 16 h + 8 s, activation rows c0 + 8 j + {0, 1}
-            float2 acc[2][4][2];
+        // this warp's share of k-step gg: weight rows 8 fw .. 8 fw + 7 (two
+        // blocks per thread) and 64 transposed activation scales
+        auto decode = [&](int gg) -> bool {
+            const int s = gg % kStages, d = gg % kDecBufs;
+            if (!wait_bar(&ld_full[s], (gg / kStages) & 1, &abort_flag, p.err, kErrWaitFull) ||
+                (gg >= kDecBufs &&
+                 !wait_bar(&dec_empty[d], ((gg / kDecBufs) - 1) & 1, &abort_flag, p.err, kErrWaitEmpty)))
+                return false;
+            const uint8_t *raw = smem + kOffStage + s * kStageBytes;
+            uint8_t *dec = smem + kOffDec + d * kDecBytes;
+            float *sw = reinterpret_cast<float *>(dec + kWOpBytes);
 #pragma unroll
-            for (int h = 0; h < 2; ++h)
+            for (int i = 0; i < 2; ++i) {
+                const int task = fw * 64 + i * 32 + lane;  // (row, block)
+                const int row = task >> 3, u = task & 7;
+                uint32_t q[4], dbits;
+                load_q4_0_block_smem(raw, row * kRawRow + 18u * u, q, dbits);
+                // q - 8 per byte: set bit 7, subtract 8 (no borrow crosses a byte), clear bit 7 again
+                uint4 lo, hi;
+                lo.x = (((q[0] & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
+                lo.y = (((q[1] & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
+                lo.z = (((q[2] & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
+                lo.w = (((q[3] & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
+                hi.x = ((((q[0] >> 4) & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
+                hi.y = ((((q[1] >> 4) & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
+                hi.z = ((((q[2] >> 4) & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
+                hi.w = ((((q[3] >> 4) & 0x0f0f0f0fu) | 0x80808080u) - 0x08080808u) ^ 0x80808080u;
+                // the 8 threads of a row store together: order the two chunks so
+                // that each store instruction covers 8 distinct bank groups
+                const bool swap = u >= 4;
+                *reinterpret_cast<uint4 *>(dec + op_off(row, swap ? 2 * u + 1 : 2 * u)) = swap ? hi : lo;
+                *reinterpret_cast<uint4 *>(dec + op_off(row, swap ? 2 * u : 2 * u + 1)) = swap ? lo : hi;
+                sw[row * 8 + u] = f16_bits_to_f32(dbits);
+            }
+            // activation scales, transposed to [sub-block][row]
+            const float *dar = reinterpret_cast<const float *>(raw + kRawBytes + kActBytes);
+            float *dat = reinterpret_cast<float *>(dec + kWOpBytes + kSwBytes);
 #pragma unroll
-                for (int j = 0; j < 4; ++j) acc[h][j][0] = acc[h][j][1] = make_float2(0.0f, 0.0f);
-            for (int ks = 0; ks < ksteps && ok; ++ks, ++g) {
-                const int d = g % kDecBufs;
-                if (!wait_bar(&dec_full[d], (g / kDecBufs) & 1, &abort_flag, p.err, kErrWaitFull)) {
+            for (int i = 0; i < 2; ++i) {
+                const int e = fw * 64 + i * 32 + lane;  // e = sb * TN + activation row
+                dat[e] = dar[(e % TN) * 8 + e / TN];
+            }
+            fence_proxy_async_smem();  // the decoded operand is read by the tensor cores
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&dec_full[d]);
+                mbar_arrive(&ld_empty[s]);
+            }
+            return true;
+        };
+
+        bool ok = total == 0 || decode(0);
+        // acc[h][j][s]: weight row r0 + 16 h + 8 s, activation rows c0 + 8 j + {0, 1}
+        float2 acc[2][4][2];
+        for (int g = 0; g < total && ok; ++g) {
+            const int ks = g % ksteps;
+            if (ks == 0) {
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) acc[h][j][0] = acc[h][j][1] = make_float2(0.0f, 0.0f);
+            }
+            // the next k-step's decode first, then this one's fold
+            if (g + 1 < total && !decode(g + 1)) {
+                ok = false;
+                break;
+            }
+            const int d = g % kDecBufs;
+            if (!wait_bar(&dec_full[d], (g / kDecBufs) & 1, &abort_flag, p.err, kErrWaitFull)) {
+                ok = false;
+                break;
+            }
+            const uint8_t *dec = smem + kOffDec + d * kDecBytes;
+            const float *swr = reinterpret_cast<const float *>(dec + kWOpBytes) + r0 * 8;
+            const float *dat = reinterpret_cast<const float *>(dec + kWOpBytes + kSwBytes) + c0;
+            // the sub-block counter advances by 8 (twice the buffer count) per
+            // k-step, so each sub-block's buffer and phase parity are constants
+            static_assert(kTmemBufs == 4, "buffer = sb % 4, parity = sb / 4");
+#pragma unroll
+            for (int sb = 0; sb < 8; ++sb) {
+                const int buf = sb & 3;
+                if (!wait_bar(&tm_full[buf], (sb >> 2) & 1, &abort_flag, p.err, kErrWaitFull)) {
                     ok = false;
                     break;
                 }
-                const uint8_t *dec = smem + kOffDec + d * kDecBytes;
-                const float *swr = reinterpret_cast<const float *>(dec + kWOpBytes) + r0 * 8;
-                const float *dat = reinterpret_cast<const float *>(dec + kWOpBytes + kSwBytes) + c0;
-#pragma unroll
-                for (int sb = 0; sb < 8; ++sb) {
-                    const int buf = (gsb + sb) % kTmemBufs;
-                    if (!ok || !wait_bar(&tm_full[buf], ((gsb + sb) / kTmemBufs) & 1, &abort_flag, p.err,
-                                         kErrWaitFull)) {
-                        ok = false;
-                        continue;
-                    }
-                    tc_fence_after();
-                    uint64_t r[16];
-                    tmem_ld_16x256b_2x4(ta + buf * TN, tb + buf * TN, r);
-                    // the products are in registers: hand the buffer back to
-                    // the MMA issuer before the arithmetic
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&tm_empty[buf]);
-                    // weight scales of rows r0 + 8 i (i = 2 h + s), activation scales of the columns
-                    float sv[4];
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) sv[i] = swr[i * 64 + sb];
-                    float2 da[4];
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) da[j] = *reinterpret_cast<const float2 *>(dat + sb * TN + 8 * j);
-#pragma unroll
-                    for (int h = 0; h < 2; ++h)
-#pragma unroll
-                        for (int ss = 0; ss < 2; ++ss) {
-                            const float s1 = sv[2 * h + ss];
-                            const float2 sc = make_float2(s1, s1);
-                            const float2 cm = make_float2(-kMagic * s1, -kMagic * s1);
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                // P + 0x4B400000 as an integer is the float 2^23 + 2^22 + P
-                                const uint64_t q = r[8 * h + 2 * j + ss];
-                                const float2 y = make_float2(__uint_as_float(static_cast<uint32_t>(q) + kMagicBits),
-                                                             __uint_as_float(static_cast<uint32_t>(q >> 32) + kMagicBits));
-                                const float2 tt = __ffma2_rn(y, sc, cm);
-                                acc[h][j][ss] = __ffma2_rn(tt, da[j], acc[h][j][ss]);
-                            }
-                        }
-                }
-                gsb += 8;
-                if (!ok) break;
+                tc_fence_after();
+                uint64_t r[16];
+                tmem_ld_16x256b_2x4(ta + buf * TN, tb + buf * TN, r);
+                // the products are in registers: hand the buffer back to
+                // the MMA issuer before the arithmetic
+                tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&dec_empty[d]);
+                if (lane == 0) mbar_arrive(&tm_empty[buf]);
+                // weight scales of rows r0 + 8 i (i = 2 h + s), activation scales of the columns
+                float sv[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) sv[i] = swr[i * 64 + sb];
+                float2 da[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) da[j] = *reinterpret_cast<const float2 *>(dat + sb * TN + 8 * j);
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int ss = 0; ss < 2; ++ss) {
+                        const float s1 = sv[2 * h + ss];
+                        const float2 sc = make_float2(s1, s1);
+                        const float2 cm = make_float2(-kMagic * s1, -kMagic * s1);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            // P + 0x4B400000 as an integer is the float 2^23 + 2^22 + P
+                            const uint64_t q = r[8 * h + 2 * j + ss];
+                            const float2 y = make_float2(__uint_as_float(static_cast<uint32_t>(q) + kMagicBits),
+                                                         __uint_as_float(static_cast<uint32_t>(q >> 32) + kMagicBits));
+                            const float2 tt = __ffma2_rn(y, sc, cm);
+                            acc[h][j][ss] = __ffma2_rn(tt, da[j], acc[h][j][ss]);
+                        }
+                    }
             }
             if (!ok) break;
-            // epilogue: C[m][n] for this thread's 4 weight rows x 8 activation rows
-            const int64_t m0 = static_cast<int64_t>(mb) * TN + c0;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&dec_empty[d]);
+            if (ks == ksteps - 1) {
+                // epilogue: C[m][n] for this thread's 4 weight rows x 8 activation rows
+                const int t = static_cast<int>(blockIdx.x) + (g / ksteps) * static_cast<int>(gridDim.x);
+                const int mb = t % p.mtiles, nb = t / p.mtiles;
+                const int64_t m0 = static_cast<int64_t>(mb) * TN + c0;
 #pragma unroll
-            for (int h = 0; h < 2; ++h)
+                for (int h = 0; h < 2; ++h)
 #pragma unroll
-                for (int ss = 0; ss < 2; ++ss) {
-                    const int64_t n = static_cast<int64_t>(nb) * TM + r0 + 16 * h + 8 * ss;
-                    if (n >= p.n) continue;
+                    for (int ss = 0; ss < 2; ++ss) {
+                        const int64_t n = static_cast<int64_t>(nb) * TM + r0 + 16 * h + 8 * ss;
+                        if (n >= p.n) continue;
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const int64_t m = m0 + 8 * j;
-                        if (m < p.m) p.c[m * p.ldc + n] = acc[h][j][ss].x;
-                        if (m + 1 < p.m) p.c[(m + 1) * p.ldc + n] = acc[h][j][ss].y;
+                        for (int j = 0; j < 4; ++j) {
+                            const int64_t m = m0 + 8 * j;
+                            if (m < p.m) p.c[m * p.ldc + n] = acc[h][j][ss].x;
+                            if (m + 1 < p.m) p.c[(m + 1) * p.ldc + n] = acc[h][j][ss].y;
+                        }
                     }
-                }
+            }
         }
         if (!ok) abort_flag = 1;
     }
