@@ -689,7 +689,9 @@ def one_config(args) -> int:
         r = sweep_decode(ctx, args)
     else:
         r = sweep_small(ctx, args, args.wtype, args.m, args.n, args.k, 0.02 if args.wtype == "q4_0" else 1.0)
-    print(json.dumps(dict(workload=args.workload, wtype=args.wtype, m=args.m, n=args.n, k=args.k, **r)), flush=True)
+    line = dict(workload=args.workload, wtype=args.wtype, m=args.m, n=args.n, k=args.k)
+    line.update(r)
+    print(json.dumps(line), flush=True)
     return 0
 
 
