@@ -412,7 +412,10 @@ def launches_per_step(world: int, rank: int) -> int:
     """Kernels of this library one headline step launches on this rank."""
     if world == 1:
         return 2  # activation quantizer (split operand), GEMM
-    return (1 if rank == 0 else 0) + 3  # q8_0 quantizer on rank 0; q8_0 -> operand, GEMM, peer-store copies
+    # q8_0 quantizer on rank 0; q8_0 -> operand; the GEMM as two row bands
+    # (their copies to the peers run on copy engines), or one GEMM and the
+    # peer-store copy kernel for products under four 128-row tiles
+    return (1 if rank == 0 else 0) + 3
 
 
 def headline(ctx: Ctx, args) -> dict:

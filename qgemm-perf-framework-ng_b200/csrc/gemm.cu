@@ -30,6 +30,7 @@
 // reference only by where fp32 rounding happens.
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 
 #include <cuda_bf16.h>
 
@@ -1174,7 +1175,13 @@ constexpr bool kOvType = WT != kWQ4_K;
 // (<= 128 registers, no spills; q4_K 32x11008x4096 35.8 -> 31.3 us).  On 128 x 128
 // tiles the direct two-phase kernel also beats the overlapped decode:
 // 2048x11008x4096 589.6 vs 622.7, 2048x4096x4096 242.4 vs 255.4,
-// 512x4096x4096 62.4 vs 65.5, 2048x4096x11008 629.8 vs 661.5.
+// 512x4096x4096 62.4 vs 65.5, 2048x4096x11008 629.8 vs 661.5.  Two variants
+// of the 128 x 128 direct kernel gave the same bits and were slower
+// (2048x32000x4096 / 2048x11008x4096 / 512x4096x4096, us): 16 warps of
+// 64 x 16 (128 registers) 1705 / 621 / 64.8, and float4 fold constants that
+// each warp converts once per k-step into shared memory 1651 / 601 / 63.3,
+// against 1639 / 597 / 62.8 for 8 warps of 64 x 32 converting the fp16
+// scales in the sub-block loop.
 inline bool direct_enabled() {
     const char *e = std::getenv("PFNG_B200_GEMM_DIRECT");
     return !(e && std::strcmp(e, "0") == 0);
@@ -1326,9 +1333,125 @@ bool m_fast_raster(const GemmParams &p, int bm, int bn) {
     return p.m > bm && a_bytes <= (48LL << 20);
 }
 
+// Row bands of a product whose C also goes to other destinations (the
+// all-gather of row-sharded weights): the first band's rows are copied to
+// the destinations while the second band is computed, so that part of the
+// transfer over NVLink overlaps the GEMM instead of following it.  Every tile
+// is computed exactly as without bands (bit-identical C).  The split puts
+// the smallest last band under which the first band's copies still finish:
+// with r = copy time / GEMM time per row ~ 1100 x destinations / k (measured
+// on B200: ~330 Top/s for the GEMM, ~600 GB/s out over NVLink), the last
+// band takes r / (1 + r) of the 128-row tiles.  Measured on two B200s at
+// 2048 x 32000 x 4096 (us per sharded step): no bands 1101; two equal bands
+// 1005, four 1077, eight 1061 (copy engines); four with the push kernel
+// 1084.  Products of fewer than four 128-row tiles run unbanded;
+// PFNG_B200_GATHER_BANDS=1 turns the bands off.
+int gather_split_tiles(const GemmParams &p, int64_t tiles) {
+    if (const char *e = std::getenv("PFNG_B200_GATHER_BANDS"))
+        if (std::strcmp(e, "1") == 0) return 0;
+    if (tiles < 4) return 0;
+    const double r = 1100.0 * p.ncopies / static_cast<double>(p.k);
+    int64_t last = static_cast<int64_t>(tiles * r / (1.0 + r) + 0.999);
+    if (last < 1) last = 1;
+    if (last > tiles - 1) last = tiles - 1;
+    return static_cast<int>(tiles - last);
+}
+
+// Side streams (one per destination, high priority) and their events, one
+// set per device, created on first use.
+struct SideStreams {
+    cudaStream_t stream[kMaxCopies] = {};
+    cudaEvent_t band = nullptr;
+    cudaEvent_t join[kMaxCopies] = {};
+    bool ready = false;
+};
+SideStreams g_side[64];
+std::mutex g_side_mutex;  // also serialises the banded launch sequences of concurrent host threads
+
+cudaError_t side_streams(SideStreams **out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    SideStreams &ss = g_side[dev];
+    if (!ss.ready) {
+        int least = 0, greatest = 0;
+        if ((e = cudaDeviceGetStreamPriorityRange(&least, &greatest)) != cudaSuccess) return e;
+        for (int i = 0; i < kMaxCopies; ++i) {
+            if ((e = cudaStreamCreateWithPriority(&ss.stream[i], cudaStreamNonBlocking, greatest)) != cudaSuccess)
+                return e;
+            if ((e = cudaEventCreateWithFlags(&ss.join[i], cudaEventDisableTiming)) != cudaSuccess) return e;
+        }
+        if ((e = cudaEventCreateWithFlags(&ss.band, cudaEventDisableTiming)) != cudaSuccess) return e;
+        ss.ready = true;
+    }
+    *out = &ss;
+    return cudaSuccess;
+}
+
+template <int WT, bool kPartials>
+cudaError_t launch_tile(GemmParams &p, cudaStream_t s);
+
+// Rows [r0, r1) of the product (the activation operand and every output
+// offset to them).
+GemmParams row_band(const GemmParams &p, int64_t r0, int64_t r1, int64_t blk) {
+    GemmParams q = p;
+    q.m = r1 - r0;
+    q.c = p.c + r0 * p.ldc;
+    q.a.qs = p.a.qs + r0 * p.k;
+    q.a.d = p.a.d + r0 * (p.k / blk);
+    q.a.aux = p.a.aux + r0 * (p.k / 32);
+    q.a.rows_pad = p.a.rows_pad - r0;
+    for (int d = 0; d < p.ncopies; ++d) q.copies[d] = p.copies[d] + r0 * p.ldc;
+    return q;
+}
+
+// Copies of rows [0, q.m) of q.c to q's destinations, each destination on
+// its own side stream (the copy engines work on them in parallel).
+cudaError_t copy_band(const GemmParams &q, SideStreams *side) {
+    const size_t pitch = static_cast<size_t>(q.ldc) * sizeof(float);
+    for (int d = 0; d < q.ncopies; ++d) {
+        cudaError_t e = cudaStreamWaitEvent(side->stream[d], side->band, 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpy2DAsync(q.copies[d], pitch, q.c, pitch, static_cast<size_t>(q.n) * sizeof(float),
+                                  static_cast<size_t>(q.m), cudaMemcpyDeviceToDevice, side->stream[d]);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+template <int WT>
+cudaError_t launch_banded_gather(const GemmParams &p, cudaStream_t s, int64_t split_rows) {
+    std::lock_guard<std::mutex> lock(g_side_mutex);
+    SideStreams *side = nullptr;
+    cudaError_t e = side_streams(&side);
+    if (e != cudaSuccess) return e;
+    const int64_t blk = kQ8_0Act<WT> ? 32 : 256;
+    const int64_t bounds[3] = {0, split_rows, p.m};
+    for (int b = 0; b < 2; ++b) {
+        const GemmParams q = row_band(p, bounds[b], bounds[b + 1], blk);
+        GemmParams g = q;
+        g.ncopies = 0;
+        if ((e = launch_tile<WT, false>(g, s)) != cudaSuccess) return e;
+        if ((e = cudaEventRecord(side->band, s)) != cudaSuccess) return e;
+        if ((e = copy_band(q, side)) != cudaSuccess) return e;
+    }
+    // the caller's stream continues once every copy has landed
+    for (int d = 0; d < p.ncopies; ++d) {
+        if ((e = cudaEventRecord(side->join[d], side->stream[d])) != cudaSuccess) return e;
+        if ((e = cudaStreamWaitEvent(s, side->join[d], 0)) != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
 template <int WT, bool kPartials>
 cudaError_t launch_tile(GemmParams &p, cudaStream_t s) {
     if (p.ncopies > 0 && p.out_format == kOutF32 && push_copies()) {
+        if constexpr (!kPartials) {
+            const int64_t tiles = (p.m + kGemmTileM - 1) / kGemmTileM;
+            const int split = gather_split_tiles(p, tiles);
+            if (split > 0) return launch_banded_gather<WT>(p, s, split * kGemmTileM);
+        }
         GemmParams q = p;
         q.ncopies = 0;
         cudaError_t e = launch_tile<WT, kPartials>(q, s);

@@ -2,7 +2,9 @@
 
 * One process: every destination must hold exactly what pfng_b200_compute_*
   writes for the same arguments (bit for bit, on every path, with split-K
-  and ragged shapes, copies written by the push kernel or by the GEMM
+  and ragged shapes; copies written by the push kernel, by copy engines
+  per row band (from four 128-row tiles the product runs as two bands and
+  the first band's copies overlap the second band's GEMM), or by the GEMM
   epilogue), and nothing outside the [m][n] window of its rows; the
   pre-quantized entry (mm_gather) likewise equals mm().
 * Two processes through CUDA IPC (GatheredC): each rank computes the columns
@@ -36,6 +38,8 @@ CASES = [
     ("q4_0", "mma", 2048, 256, 512), ("q4_0", "gemv", 1, 300, 1024), ("q4_0", "gemv", 5, 96, 512),
     ("q4_0", "simple", 3, 40, 256), ("q4_K", "mma", 70, 256, 1536), ("iq2_xxs", "mma", 40, 192, 512),
     ("q4_0_planar", "mma", 200, 384, 2048),
+    # two row bands (the split follows the destination count and k; ragged second band in the first two)
+    ("q4_0", "mma", 1100, 640, 1024), ("q4_K", "mma", 600, 256, 1536), ("iq2_xxs", "mma", 1024, 192, 512),
 ]
 
 
