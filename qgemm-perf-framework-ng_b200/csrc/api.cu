@@ -361,6 +361,7 @@ SplitA split_a_carve(void *workspace, int64_t m, int64_t k, int block) {
     SplitA s{};
     s.rows_pad = round_up(m, kGemmTileM);
     s.k = k;
+    s.d_ld = s.rows_pad;
     uint8_t *p = static_cast<uint8_t *>(align_ptr(workspace, 256));
     s.qs = reinterpret_cast<int8_t *>(p);
     p += round_up(s.rows_pad * k, 256);

@@ -7,8 +7,8 @@
 // bench/llama_reference/llama_reference.cpp:113-205.
 //
 // CTA tile BM x BN (64..128 each, chosen per shape to fill the SMs), k-step
-// 256, 8 warps (2 along m, 4 along n), a 3-stage cp.async ring for the A
-// rows, A scales and raw W bytes.  Each k-step the CTA unpacks its raw W tile
+// 256, 8 warps (2 along m and 4 along n; 1 x 8 on 128 x 128 q4_0 tiles), a
+// 3-stage cp.async ring for the A rows, A scales and raw W bytes.  Each k-step the CTA unpacks its raw W tile
 // once into an int8 [n][k] tile (q4_0: nibble - 8; q4_K: nibble; iq2_xxs:
 // signed grid value) and a per-(sub-block, column) scale s, then every
 // 32-deep sub-block is one m16n8k32 s8 MMA per 16 x 8 fragment.
@@ -58,18 +58,21 @@ constexpr uint32_t kMaxSmemPerCta = 227 * 1024;  // opt-in dynamic shared memory
 constexpr uint32_t kWRowSlot = 160;          // >= 144 raw bytes + 8 window slack, multiple of 16
 constexpr int kAScaleStride = 12;
 
-template <int BM_, int BN_, int ST_ = kStages, uint32_t SLOT_ = kWRowSlot>
+template <int BM_, int BN_, int ST_ = kStages, uint32_t SLOT_ = kWRowSlot, int WGM_ = 2>
 struct Cfg {
     static constexpr int BM = BM_, BN = BN_;
     static constexpr int ST = ST_;  // cp.async ring depth of the two-phase kernel
     static constexpr uint32_t kSlot = SLOT_;  // bytes per raw W row in shared memory
-    static constexpr int WM = BM / 2, WN = BN / 4;  // warp tile
+    // the 8 warps as WGM along m x WGN along n
+    static constexpr int WGM = WGM_, WGN = 8 / WGM_;
+    static constexpr int WM = BM / WGM, WN = BN / WGN;  // warp tile
     static constexpr int MT = WM / 16, NT = WN / 8;  // m16n8 fragments per warp
     static_assert(MT >= 1 && NT >= 2 && NT % 2 == 0, "tile shape");
     // shared memory (per stage, then single buffers)
     static constexpr uint32_t kAQs = BM * BK;
-    // q4_0: d per (row, sub-block); q8_K: bsum32 per (row, sub-block).  Rows are
-    // kAScaleStride words apart so that 8 consecutive rows hit 8 distinct banks.
+    // q8_0: d per (sub-block, row) as [kb][g][BM / 8] (load_a); q8_K: bsum32
+    // per (row, sub-block), rows kAScaleStride words apart so that 8
+    // consecutive rows hit 8 distinct banks.
     static constexpr uint32_t kAScale = BM * kAScaleStride * 4;
     static constexpr uint32_t kAD8K = BM * 4;        // q8_K: d per row
     static constexpr uint32_t kWRaw = BN * kSlot;
@@ -191,10 +194,19 @@ PFNG_DEV void load_a(const GemmParams &p, int8_t *a_qs, float *a_scale, float *a
         cp_async16(a_qs + swz(row, ch), p.a.qs + (m0 + row) * K + ks * BK + ch * 16, 16);
     }
     if (tid < C::BM * 2) {
-        const int row = tid >> 1, half = tid & 1;
-        const void *src = kQ8_0Act<WT> ? static_cast<const void *>(p.a.d + (m0 + row) * (K / 32) + ks * 8 + half * 4)
-                                  : static_cast<const void *>(p.a.aux + (m0 + row) * (K / 32) + ks * 8 + half * 4);
-        cp_async16(a_scale + row * kAScaleStride + half * 4, src, 16);
+        if constexpr (kQ8_0Act<WT>) {
+            // q8_0 scales of the 8 blocks of k-step ks: stage layout
+            // [kb][g][BM / 8], row 8 j + g of the tile at j (split_d_index's
+            // order restricted to the tile's rows), BM / 32 chunks per (kb, g)
+            constexpr int kChunks = C::BM / 32;
+            const int kbg = tid / kChunks, c = tid % kChunks;
+            const int kb = kbg >> 3, g = kbg & 7;
+            const float *src = p.a.d + (ks * 8 + kb) * p.a.d_ld + (m0 & ~int64_t(127)) + g * 16 + ((m0 & 127) >> 3) + 4 * c;
+            cp_async16(a_scale + kbg * (C::BM / 8) + 4 * c, src, 16);
+        } else {
+            const int row = tid >> 1, half = tid & 1;
+            cp_async16(a_scale + row * kAScaleStride + half * 4, p.a.aux + (m0 + row) * (K / 32) + ks * 8 + half * 4, 16);
+        }
     }
     if constexpr (!kQ8_0Act<WT>) {
         if (tid < C::BM) cp_async4(a_d8k + tid, p.a.d + (m0 + tid) * (K / 256) + ks, 4);
@@ -563,7 +575,7 @@ __global__ void __launch_bounds__(kThreads, kDirect && (C::BM == 64 || (C::BM ==
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const Smem<C> sm{smem_raw};
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int wm = warp >> 2, wn = warp & 3;
+    const int wm = warp / C::WGN, wn = warp % C::WGN;
     const int g = lane >> 2, t4 = lane & 3;
     int64_t m0, n0;
     tile_origin<C>(p, m0, n0);
@@ -687,12 +699,31 @@ __global__ void __launch_bounds__(kThreads, kDirect && (C::BM == 64 || (C::BM ==
             // same bits.
             uint32_t shs[2][NT];
             float dan[2][MT][2];
+            // the q8_0 scales of this thread's rows for sub-block kb: rows
+            // wm WM + 16 mt + 8 h + g sit at j = wm WM / 8 + 2 mt + h of
+            // the stage's [kb][g][BM / 8] layout, four per 16-byte load
+            auto load_da = [&](int kb, float(&d)[MT][2]) {
+                if constexpr (kQ8_0Act<WT>) {
+                    const float *base = sm.a_scale(s) + (kb * 8 + g) * (C::BM / 8) + wm * (C::WM / 8);
+                    if constexpr (MT % 2 == 0) {
 #pragma unroll
-            for (int mt = 0; mt < MT; ++mt)
+                        for (int q = 0; q < MT / 2; ++q) {
+                            const float4 v = *reinterpret_cast<const float4 *>(base + 4 * q);
+                            d[2 * q][0] = v.x, d[2 * q][1] = v.y, d[2 * q + 1][0] = v.z, d[2 * q + 1][1] = v.w;
+                        }
+                    } else {
+                        static_assert(MT == 1, "one m16 fragment per warp, or an even count");
+                        const float2 v = *reinterpret_cast<const float2 *>(base);
+                        d[0][0] = v.x, d[0][1] = v.y;
+                    }
+                } else {
 #pragma unroll
-                for (int h = 0; h < 2; ++h)
-                    dan[0][mt][h] = kQ8_0Act<WT> ? sm.a_scale(s)[(wm * C::WM + mt * 16 + g + 8 * h) * kAScaleStride]
-                                            : da8k[mt][h];
+                    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) d[mt][h] = da8k[mt][h];
+                }
+            };
+            load_da(0, dan[0]);
             if constexpr (kDirect && WT != kWQ4_K) {
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
@@ -713,12 +744,8 @@ __global__ void __launch_bounds__(kThreads, kDirect && (C::BM == 64 || (C::BM ==
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        da[mt][h] = dan[kb & 1][mt][h];
-                        if (kb + 1 < 8)
-                            dan[nx][mt][h] = kQ8_0Act<WT> ? sm.a_scale(s)[(wm * C::WM + mt * 16 + g + 8 * h) * kAScaleStride + kb + 1]
-                                                   : da8k[mt][h];
-                    }
+                    for (int h = 0; h < 2; ++h) da[mt][h] = dan[kb & 1][mt][h];
+                if (kb + 1 < 8) load_da(kb + 1, dan[nx]);
                 const float2 *fold = sm.fold() + kb * C::BN;
                 if constexpr (kDirect && WT != kWQ4_K) {
                     if (kb + 1 < 8) {
@@ -868,7 +895,7 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel_ov(const GemmParams p) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     const SmemOv<C> sm{smem_raw};
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int wm = warp >> 2, wn = warp & 3;
+    const int wm = warp / C::WGN, wn = warp % C::WGN;
     const int g = lane >> 2, t4 = lane & 3;
     int64_t m0, n0;
     tile_origin<C>(p, m0, n0);
@@ -960,7 +987,7 @@ __global__ void __launch_bounds__(kThreads) gemm_kernel_ov(const GemmParams p) {
             for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
                 for (int h = 0; h < 2; ++h)
-                    da[mt][h] = kQ8_0Act<WT> ? ascale[(wm * C::WM + mt * 16 + g + 8 * h) * kAScaleStride + kb]
+                    da[mt][h] = kQ8_0Act<WT> ? ascale[(kb * 8 + g) * (C::BM / 8) + wm * (C::WM / 8) + 2 * mt + h]
                                              : da8k[mt][h];
             const float2 *fold = sm.fold(cur) + kb * C::BN;
 #pragma unroll
@@ -1026,7 +1053,7 @@ PFNG_DEV void epilogue_q8_0(const GemmParams &p, uint8_t *smem, const float2 (&a
                             int64_t n0, int tid) {
     constexpr int CS = C::BN + 4;  // row stride of the staged tile (floats)
     static_assert(C::BM * CS * 4 <= C::kSmem, "staged C tile");
-    const int warp = tid >> 5, lane = tid & 31, wm = warp >> 2, wn = warp & 3, g = lane >> 2, t4 = lane & 3;
+    const int warp = tid >> 5, lane = tid & 31, wm = warp / C::WGN, wn = warp % C::WGN, g = lane >> 2, t4 = lane & 3;
     float *ct = reinterpret_cast<float *>(smem);
     __syncthreads();  // every warp is past its last read of the stage buffers
 #pragma unroll
@@ -1238,7 +1265,14 @@ cudaError_t launch_pick(const GemmParams &p, cudaStream_t s) {
         // all 32 banks (160-byte slots: rows r and r + 4 collide).  q4_K
         // keeps 160-byte slots: its full layout (fold data, mins) with
         // 176-byte rows would pass the per-CTA limit on 128 x 128 tiles.
-        using D = Cfg<C::BM, C::BN, C::ST, WT == kWQ4_K ? kWRowSlot : 176u>;
+        //
+        // 128 x 128 q4_0 tiles give each warp all 128 rows and 16 columns
+        // (128 x 16 warp tiles, 8 m16 fragments per column group): every
+        // column's unpack and scale conversion serves twice the MMAs of a
+        // 64 x 32 warp tile (254 registers, no spills; 2048x32000x4096
+        // 1621 -> 1585 us, 2048x11008x4096 591 -> 579 us, same bits).
+        using D = Cfg<C::BM, C::BN, C::ST, WT == kWQ4_K ? kWRowSlot : 176u,
+                      (C::BM == 128 && C::BN == 128 && WT == kWQ4_0) ? 1 : 2>;
         if ((WT == kWQ4_0P || p.w_vec16) && direct_enabled()) {
             if constexpr (kPartials) return launch_t<WT, D, true, false, true>(p, s);
             return copies ? launch_t<WT, D, false, true, true>(p, s) : launch_t<WT, D, false, false, true>(p, s);
@@ -1430,7 +1464,9 @@ GemmParams row_band(const GemmParams &p, int64_t r0, int64_t r1, int64_t blk) {
     q.m = r1 - r0;
     q.c = p.c + r0 * p.ldc;
     q.a.qs = p.a.qs + r0 * p.k;
-    q.a.d = p.a.d + r0 * (p.k / blk);
+    // q8_0 scales: r0 is a multiple of 128, so the rows keep their places
+    // inside their 128-row groups and the block slabs keep their stride
+    q.a.d = blk == 32 ? p.a.d + r0 : p.a.d + r0 * (p.k / blk);
     q.a.aux = p.a.aux + r0 * (p.k / 32);
     q.a.rows_pad = p.a.rows_pad - r0;
     for (int d = 0; d < p.ncopies; ++d) q.copies[d] = p.copies[d] + r0 * p.ldc;

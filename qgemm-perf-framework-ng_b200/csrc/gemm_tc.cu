@@ -77,7 +77,7 @@ constexpr float kMagic = 12582912.0f;
 // shared memory plan (dynamic, base aligned to 1024 for the swizzle atoms)
 constexpr uint32_t kRawBytes = TM * kRawRow;               // 18 KB: W rows as in memory
 constexpr uint32_t kActBytes = TN * BK;                    // 32 KB: [2 col blocks][128 rows][128 B], swizzled
-constexpr uint32_t kActScaleBytes = TN * 8 * 4;            // 4 KB: [128 rows][8] floats
+constexpr uint32_t kActScaleBytes = TN * 8 * 4;            // 4 KB: [8 blocks][128 rows] floats (split_d_index order)
 constexpr uint32_t kStageBytes = kRawBytes + kActBytes + kActScaleBytes;  // 54 KB
 constexpr uint32_t kWOpBytes = TM * BK;                    // 32 KB: decoded W, [2 col blocks][128 rows][128 B]
 constexpr uint32_t kSwBytes = TM * 8 * 4;                  // 4 KB: weight scales [128 rows][8]
@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tma_load_2d(st, &map_w, ks * static_cast<int>(kRawRow), nb * TM, &ld_full[s]);
                     tma_load_2d(st + kRawBytes, &map_a, ks * BK, mb * TN, &ld_full[s]);
                     tma_load_2d(st + kRawBytes + kActBytes / 2, &map_a, ks * BK + 128, mb * TN, &ld_full[s]);
-                    tma_load_2d(st + kRawBytes + kActBytes, &map_ad, ks * 8, mb * TN, &ld_full[s]);
+                    tma_load_2d(st + kRawBytes + kActBytes, &map_ad, mb * TN, ks * 8, &ld_full[s]);
                 }
             }
             // on an abort the consumers stop waiting: do not let the CTA end
@@ -427,13 +427,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 *reinterpret_cast<uint4 *>(dec + op_off(row, swap ? 2 * u : 2 * u + 1)) = swap ? lo : hi;
                 sw[row * 8 + u] = f16_bits_to_f32(dbits);
             }
-            // activation scales, transposed to [sub-block][row]
+            // activation scales: the stage holds [sub-block][g 16 + j] for
+            // tile row 8 j + g (split_d_index); put them in row order
             const float *dar = reinterpret_cast<const float *>(raw + kRawBytes + kActBytes);
             float *dat = reinterpret_cast<float *>(dec + kWOpBytes + kSwBytes);
+            static_assert(TN == 128, "one 128-row group of the split operand per tile");
 #pragma unroll
             for (int i = 0; i < 2; ++i) {
                 const int e = fw * 64 + i * 32 + lane;  // e = sb * TN + activation row
-                dat[e] = dar[(e % TN) * 8 + e / TN];
+                const int row = e % TN;
+                dat[e] = dar[(e / TN) * TN + (row & 7) * 16 + (row >> 3)];
             }
             fence_proxy_async_smem();  // the decoded operand is read by the tensor cores
             __syncwarp();
@@ -591,8 +594,10 @@ cudaError_t launch_gemm_tc(const GemmArgs &args, int *err, cudaStream_t s) {
         !encode_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, args.a.qs, static_cast<uint64_t>(args.k),
                    static_cast<uint64_t>(args.a.rows_pad), static_cast<uint64_t>(args.k), 128, TN,
                    CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_2d(&map_ad, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, args.a.d, static_cast<uint64_t>(args.k / 32),
-                   static_cast<uint64_t>(args.a.rows_pad), static_cast<uint64_t>(args.k / 32 * 4), 8, TN,
+        // q8_0 scales: [k / 32] slabs of d_ld floats (split_d_index), a box
+        // of one tile's 128 rows x the k-step's 8 blocks
+        !encode_2d(&map_ad, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, args.a.d, static_cast<uint64_t>(args.a.rows_pad),
+                   static_cast<uint64_t>(args.k / 32), static_cast<uint64_t>(args.a.d_ld * 4), TN, 8,
                    CU_TENSOR_MAP_SWIZZLE_NONE))
         return cudaErrorInvalidValue;
     TcParams p{};

@@ -12,13 +12,27 @@ namespace pfng {
 // row-major [rows][k] (rows 16-byte aligned), one fp32 scale per block and an
 // int32 per 32-value sub-block (see each producer for its meaning).  The
 // layout lives in the caller's workspace and is rebuilt every call.
+//
+// q8_0 scales (one per 32-value block) are stored block-major: the scales
+// of block b of every row form one slab of d_ld floats, and inside each
+// 128-row group row 8 j + g sits at g * 16 + j (split_d_index).  A GEMM
+// thread folds rows g, g + 8, g + 16, ... of a tile, so that order puts a
+// thread's scales side by side (one 16-byte load for four rows), and a
+// tile's rows of one block are 8 contiguous runs (16-byte copies).
+// q8_K scales (one per 256 values) are row-major [rows_pad][k / 256].
 struct SplitA {
     int8_t *qs;      // [rows_pad][k]
-    float *d;        // [rows_pad][k / block]   block = 32 (q8_0) or 256 (q8_K)
+    float *d;        // q8_0: [k / 32][d_ld] as above; q8_K: [rows_pad][k / 256]
     int32_t *aux;    // [rows_pad][k / 32]
     int64_t rows_pad;
     int64_t k;
+    int64_t d_ld;    // q8_0: floats between the block slabs of d (the carved rows_pad)
 };
+
+// Position of (row, 32-value block b) in a q8_0 split operand's d.
+__host__ __device__ inline int64_t split_d_index(int64_t row, int64_t b, int64_t d_ld) {
+    return b * d_ld + (row & ~int64_t(127)) + ((row & 7) << 4) + ((row >> 3) & 15);
+}
 
 constexpr int64_t kGemmTileM = 128;
 inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }

@@ -57,7 +57,7 @@ __global__ void __launch_bounds__(kThreads) quantize_q8_0_kernel(const float *__
         if constexpr (kSplit) {
             *reinterpret_cast<uint32_t *>(split.qs + row * k + col * 32 + 4 * g) = r.q;
             if (g == 0) {
-                split.d[row * nb + col] = f16_bits_to_f32(r.dbits);
+                split.d[split_d_index(row, col, split.d_ld)] = f16_bits_to_f32(r.dbits);
                 split.aux[row * nb + col] = 0x4B400000 - 8 * r.qsum;
             }
         } else {
@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(kThreads) convert_q8_0_split_kernel(const uint
         if (!live) continue;
         *reinterpret_cast<uint32_t *>(split.qs + row * k + col * 32 + 4 * g) = q;
         if (g == 0) {
-            split.d[row * nb + col] = f16_bits_to_f32(dbits);
+            split.d[split_d_index(row, col, split.d_ld)] = f16_bits_to_f32(dbits);
             split.aux[row * nb + col] = 0x4B400000 - 8 * s;
         }
     }
