@@ -38,6 +38,7 @@
 #include "pfng_common.cuh"
 #include "pfng_internal.h"
 #include "pfng_quant.cuh"
+#include "pfng_tma.h"
 
 namespace pfng {
 namespace {
@@ -58,11 +59,17 @@ constexpr uint32_t kMaxSmemPerCta = 227 * 1024;  // opt-in dynamic shared memory
 constexpr uint32_t kWRowSlot = 160;          // >= 144 raw bytes + 8 window slack, multiple of 16
 constexpr int kAScaleStride = 12;
 
-template <int BM_, int BN_, int ST_ = kStages, uint32_t SLOT_ = kWRowSlot, int WGM_ = 2>
+template <int BM_, int BN_, int ST_ = kStages, uint32_t SLOT_ = kWRowSlot, int WGM_ = 2, bool TMA_ = false>
 struct Cfg {
     static constexpr int BM = BM_, BN = BN_;
     static constexpr int ST = ST_;  // cp.async ring depth of the two-phase kernel
     static constexpr uint32_t kSlot = SLOT_;  // bytes per raw W row in shared memory
+    // Stages loaded by tensor-map bulk copies from one thread (direct q4_0
+    // operands on 128 x 128 tiles): the activation rows as two 128-byte-wide
+    // boxes with the 128-byte swizzle ([half][row][128 B]), raw W rows of
+    // step_bytes (kSlot = 144), the q8_0 scales as one [8][128] box; stages
+    // 1024-byte aligned for the swizzle.
+    static constexpr bool kTma = TMA_;
     // the 8 warps as WGM along m x WGN along n
     static constexpr int WGM = WGM_, WGN = 8 / WGM_;
     static constexpr int WM = BM / WGM, WN = BN / WGN;  // warp tile
@@ -76,7 +83,9 @@ struct Cfg {
     static constexpr uint32_t kAScale = BM * kAScaleStride * 4;
     static constexpr uint32_t kAD8K = BM * 4;        // q8_K: d per row
     static constexpr uint32_t kWRaw = BN * kSlot;
-    static constexpr uint32_t kStage = kAQs + kAScale + kAD8K + kWRaw;
+    static constexpr uint32_t kStageRaw = kAQs + kAScale + kAD8K + kWRaw;
+    static constexpr uint32_t kStage = kTma ? (kStageRaw + 1023) / 1024 * 1024 : kStageRaw;
+    static_assert(!kTma || (BM == 128 && BN == 128 && kSlot == 144), "tensor-map stages: 128 x 128, 144-byte rows");
     static constexpr uint32_t kBTile = BN * BK;
     static constexpr uint32_t kFold = 8 * BN * 8;    // float2 (s, -M s) per (sub-block, column)
     static constexpr uint32_t kMin = BN * 16;        // q4_K: (dmin, -M dmin) and packed mins per column
@@ -113,6 +122,7 @@ struct GemmParams {
     // tile raster: 1 = blockIdx.x walks the m tiles (consecutive CTAs share
     // a W tile, which is then fetched from DRAM once), 0 = the n tiles
     int m_fast;
+    int *err;  // library error word (bounded waits of the tensor-map stages)
 };
 
 // Origin (m0, n0) of this CTA's tile in the raster order of p.m_fast.
@@ -437,7 +447,8 @@ struct FragOff {
 #pragma unroll
         for (int mt = 0; mt < C::MT; ++mt) {
             const int row = wm * C::WM + mt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-            a[mt] = static_cast<uint32_t>(row * 256 + ((((lane >> 4) & 1) ^ (lane & 7)) << 4));
+            // tensor-map stages: 128-byte rows per half (a_off)
+            a[mt] = static_cast<uint32_t>(row * (C::kTma ? 128 : 256) + ((((lane >> 4) & 1) ^ (lane & 7)) << 4));
         }
 #pragma unroll
         for (int np = 0; np < C::NT / 2; ++np) {
@@ -482,9 +493,20 @@ PFNG_DEV uint32_t raw_q4_scale(const uint8_t *row, int kb) {
 template <int WT, class C>
 PFNG_DEV void load_frags_direct(uint32_t at_s, const uint8_t *wr, int kb, const FragOff<C> &fo, int wn, int g, int t4,
                                 uint32_t (&af)[C::MT][4], uint32_t (&bf)[C::NT][2]) {
-    const uint32_t x = static_cast<uint32_t>(kb) * 32u;
+    if constexpr (C::kTma) {
+        // [half][row][128 B] with the 128-byte swizzle: sub-block kb is
+        // 16-byte chunks 2 (kb & 3) + {0, 1} of half kb / 4
+        const uint32_t half = at_s + static_cast<uint32_t>(kb >> 2) * (C::BM * 128u);
+        const uint32_t x = static_cast<uint32_t>(kb & 3) * 32u;
 #pragma unroll
-    for (int mt = 0; mt < C::MT; ++mt) ldmatrix_x4_s(af[mt][0], af[mt][1], af[mt][2], af[mt][3], at_s + (fo.a[mt] ^ x));
+        for (int mt = 0; mt < C::MT; ++mt)
+            ldmatrix_x4_s(af[mt][0], af[mt][1], af[mt][2], af[mt][3], half + (fo.a[mt] ^ x));
+    } else {
+        const uint32_t x = static_cast<uint32_t>(kb) * 32u;
+#pragma unroll
+        for (int mt = 0; mt < C::MT; ++mt)
+            ldmatrix_x4_s(af[mt][0], af[mt][1], af[mt][2], af[mt][3], at_s + (fo.a[mt] ^ x));
+    }
 #pragma unroll
     for (int nt = 0; nt < C::NT; ++nt) {
         const uint8_t *row = wr + (wn * C::WN + nt * 8 + g) * C::kSlot;
@@ -569,11 +591,39 @@ PFNG_DEV void copy_tile_to_copies(const GemmParams &p) {
     __threadfence_system();
 }
 
+// Tensor maps of a Cfg::kTma launch (unused otherwise): the split
+// operand's int8 rows, the raw W rows, the split operand's q8_0 scales.
+struct TmaMaps {
+    CUtensorMap a, w, ad;
+};
+
+// Bounded wait on a stage barrier of a Cfg::kTma kernel: false once the
+// CTA's abort flag is up, or after about a second, when it records `code`
+// and raises the flag so that every other wait of the CTA ends too.
+PFNG_DEV bool stage_wait(uint64_t *bar, uint32_t parity, int *abort_flag, int *err, int code) {
+    volatile int *ab = abort_flag;
+    for (uint32_t i = 0; i < kWaitAttempts; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*ab) return false;
+    }
+    report_error(err, code);
+    *ab = 1;
+    return false;
+}
+
 template <int WT, class C, bool kPartials, bool kCopies = false, bool kDirect = false>
-__global__ void __launch_bounds__(kThreads, kDirect && (C::BM == 64 || (C::BM == 32 && WT == kWQ4_K)) ? 2 : 1) gemm_kernel(const GemmParams p) {
+__global__ void __launch_bounds__(kThreads, kDirect && (C::BM == 64 || (C::BM == 32 && WT == kWQ4_K)) ? 2 : 1)
+    gemm_kernel(const __grid_constant__ TmaMaps maps, const GemmParams p) {
     static_assert(!kDirect || WT == kWQ4_0 || WT == kWQ4_0P || WT == kWQ4_K, "direct operands: q4_0 and q4_K");
+    static_assert(!C::kTma || (kDirect && WT == kWQ4_0), "tensor-map stages: direct q4_0 operands");
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    const Smem<C> sm{smem_raw};
+    // tensor-map stages start on a 1024-byte boundary (the 128-byte swizzle;
+    // the launch adds the slack)
+    const Smem<C> sm{C::kTma ? smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u) : smem_raw};
+    // Cfg::kTma: stage s holds its k-step once tma_full[s] completes, and is
+    // free for the next copies once every warp has arrived on tma_empty[s]
+    __shared__ uint64_t tma_full[C::ST], tma_empty[C::ST];
+    __shared__ int tma_abort;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int wm = warp / C::WGN, wn = warp % C::WGN;
     const int g = lane >> 2, t4 = lane & 3;
@@ -617,30 +667,85 @@ __global__ void __launch_bounds__(kThreads, kDirect && (C::BM == 64 || (C::BM ==
     // weights of the first stages are fetched before waiting for it, the
     // activations after.  Group s holds A[s] (group 0 also every W prologue
     // stage), so the wait_group accounting of the loop is unchanged.
+    // Cfg::kTma: thread 0 issues every stage's copies; bytes one stage lands
+    constexpr uint32_t kTmaTx = C::BM * BK + C::BN * 144u + C::BM * 8u * 4u;
+    int tma_issued = 0, tma_used = 0;  // (thread 0) k-steps issued / consumed
+    auto tma_w = [&](int st, int64_t ks) {
+        mbar_arrive_expect_tx(&tma_full[st], kTmaTx);
+        tma_load_2d(smem_u32(sm.w_raw(st)), &maps.w, static_cast<int>(ks * p.step_bytes), static_cast<int>(n0),
+                    &tma_full[st]);
+    };
+    auto tma_a = [&](int st, int64_t ks) {
+        const uint32_t a = smem_u32(sm.a_qs(st));
+        tma_load_2d(a, &maps.a, static_cast<int>(ks * BK), static_cast<int>(m0), &tma_full[st]);
+        tma_load_2d(a + C::BM * 128u, &maps.a, static_cast<int>(ks * BK + 128), static_cast<int>(m0), &tma_full[st]);
+        tma_load_2d(smem_u32(sm.a_scale(st)), &maps.ad, static_cast<int>(m0), static_cast<int>(ks * 8), &tma_full[st]);
+    };
+    if constexpr (C::kTma) {
+        if (tid == 0) {
+            for (int i = 0; i < ST; ++i) {
+                mbar_init(&tma_full[i], 1);
+                mbar_init(&tma_empty[i], kThreads / 32);
+            }
+            fence_mbar_init();
+            tma_abort = 0;
+            prefetch_map(&maps.a);
+            prefetch_map(&maps.w);
+            prefetch_map(&maps.ad);
+        }
+        __syncthreads();
+        if (tid == 0)
+            for (int s = 0; s < ST - 1; ++s)
+                if (k0 + s < k1) tma_w(s, k0 + s);
+        pdl_wait();
+        if (tid == 0)
+            for (int s = 0; s < ST - 1; ++s)
+                if (k0 + s < k1) {
+                    tma_a(s, k0 + s);
+                    ++tma_issued;
+                }
+    } else {
 #pragma unroll
-    for (int s = 0; s < ST - 1; ++s)
-        if (k0 + s < k1) load_w<WT, C>(p, sm.w_raw(s), k0 + s, n0, tid);
-    pdl_wait();
+        for (int s = 0; s < ST - 1; ++s)
+            if (k0 + s < k1) load_w<WT, C>(p, sm.w_raw(s), k0 + s, n0, tid);
+        pdl_wait();
 #pragma unroll
-    for (int s = 0; s < ST - 1; ++s) {
-        if (k0 + s < k1) load_a<WT, C>(p, sm.a_qs(s), sm.a_scale(s), sm.a_d8k(s), k0 + s, m0, tid);
-        cp_async_commit();
+        for (int s = 0; s < ST - 1; ++s) {
+            if (k0 + s < k1) load_a<WT, C>(p, sm.a_qs(s), sm.a_scale(s), sm.a_d8k(s), k0 + s, m0, tid);
+            cp_async_commit();
+        }
     }
 
     for (int64_t ks = k0; ks < k1; ++ks) {
         const int s = static_cast<int>((ks - k0) % ST);
-        cp_async_wait<ST - 2>();
-        __syncthreads();
-        // q4_K with direct operands still decodes its 6-bit scales and mins
-        // (fold constants, min term) -- everything but the B tile
-        if constexpr (!kDirect)
-            decode_w<WT, C>(p, sm, s, ks, n0, tid);
-        else if constexpr (WT == kWQ4_K)
-            decode_w<WT, C, false>(p, sm, s, ks, n0, tid);
-        if (ks + ST - 1 < k1)
-            load_stage<WT, C>(p, sm, static_cast<int>((ks - k0 + ST - 1) % ST), ks + ST - 1, m0, n0, tid);
-        cp_async_commit();
-        if constexpr (!kDirect || WT == kWQ4_K) __syncthreads();
+        if constexpr (C::kTma) {
+            // refill the stage of k-step ks - 1 (free once every warp has
+            // arrived on it) with k-step ks + ST - 1, then wait for k-step ks
+            const int i = static_cast<int>(ks - k0);
+            if (tid == 0 && ks + ST - 1 < k1) {
+                const int j = i + ST - 1, t = j % ST;
+                if (j < ST || stage_wait(&tma_empty[t], ((j / ST) - 1) & 1, &tma_abort, p.err, kErrWaitEmpty)) {
+                    tma_w(t, ks + ST - 1);
+                    tma_a(t, ks + ST - 1);
+                    ++tma_issued;
+                }
+            }
+            if (!stage_wait(&tma_full[s], (i / ST) & 1, &tma_abort, p.err, kErrWaitFull)) break;
+            if (tid == 0) ++tma_used;
+        } else {
+            cp_async_wait<ST - 2>();
+            __syncthreads();
+            // q4_K with direct operands still decodes its 6-bit scales and mins
+            // (fold constants, min term) -- everything but the B tile
+            if constexpr (!kDirect)
+                decode_w<WT, C>(p, sm, s, ks, n0, tid);
+            else if constexpr (WT == kWQ4_K)
+                decode_w<WT, C, false>(p, sm, s, ks, n0, tid);
+            if (ks + ST - 1 < k1)
+                load_stage<WT, C>(p, sm, static_cast<int>((ks - k0 + ST - 1) % ST), ks + ST - 1, m0, n0, tid);
+            cp_async_commit();
+            if constexpr (!kDirect || WT == kWQ4_K) __syncthreads();
+        }
 
         const int8_t *at = sm.a_qs(s);
         const int8_t *bt = sm.b_tile();
@@ -814,8 +919,23 @@ __global__ void __launch_bounds__(kThreads, kDirect && (C::BM == 64 || (C::BM ==
                     }
                 }
         }
+        if constexpr (C::kTma) {
+            // this warp is done with stage s
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tma_empty[s]);
+        }
     }
-    cp_async_wait<0>();
+    if constexpr (C::kTma) {
+        // after an abort, copies issued for k-steps nobody consumed must
+        // land before the CTA exits
+        if (tid == 0)
+            for (int j = tma_used; j < tma_issued; ++j)
+                mbar_wait(&tma_full[j % ST], static_cast<uint32_t>((j / ST) & 1), p.err, kErrWaitFull);
+        __syncthreads();
+        if (tma_abort) return;
+    } else {
+        cp_async_wait<0>();
+    }
 
     if constexpr (!kPartials) {
         if (p.splits > 1) {
@@ -1155,8 +1275,8 @@ __global__ void __launch_bounds__(kThreads) reduce_splits_kernel(const GemmParam
 // Launch as a programmatic dependent of the preceding kernel on the stream
 // (the activation quantizer): the kernels fetch weights before pdl_wait()
 // and read activations after it.
-template <class C, class K>
-cudaError_t launch_pdl(K kernel, const GemmParams &p, uint32_t smem, cudaStream_t s) {
+template <class C, class K, class... Args>
+cudaError_t launch_pdl(K kernel, const GemmParams &p, uint32_t smem, cudaStream_t s, const Args &...args) {
     cudaLaunchConfig_t cfg{};
     const unsigned nt = static_cast<unsigned>((p.n + C::BN - 1) / C::BN);
     const unsigned mt = static_cast<unsigned>((p.m + C::BM - 1) / C::BM);
@@ -1169,7 +1289,23 @@ cudaError_t launch_pdl(K kernel, const GemmParams &p, uint32_t smem, cudaStream_
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, p);
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+// The tensor maps of a Cfg::kTma launch over p's operands (this GPU's
+// memory): activation rows [rows_pad][k] int8 in 128 x 128-byte boxes with
+// the 128-byte swizzle, raw W rows [n][row_bytes] in 128 x 144-byte boxes
+// (rows past n read as zeros), q8_0 scales [k / 32][d_ld] in 8 x 128 boxes.
+bool encode_tma_maps(const GemmParams &p, TmaMaps *maps) {
+    return encode_2d(&maps->a, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.a.qs, static_cast<uint64_t>(p.k),
+                     static_cast<uint64_t>(p.a.rows_pad), static_cast<uint64_t>(p.k), 128, 128,
+                     CU_TENSOR_MAP_SWIZZLE_128B) &&
+           encode_2d(&maps->w, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.w, static_cast<uint64_t>(p.row_bytes),
+                     static_cast<uint64_t>(p.n), static_cast<uint64_t>(p.row_bytes), p.step_bytes, 128,
+                     CU_TENSOR_MAP_SWIZZLE_NONE) &&
+           encode_2d(&maps->ad, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.a.d, static_cast<uint64_t>(p.a.rows_pad),
+                     static_cast<uint64_t>(p.k / 32), static_cast<uint64_t>(p.a.d_ld * 4), 128, 8,
+                     CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 template <int WT, class C, bool kPartials, bool kCopies = false, bool kDirect = false>
@@ -1177,8 +1313,15 @@ cudaError_t launch_t(const GemmParams &p, cudaStream_t s) {
     auto kernel = gemm_kernel<WT, C, kPartials, kCopies, kDirect>;
     // direct q4_0 operands use the stage ring only (no B tile, fold data or
     // tables); q4_K keeps the layout for its fold data and mins
-    constexpr uint32_t smem = kDirect && WT != kWQ4_K ? C::ST * C::kStage : C::kSmem;
+    // tensor-map stages: + the slack that aligns them to 1024 bytes
+    constexpr uint32_t smem = kDirect && WT != kWQ4_K ? C::ST * C::kStage + (C::kTma ? 1024u : 0u) : C::kSmem;
     static_assert(smem <= kMaxSmemPerCta, "dynamic shared memory above the per-CTA limit");
+    TmaMaps maps;
+    if constexpr (C::kTma) {
+        if (!encode_tma_maps(p, &maps)) return cudaErrorNotSupported;  // the caller takes the cp.async kernel
+    } else {
+        std::memset(&maps, 0, sizeof maps);
+    }
     // the q8_0 epilogue stages the CTA's C tile in the launched shared memory
     static_assert(C::BM * (C::BN + 4) * 4 <= smem, "staged C tile of the q8_0 epilogue");
     static thread_local bool configured[64] = {false};
@@ -1189,7 +1332,7 @@ cudaError_t launch_t(const GemmParams &p, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) configured[dev] = true;
     }
-    return launch_pdl<C>(kernel, p, smem, s);
+    return launch_pdl<C>(kernel, p, smem, s, maps, p);
 }
 
 template <int WT, class C, bool kCopies = false, bool kPartials = false>
@@ -1206,7 +1349,7 @@ cudaError_t launch_t_ov(const GemmParams &p, cudaStream_t s) {
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) configured[dev] = true;
     }
-    return launch_pdl<C>(kernel, p, smem, s);
+    return launch_pdl<C>(kernel, p, smem, s, p);
 }
 
 // The overlapped kernel serves q4_0 (both layouts) and iq2_xxs products
@@ -1248,6 +1391,10 @@ inline bool ov_enabled() {
     const char *e = std::getenv("PFNG_B200_GEMM_OV");
     return !(e && std::strcmp(e, "0") == 0);
 }
+inline bool tma_enabled() {
+    const char *e = std::getenv("PFNG_B200_GEMM_TMA");
+    return !(e && std::strcmp(e, "0") == 0);
+}
 
 // The partials mode (integer sub-block products instead of C) takes the
 // same kernel as the product of the same shape, so the integers it exports
@@ -1273,6 +1420,19 @@ cudaError_t launch_pick(const GemmParams &p, cudaStream_t s) {
         // 1621 -> 1585 us, 2048x11008x4096 591 -> 579 us, same bits).
         using D = Cfg<C::BM, C::BN, C::ST, WT == kWQ4_K ? kWRowSlot : 176u,
                       (C::BM == 128 && C::BN == 128 && WT == kWQ4_0) ? 1 : 2>;
+        if constexpr (C::BM == 128 && C::BN == 128 && WT == kWQ4_0) {
+            // the same kernel with its stages loaded by tensor maps from one
+            // thread (PFNG_B200_GEMM_TMA=0: the per-thread cp.async loads)
+            if (p.w_vec16 && direct_enabled() && tma_enabled()) {
+                using DT = Cfg<128, 128, C::ST, 144u, 1, true>;
+                cudaError_t e;
+                if constexpr (kPartials)
+                    e = launch_t<WT, DT, true, false, true>(p, s);
+                else
+                    e = copies ? launch_t<WT, DT, false, true, true>(p, s) : launch_t<WT, DT, false, false, true>(p, s);
+                if (e != cudaErrorNotSupported) return e;
+            }
+        }
         if ((WT == kWQ4_0P || p.w_vec16) && direct_enabled()) {
             if constexpr (kPartials) return launch_t<WT, D, true, false, true>(p, s);
             return copies ? launch_t<WT, D, false, true, true>(p, s) : launch_t<WT, D, false, false, true>(p, s);
@@ -1587,6 +1747,7 @@ cudaError_t launch_gemm(const GemmArgs &args, cudaStream_t s) {
     p.c = args.c;
     p.ldc = args.ldc;
     p.partials = args.partials;
+    p.err = args.err;
     p.m = args.m;
     p.n = args.n;
     p.k = args.k;

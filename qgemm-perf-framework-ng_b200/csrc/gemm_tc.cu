@@ -49,13 +49,11 @@
 // its own copy.  Every wait is bounded; a wait that gives up records an error,
 // raises the CTA's abort flag (which ends every other role's waits at once)
 // and the CTA frees its TMEM before returning.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
 #include <mutex>
 
 #include "pfng_common.cuh"
 #include "pfng_internal.h"
+#include "pfng_tma.h"
 
 namespace pfng {
 namespace {
@@ -100,16 +98,6 @@ struct TcParams {
 };
 
 // ---- TMA / tcgen05 / proxy primitives ----------------------------------------
-PFNG_DEV void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-            "r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-PFNG_DEV void prefetch_map(const CUtensorMap *map) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
-}
 PFNG_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 PFNG_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 PFNG_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -548,6 +536,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+}  // namespace
+
 // ---- host: tensor maps ------------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -562,8 +552,6 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 2-D tiled map over a row-major array [rows][cols] of `elem`-byte elements
-// (row stride `stride` bytes), boxes of box_cols x box_rows elements.
 bool encode_2d(CUtensorMap *map, CUtensorMapDataType type, const void *base, uint64_t cols, uint64_t rows,
                uint64_t stride, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
     auto fn = encode_fn();
@@ -575,8 +563,6 @@ bool encode_2d(CUtensorMap *map, CUtensorMapDataType type, const void *base, uin
     return fn(map, type, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
-
-}  // namespace
 
 bool gemm_tc_supported(int wtype, int64_t m, int64_t n, int64_t k, const void *w) {
     (void)m;
