@@ -80,8 +80,9 @@ struct Cfg {
     // q8_0: d per (sub-block, row) as [kb][g][BM / 8] (load_a); q8_K: bsum32
     // per (row, sub-block), rows kAScaleStride words apart so that 8
     // consecutive rows hit 8 distinct banks.
-    static constexpr uint32_t kAScale = BM * kAScaleStride * 4;
-    static constexpr uint32_t kAD8K = BM * 4;        // q8_K: d per row
+    // (tensor-map stages: the q8_0 scales' [8][BM] box, no q8_K block scales)
+    static constexpr uint32_t kAScale = kTma ? BM * 8 * 4 : BM * kAScaleStride * 4;
+    static constexpr uint32_t kAD8K = kTma ? 0 : BM * 4;  // q8_K: d per row
     static constexpr uint32_t kWRaw = BN * kSlot;
     static constexpr uint32_t kStageRaw = kAQs + kAScale + kAD8K + kWRaw;
     static constexpr uint32_t kStage = kTma ? (kStageRaw + 1023) / 1024 * 1024 : kStageRaw;
@@ -1422,9 +1423,11 @@ cudaError_t launch_pick(const GemmParams &p, cudaStream_t s) {
                       (C::BM == 128 && C::BN == 128 && WT == kWQ4_0) ? 1 : 2>;
         if constexpr (C::BM == 128 && C::BN == 128 && WT == kWQ4_0) {
             // the same kernel with its stages loaded by tensor maps from one
-            // thread (PFNG_B200_GEMM_TMA=0: the per-thread cp.async loads)
+            // thread (PFNG_B200_GEMM_TMA=0: the per-thread cp.async loads);
+            // the 54 KB stages fit a 4-deep ring (2048x32000x4096: 1332 ->
+            // 1305 us against 3 stages)
             if (p.w_vec16 && direct_enabled() && tma_enabled()) {
-                using DT = Cfg<128, 128, C::ST, 144u, 1, true>;
+                using DT = Cfg<128, 128, 4, 144u, 1, true>;
                 cudaError_t e;
                 if constexpr (kPartials)
                     e = launch_t<WT, DT, true, false, true>(p, s);
