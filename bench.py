@@ -483,7 +483,8 @@ def headline(ctx: Ctx, args) -> dict:
         "roofline": {
             "bound": "tensor", "achieved": achieved, "peak": pk["int8_tops"], "unit": "TFLOP/s",
             "frac": achieved / pk["int8_tops"], "traffic": traffic,
-            "kernel": "gemm_kernel (q4_0 x q8_0, int8 mma.sync m16n8k32, 128x128 tiles, direct B fragments)"
+            "kernel": "gemm_kernel (q4_0 x q8_0, int8 mma.sync m16n8k32, 128x128 tiles, direct B fragments, "
+                      "stages filled by tensor-map bulk copies)"
                       if not os.environ.get("PFNG_B200_GEMM") else f"GEMM ({os.environ['PFNG_B200_GEMM']})",
             "flops_per_launch": 2.0 * m * ns * k, "avg_launch_us": t_kernel / args.steps * 1e6,
             "timing": "CUDA events around K back-to-back pfng_b200_mm_prepared launches on the launching "
