@@ -86,7 +86,7 @@ struct Cfg {
     static constexpr uint32_t kWRaw = BN * kSlot;
     static constexpr uint32_t kStageRaw = kAQs + kAScale + kAD8K + kWRaw;
     static constexpr uint32_t kStage = kTma ? (kStageRaw + 1023) / 1024 * 1024 : kStageRaw;
-    static_assert(!kTma || (BM == 128 && BN == 128 && kSlot == 144), "tensor-map stages: 128 x 128, 144-byte rows");
+    static_assert(!kTma || (BM % 32 == 0 && kSlot == 144), "tensor-map stages: 32-row multiples, 144-byte rows");
     static constexpr uint32_t kBTile = BN * BK;
     static constexpr uint32_t kFold = 8 * BN * 8;    // float2 (s, -M s) per (sub-block, column)
     static constexpr uint32_t kMin = BN * 16;        // q4_K: (dmin, -M dmin) and packed mins per column
@@ -680,7 +680,12 @@ __global__ void __launch_bounds__(kThreads, kDirect && (C::BM == 64 || (C::BM ==
         const uint32_t a = smem_u32(sm.a_qs(st));
         tma_load_2d(a, &maps.a, static_cast<int>(ks * BK), static_cast<int>(m0), &tma_full[st]);
         tma_load_2d(a + C::BM * 128u, &maps.a, static_cast<int>(ks * BK + 128), static_cast<int>(m0), &tma_full[st]);
-        tma_load_2d(smem_u32(sm.a_scale(st)), &maps.ad, static_cast<int>(m0), static_cast<int>(ks * 8), &tma_full[st]);
+        if constexpr (C::BM == 128)  // the tile's 128-row group of the scales: a 2-D box
+            tma_load_2d(smem_u32(sm.a_scale(st)), &maps.ad, static_cast<int>(m0), static_cast<int>(ks * 8),
+                        &tma_full[st]);
+        else  // j (BM / 8 of the group's 16), g, group, block
+            tma_load_4d(smem_u32(sm.a_scale(st)), &maps.ad, static_cast<int>((m0 & 127) >> 3), 0,
+                        static_cast<int>(m0 >> 7), static_cast<int>(ks * 8), &tma_full[st]);
     };
     if constexpr (C::kTma) {
         if (tid == 0) {
@@ -1294,19 +1299,31 @@ cudaError_t launch_pdl(K kernel, const GemmParams &p, uint32_t smem, cudaStream_
 }
 
 // The tensor maps of a Cfg::kTma launch over p's operands (this GPU's
-// memory): activation rows [rows_pad][k] int8 in 128 x 128-byte boxes with
-// the 128-byte swizzle, raw W rows [n][row_bytes] in 128 x 144-byte boxes
-// (rows past n read as zeros), q8_0 scales [k / 32][d_ld] in 8 x 128 boxes.
+// memory): activation rows [rows_pad][k] int8 in BM x 128-byte boxes with
+// the 128-byte swizzle, raw W rows [n][row_bytes] in BN x 144-byte boxes
+// (rows past n read as zeros), and the q8_0 scales: with 128-row tiles
+// [k / 32][d_ld] in 8 x 128 boxes, else as [block][group][g][j]
+// (split_d_index) in boxes of {BM / 8 j, 8 g, 1 group, 8 blocks}
+// (measured on 128-row tiles: the 2-D box 1% faster than the 4-D one).
+template <class C>
 bool encode_tma_maps(const GemmParams &p, TmaMaps *maps) {
-    return encode_2d(&maps->a, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.a.qs, static_cast<uint64_t>(p.k),
-                     static_cast<uint64_t>(p.a.rows_pad), static_cast<uint64_t>(p.k), 128, 128,
-                     CU_TENSOR_MAP_SWIZZLE_128B) &&
-           encode_2d(&maps->w, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.w, static_cast<uint64_t>(p.row_bytes),
-                     static_cast<uint64_t>(p.n), static_cast<uint64_t>(p.row_bytes), p.step_bytes, 128,
-                     CU_TENSOR_MAP_SWIZZLE_NONE) &&
-           encode_2d(&maps->ad, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.a.d, static_cast<uint64_t>(p.a.rows_pad),
-                     static_cast<uint64_t>(p.k / 32), static_cast<uint64_t>(p.a.d_ld * 4), 128, 8,
-                     CU_TENSOR_MAP_SWIZZLE_NONE);
+    bool ok = encode_2d(&maps->a, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.a.qs, static_cast<uint64_t>(p.k),
+                        static_cast<uint64_t>(p.a.rows_pad), static_cast<uint64_t>(p.k), 128, C::BM,
+                        CU_TENSOR_MAP_SWIZZLE_128B) &&
+              encode_2d(&maps->w, CU_TENSOR_MAP_DATA_TYPE_UINT8, p.w, static_cast<uint64_t>(p.row_bytes),
+                        static_cast<uint64_t>(p.n), static_cast<uint64_t>(p.row_bytes), p.step_bytes, C::BN,
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (!ok) return false;
+    if constexpr (C::BM == 128) {
+        return encode_2d(&maps->ad, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.a.d, static_cast<uint64_t>(p.a.rows_pad),
+                         static_cast<uint64_t>(p.k / 32), static_cast<uint64_t>(p.a.d_ld * 4), 128, 8,
+                         CU_TENSOR_MAP_SWIZZLE_NONE);
+    } else {
+        const uint64_t dims[4] = {16, 8, static_cast<uint64_t>(p.a.rows_pad / 128), static_cast<uint64_t>(p.k / 32)};
+        const uint64_t strides[3] = {64, 512, static_cast<uint64_t>(p.a.d_ld * 4)};
+        const uint32_t box[4] = {C::BM / 8, 8, 1, 8};
+        return encode_nd(&maps->ad, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.a.d, dims, strides, box);
+    }
 }
 
 template <int WT, class C, bool kPartials, bool kCopies = false, bool kDirect = false>
@@ -1319,7 +1336,7 @@ cudaError_t launch_t(const GemmParams &p, cudaStream_t s) {
     static_assert(smem <= kMaxSmemPerCta, "dynamic shared memory above the per-CTA limit");
     TmaMaps maps;
     if constexpr (C::kTma) {
-        if (!encode_tma_maps(p, &maps)) return cudaErrorNotSupported;  // the caller takes the cp.async kernel
+        if (!encode_tma_maps<C>(p, &maps)) return cudaErrorNotSupported;  // the caller takes the cp.async kernel
     } else {
         std::memset(&maps, 0, sizeof maps);
     }
@@ -1421,13 +1438,17 @@ cudaError_t launch_pick(const GemmParams &p, cudaStream_t s) {
         // 1621 -> 1585 us, 2048x11008x4096 591 -> 579 us, same bits).
         using D = Cfg<C::BM, C::BN, C::ST, WT == kWQ4_K ? kWRowSlot : 176u,
                       (C::BM == 128 && C::BN == 128 && WT == kWQ4_0) ? 1 : 2>;
-        if constexpr (C::BM == 128 && C::BN == 128 && WT == kWQ4_0) {
+        if constexpr (WT == kWQ4_0 && !(C::BM == 64 && C::BN == 128)) {
             // the same kernel with its stages loaded by tensor maps from one
-            // thread (PFNG_B200_GEMM_TMA=0: the per-thread cp.async loads);
-            // the 54 KB stages fit a 4-deep ring (2048x32000x4096: 1332 ->
-            // 1305 us against 3 stages)
+            // thread (PFNG_B200_GEMM_TMA=0: the per-thread cp.async loads).
+            // The 54 KB stages of 128 x 128 tiles fit a 4-deep ring
+            // (2048x32000x4096: 1332 -> 1305 us against 3 stages); the
+            // smaller tiles keep 3 stages and two CTAs per SM (480x1536x1536
+            // 18.7 -> 17.5 us, 32x32000x4096 52.9 -> 47.3 us against
+            // cp.async).  64 x 128 tiles (32 < m <= 128 with large n, no
+            // BASELINE shape) keep the cp.async loads.
             if (p.w_vec16 && direct_enabled() && tma_enabled()) {
-                using DT = Cfg<128, 128, 4, 144u, 1, true>;
+                using DT = Cfg<C::BM, C::BN, (C::BM == 128 && C::BN == 128) ? 4 : 3, 144u, D::WGM, true>;
                 cudaError_t e;
                 if constexpr (kPartials)
                     e = launch_t<WT, DT, true, false, true>(p, s);

@@ -552,6 +552,23 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
+bool encode_nd(CUtensorMap *map, CUtensorMapDataType type, int rank, const void *base, const uint64_t *dims,
+               const uint64_t *strides, const uint32_t *box) {
+    auto fn = encode_fn();
+    if (!fn || rank < 1 || rank > 5) return false;
+    cuuint64_t d[5], st[4];
+    cuuint32_t b[5], e[5];
+    for (int i = 0; i < rank; ++i) {
+        d[i] = dims[i];
+        b[i] = box[i];
+        e[i] = 1;
+        if (i + 1 < rank) st[i] = strides[i];
+    }
+    return fn(map, type, static_cast<cuuint32_t>(rank), const_cast<void *>(base), d, st, b, e,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool encode_2d(CUtensorMap *map, CUtensorMapDataType type, const void *base, uint64_t cols, uint64_t rows,
                uint64_t stride, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
     auto fn = encode_fn();
