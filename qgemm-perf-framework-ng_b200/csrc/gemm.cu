@@ -1588,8 +1588,8 @@ bool m_fast_raster(const GemmParams &p, int bm, int bn) {
 // transfer over NVLink overlaps the GEMM instead of following it.  Every tile
 // is computed exactly as without bands (bit-identical C).  The split puts
 // the smallest last band under which the first band's copies still finish:
-// with r = copy time / GEMM time per row ~ 1100 x destinations / k (measured
-// on B200: ~330 Top/s for the GEMM, ~600 GB/s out over NVLink), the last
+// with r = copy time / GEMM time per row ~ 1400 x destinations / k (measured
+// on B200: ~416 Top/s for the GEMM, ~600 GB/s out over NVLink), the last
 // band takes r / (1 + r) of the 128-row tiles.  Measured on two B200s at
 // 2048 x 32000 x 4096 (us per sharded step): no bands 1101; two equal bands
 // 1005, four 1077, eight 1061 (copy engines); four with the push kernel
@@ -1599,7 +1599,7 @@ int gather_split_tiles(const GemmParams &p, int64_t tiles) {
     if (const char *e = std::getenv("PFNG_B200_GATHER_BANDS"))
         if (std::strcmp(e, "1") == 0) return 0;
     if (tiles < 4) return 0;
-    const double r = 1100.0 * p.ncopies / static_cast<double>(p.k);
+    const double r = 1400.0 * p.ncopies / static_cast<double>(p.k);
     int64_t last = static_cast<int64_t>(tiles * r / (1.0 + r) + 0.999);
     if (last < 1) last = 1;
     if (last > tiles - 1) last = tiles - 1;
