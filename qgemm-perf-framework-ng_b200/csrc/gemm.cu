@@ -1583,27 +1583,45 @@ bool m_fast_raster(const GemmParams &p, int bm, int bn) {
 }
 
 // Row bands of a product whose C also goes to other destinations (the
-// all-gather of row-sharded weights): the first band's rows are copied to
-// the destinations while the second band is computed, so that part of the
+// all-gather of row-sharded weights): each band's rows are copied to the
+// destinations while the next band is computed, so that most of the
 // transfer over NVLink overlaps the GEMM instead of following it.  Every tile
-// is computed exactly as without bands (bit-identical C).  The split puts
-// the smallest last band under which the first band's copies still finish:
-// with r = copy time / GEMM time per row ~ 1400 x destinations / k (measured
-// on B200: ~416 Top/s for the GEMM, ~600 GB/s out over NVLink), the last
-// band takes r / (1 + r) of the 128-row tiles.  Measured on two B200s at
-// 2048 x 32000 x 4096 (us per sharded step): no bands 1101; two equal bands
-// 1005, four 1077, eight 1061 (copy engines); four with the push kernel
-// 1084.  Products of fewer than four 128-row tiles run unbanded;
-// PFNG_B200_GATHER_BANDS=1 turns the bands off.
-int gather_split_tiles(const GemmParams &p, int64_t tiles) {
-    if (const char *e = std::getenv("PFNG_B200_GATHER_BANDS"))
-        if (std::strcmp(e, "1") == 0) return 0;
+// is computed exactly as without bands (bit-identical C).  Two bands, the
+// last one the smallest under which the first band's copies still finish:
+// with r = copy time / GEMM time per row ~ 1400 x destinations / k
+// (measured on B200: ~416 Top/s for the GEMM, ~600 GB/s out over NVLink)
+// it takes r / (1 + r) of the 128-row tiles.  Measured at 2048 x 32000 x
+// 4096 (us per sharded step): two B200s, no bands 1101, two equal bands
+// 1005, four 1077, eight 1061 (copy engines), four with the push kernel
+// 1084; four B200s (where the copies take as long as the GEMM), two bands
+// 666, four or eight equal bands 685.
+// Products of fewer than four 128-row tiles run unbanded;
+// PFNG_B200_GATHER_BANDS=1 turns the bands off, =2..8 forces that many
+// equal bands (comparisons).  Returns the band count (0: unbanded) and the
+// first row of each band in `start` (start[bands] = m).
+constexpr int kMaxBands = 8;
+int gather_bands(const GemmParams &p, int64_t tiles, int64_t (&start)[kMaxBands + 1]) {
+    int forced = 0;
+    if (const char *e = std::getenv("PFNG_B200_GATHER_BANDS")) {
+        forced = std::atoi(e);
+        if (forced == 1) return 0;
+        if (forced < 2 || forced > kMaxBands) forced = 0;
+    }
     if (tiles < 4) return 0;
     const double r = 1400.0 * p.ncopies / static_cast<double>(p.k);
-    int64_t last = static_cast<int64_t>(tiles * r / (1.0 + r) + 0.999);
-    if (last < 1) last = 1;
-    if (last > tiles - 1) last = tiles - 1;
-    return static_cast<int>(tiles - last);
+    int bands = forced ? forced : 2;
+    if (bands > tiles) bands = static_cast<int>(tiles);
+    if (!forced && bands == 2) {
+        int64_t last = static_cast<int64_t>(tiles * r / (1.0 + r) + 0.999);
+        if (last < 1) last = 1;
+        if (last > tiles - 1) last = tiles - 1;
+        start[0] = 0;
+        start[1] = (tiles - last) * kGemmTileM;
+    } else {
+        for (int b = 0; b < bands; ++b) start[b] = (tiles * b / bands) * kGemmTileM;
+    }
+    start[bands] = p.m;
+    return bands;
 }
 
 // Side streams (one per destination, high priority) and their events, one
@@ -1672,14 +1690,13 @@ cudaError_t copy_band(const GemmParams &q, SideStreams *side) {
 }
 
 template <int WT>
-cudaError_t launch_banded_gather(const GemmParams &p, cudaStream_t s, int64_t split_rows) {
+cudaError_t launch_banded_gather(const GemmParams &p, cudaStream_t s, const int64_t *bounds, int bands) {
     std::lock_guard<std::mutex> lock(g_side_mutex);
     SideStreams *side = nullptr;
     cudaError_t e = side_streams(&side);
     if (e != cudaSuccess) return e;
     const int64_t blk = kQ8_0Act<WT> ? 32 : 256;
-    const int64_t bounds[3] = {0, split_rows, p.m};
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < bands; ++b) {
         const GemmParams q = row_band(p, bounds[b], bounds[b + 1], blk);
         GemmParams g = q;
         g.ncopies = 0;
@@ -1700,8 +1717,9 @@ cudaError_t launch_tile(GemmParams &p, cudaStream_t s) {
     if (p.ncopies > 0 && p.out_format == kOutF32 && push_copies()) {
         if constexpr (!kPartials) {
             const int64_t tiles = (p.m + kGemmTileM - 1) / kGemmTileM;
-            const int split = gather_split_tiles(p, tiles);
-            if (split > 0) return launch_banded_gather<WT>(p, s, split * kGemmTileM);
+            int64_t start[kMaxBands + 1];
+            const int bands = gather_bands(p, tiles, start);
+            if (bands > 0) return launch_banded_gather<WT>(p, s, start, bands);
         }
         GemmParams q = p;
         q.ncopies = 0;

@@ -3,9 +3,10 @@
 * One process: every destination must hold exactly what pfng_b200_compute_*
   writes for the same arguments (bit for bit, on every path, with split-K
   and ragged shapes; copies written by the push kernel, by copy engines
-  per row band (from four 128-row tiles the product runs as two bands and
-  the first band's copies overlap the second band's GEMM), or by the GEMM
-  epilogue), and nothing outside the [m][n] window of its rows; the
+  per row band (from four 128-row tiles the product runs as two bands, or
+  as many as PFNG_B200_GATHER_BANDS forces, and each band's copies overlap
+  the next band's GEMM), or by the
+  GEMM epilogue), and nothing outside the [m][n] window of its rows; the
   pre-quantized entry (mm_gather) likewise equals mm().
 * Two processes through CUDA IPC (GatheredC): each rank computes the columns
   of its weight rows into every rank's full C; after a host barrier every
@@ -38,7 +39,7 @@ CASES = [
     ("q4_0", "mma", 2048, 256, 512), ("q4_0", "gemv", 1, 300, 1024), ("q4_0", "gemv", 5, 96, 512),
     ("q4_0", "simple", 3, 40, 256), ("q4_K", "mma", 70, 256, 1536), ("iq2_xxs", "mma", 40, 192, 512),
     ("q4_0_planar", "mma", 200, 384, 2048),
-    # two row bands (the split follows the destination count and k; ragged second band in the first two)
+    # two row bands (the split follows the destination count and k; a ragged last band in the first two)
     ("q4_0", "mma", 1100, 640, 1024), ("q4_K", "mma", 600, 256, 1536), ("iq2_xxs", "mma", 1024, 192, 512),
 ]
 
@@ -65,6 +66,24 @@ def test_every_destination_equals_compute(oracle, monkeypatch, wtype, path, m, n
         for d in range(ndst):
             assert got[d, :, :n].tobytes() == ref.tobytes(), f"{wtype}/{path}/{m}x{n}x{k} destination {d}"
             assert np.all(got[d, :, n:] == -7.0)
+
+
+@pytest.mark.parametrize("bands", ["3", "8"])
+@pytest.mark.parametrize("wtype,m,n,k", [("q4_0", 1100, 640, 1024), ("q4_K", 600, 256, 1536)])
+def test_forced_band_counts(oracle, monkeypatch, bands, wtype, m, n, k):
+    # PFNG_B200_GATHER_BANDS=3 / 8: equal row bands (ragged last band), each
+    # band's copies overlapping the next band's GEMM; same bytes as compute()
+    monkeypatch.setenv("PFNG_B200_GATHER_BANDS", bands)
+    rng = np.random.default_rng(m + n + int(bands))
+    wd = dev_bytes(make_weights(oracle, wtype, n, k, rng))
+    xd = dev(rng.standard_normal((m, k)).astype(np.float32))
+    ref = host(pb.compute(wtype, wd, xd, n, path="mma"))
+    big = torch.full((3, m, n + 5), -7.0, device="cuda")
+    pb.compute_gather(wtype, wd, xd, n, [big[d] for d in range(3)], n + 5, path="mma")
+    got = host(big)
+    for d in range(3):
+        assert got[d, :, :n].tobytes() == ref.tobytes(), f"{wtype} {m}x{n}x{k} bands={bands} destination {d}"
+        assert np.all(got[d, :, n:] == -7.0)
 
 
 @pytest.mark.parametrize("wtype,path,m,n,k", [c for c in CASES if c[1] != "simple"])
