@@ -6,12 +6,16 @@
 // Semantics: compute_q4_0 / compute_q4_K / compute_iq2_xxs,
 // bench/llama_reference/llama_reference.cpp:113-205.
 //
-// CTA tile BM x BN (64..128 each, chosen per shape to fill the SMs), k-step
-// 256, 8 warps (2 along m and 4 along n; 1 x 8 on 128 x 128 q4_0 tiles), a
-// 3-stage cp.async ring for the A rows, A scales and raw W bytes.  Each k-step the CTA unpacks its raw W tile
-// once into an int8 [n][k] tile (q4_0: nibble - 8; q4_K: nibble; iq2_xxs:
-// signed grid value) and a per-(sub-block, column) scale s, then every
-// 32-deep sub-block is one m16n8k32 s8 MMA per 16 x 8 fragment.
+// CTA tile BM x BN (32..128 each, chosen per shape to fill the SMs), k-step
+// 256, 8 warps (2 along m and 4 along n; 1 x 8 on 128 x 128 q4_0 tiles),
+// every 32-deep sub-block one m16n8k32 s8 MMA per 16 x 8 fragment.  The
+// stage ring holds the A rows, A scales and raw W bytes of a k-step: for
+// q4_0 on 128 x 128, 64 x 64 and 32 x 128 tiles it is filled by tensor-map
+// bulk copies issued by one thread (full / empty mbarriers per stage),
+// otherwise by per-thread cp.async.  q4_0 and q4_K take their B fragments
+// straight from the raw W rows ("direct operands"); iq2_xxs (and the
+// comparison switches) unpack the raw W tile once per k-step into an int8
+// [n][k] tile and a per-(sub-block, column) scale s.
 //
 // The fold (the per-sub-block scaling that makes this more than an int8
 // GEMM) is the same for all three types and costs one packed instruction
